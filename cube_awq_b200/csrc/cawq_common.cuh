@@ -1,0 +1,218 @@
+// cawq_common.cuh — device helpers shared by the sm_100a kernels of
+// libcube_awq.so: dtype traits, nibble order tables, PTX wrappers (mbarrier,
+// TMA, mma.sync, cluster shared memory) and the bounded-wait error word.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cawq_internal.h"
+
+namespace cawq {
+
+// ---------------------------------------------------------------- dtypes
+template <int DT> struct DType;
+template <> struct DType<kF32> {
+  using T = float;
+  static __device__ __forceinline__ float to_f32(T v) { return v; }
+  static __device__ __forceinline__ T from_f32(float v) { return v; }
+};
+template <> struct DType<kF16> {
+  using T = __half;
+  static __device__ __forceinline__ float to_f32(T v) { return __half2float(v); }
+  static __device__ __forceinline__ T from_f32(float v) { return __float2half_rn(v); }
+};
+template <> struct DType<kBF16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float to_f32(T v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ T from_f32(float v) { return __float2bfloat16_rn(v); }
+};
+
+__device__ __forceinline__ float load_as_f32(const void* p, size_t i, int dt) {
+  if (dt == kF32) return static_cast<const float*>(p)[i];
+  if (dt == kF16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__device__ __forceinline__ void store_from_f32(void* p, size_t i, float v, int dt) {
+  if (dt == kF32) {
+    static_cast<float*>(p)[i] = v;
+  } else if (dt == kF16) {
+    static_cast<__half*>(p)[i] = __float2half_rn(v);
+  } else {
+    static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// ------------------------------------------------------ nibble ordering
+// Nibble that holds logical column c (0..7) of a packed word.
+//   AWQ order (awq_kernel_gemm.rs:10-30): [0,4,1,5,2,6,3,7]
+//   natural (awq_kernel.rs:9-19): c
+__device__ __forceinline__ int nibble_of_col(int c, int order) {
+  return order == kOrderAwq ? ((c & 1) * 4 + (c >> 1)) : c;
+}
+// Logical column stored in nibble p (inverse of nibble_of_col).
+//   AWQ: AWQ_ORDER = [0,2,4,6,1,3,5,7] (awq_gemm.rs:248)
+__host__ __device__ __forceinline__ int col_of_nibble(int p, int order) {
+  return order == kOrderAwq ? ((p & 3) * 2 + (p >> 2)) : p;
+}
+
+// --------------------------------------------------------- bit helpers
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+  uint32_t d;
+  // (a & mask) | magic  ->  immLut 0xEA
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(magic));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// ------------------------------------------------- device error word
+// Bit 0: a bounded wait (mbarrier / cluster) gave up. Host reads it through
+// cawq_device_error(). Defined here: only cawq_kernels.cu includes this file.
+__device__ uint32_t g_cawq_device_error = 0;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------------------ mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete, for at most kWaitLimitNs.
+// On timeout it records bit 0 in the device error word and returns false; the
+// caller then skips its work but still takes every barrier it would have.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_cawq_device_error, 1u);
+      return false;
+    }
+  }
+}
+
+// ----------------------------------------------------------------- TMA
+// 2-D tiled bulk tensor load into this CTA's shared memory, completion on an
+// mbarrier (no multicast). c0 is the inner (contiguous) coordinate.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------- cluster
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_shared_rank(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// ------------------------------------------------------------- mma.sync
+// D(16x8, f32) += A(16x16) * B(16x8), A/B 16-bit (f16 or bf16).
+template <bool kBF16>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (kBF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+// ------------------------------------------------------- global access
+__device__ __forceinline__ uint32_t ldg_nc_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void stg_cs_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+}  // namespace cawq

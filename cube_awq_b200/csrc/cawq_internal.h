@@ -1,0 +1,80 @@
+// cawq_internal.h — declarations shared by the translation units of
+// libcube_awq.so (host side). Not part of the public C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/cube_awq.h"
+
+namespace cawq {
+
+enum { kF32 = CAWQ_F32, kF16 = CAWQ_F16, kBF16 = CAWQ_BF16 };
+enum { kOrderAwq = CAWQ_ORDER_AWQ, kOrderNatural = CAWQ_ORDER_NATURAL };
+
+inline size_t dtype_size(int dt) { return dt == kF32 ? 4 : 2; }
+
+// One fused GEMM call after validation.
+struct GemmProblem {
+  const void* x;         // [rows, k] dtype
+  const uint32_t* qw;    // [k, n/8]
+  const uint32_t* qz;    // [k/g, n/8]
+  const void* sc;        // [k/g, n] dtype
+  const void* bias;      // [n] dtype or nullptr
+  void* out;             // [rows, ld_out] out_dtype
+  size_t rows, k, n, g, ld_out;
+  int dtype, out_dtype, order;
+  cudaStream_t stream;
+};
+
+// Thread-local error message (cawq_last_error).
+void set_error(const std::string& msg);
+cawq_status fail(cawq_status st, const std::string& msg);
+cawq_status cuda_fail(cudaError_t e, const char* where);
+
+// Device properties cached per device.
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t smem_optin = 0;
+};
+cawq_status current_device_info(DeviceInfo* info);
+
+// Driver entry point for cuTensorMapEncodeTiled (resolved through the runtime,
+// so the library needs no -lcuda).
+typedef int (*EncodeTiledFn)(void*, int, uint32_t, void*, const uint64_t*, const uint64_t*,
+                             const uint32_t*, const uint32_t*, int, int, int, int);
+EncodeTiledFn encode_tiled_fn();
+
+// ---------------------------------------------------------- launchers
+// Each returns cudaSuccess or the launch error. `supports` functions say
+// whether a plan can run a problem (shape, dtype and alignment).
+bool generic_supports(const GemmProblem& p);
+cudaError_t launch_generic(const GemmProblem& p);
+
+bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+cudaError_t launch_decode(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+void decode_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
+                       int max_count);
+cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev);
+
+bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
+                        int max_count);
+cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev);
+
+cudaError_t launch_dequant(const uint32_t* qw, const uint32_t* qz, const void* sc, void* out,
+                           size_t k, size_t n, size_t g, int dtype, int order,
+                           cudaStream_t stream, int sm_count);
+
+cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, size_t n,
+                                      int world, size_t elem, cudaStream_t stream);
+
+cudaError_t read_device_error(uint32_t* word, int reset);
+
+}  // namespace cawq

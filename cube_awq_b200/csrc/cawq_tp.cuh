@@ -1,0 +1,51 @@
+// cawq_tp.cuh — helper kernel of the tensor-parallel layer: turns the
+// rank-major result of an all-gather of column shards, src[world][rows][n/world],
+// back into the row-major output dst[rows][n].
+#pragma once
+
+#include "cawq_common.cuh"
+
+namespace cawq {
+
+template <typename V>
+__global__ void __launch_bounds__(256)
+    interleave_columns_kernel(const V* __restrict__ src, V* __restrict__ dst, size_t rows,
+                              size_t shard_v, int world) {
+  // shard_v: vectors of type V per shard row; dst row has world * shard_v vectors
+  const size_t total = rows * shard_v * world;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / (shard_v * world);
+    const size_t rem = i - row * shard_v * world;
+    const size_t r = rem / shard_v;
+    const size_t c = rem - r * shard_v;
+    dst[i] = src[(r * rows + row) * shard_v + c];
+  }
+}
+
+cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, size_t n, int world,
+                                      size_t elem, cudaStream_t stream) {
+  const size_t shard_bytes = n / world * elem;
+  const bool v16 = shard_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dst) % 16 == 0;
+  const size_t total_bytes = rows * n * elem;
+  const size_t vec = v16 ? 16 : elem;
+  size_t blocks = (total_bytes / vec + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  if (v16) {
+    interleave_columns_kernel<uint4><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint4*>(src), static_cast<uint4*>(dst), rows, shard_bytes / 16, world);
+  } else if (elem == 4) {
+    interleave_columns_kernel<uint32_t><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), rows, shard_bytes / 4,
+        world);
+  } else {
+    interleave_columns_kernel<uint16_t><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), rows, shard_bytes / 2,
+        world);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace cawq

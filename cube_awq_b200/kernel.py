@@ -1,0 +1,304 @@
+"""Kernel-level API: the counterpart of the reference's ``src/kernel`` module.
+
+=========================================  ==========================================
+reference (joshuawm/cube-awq)              here
+=========================================  ==========================================
+``ShapeConfig`` (awq_kernel_gemm.rs:35-79)  :class:`ShapeConfig`
+``validate_launch_params`` (:160)           :func:`validate_launch_params`
+``validate_decode_launch_params`` (:164)    :func:`validate_decode_launch_params`
+``awq_gemm_linear`` (:626-771)              :func:`awq_gemm_linear`
+``dequantize_native`` (awq_kernel.rs:63)    :func:`dequantize_native`
+``dequantize_awq`` (kernel/mod.rs:9-51)     :func:`dequantize_awq`
+=========================================  ==========================================
+
+Buffers are torch tensors on an sm_100 GPU (torch supplies device memory and
+the current stream); all arithmetic runs in libcube_awq.so.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .errors import CubeAwqError, DTypeError, ShapeError, check
+
+DECODE_M_THRESHOLD = 8  # awq_kernel_gemm.rs:81
+DECODE_TILE_M = 8       # awq_kernel_gemm.rs:82
+
+_DTYPES = {torch.float32: _lib.CAWQ_F32, torch.float16: _lib.CAWQ_F16,
+           torch.bfloat16: _lib.CAWQ_BF16}
+_PACKED = (torch.int32, getattr(torch, "uint32", torch.int32))
+
+
+def cawq_dtype(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise DTypeError(f"unsupported float dtype {dtype}; use float32, float16 or bfloat16",
+                         _lib.CAWQ_ERR_DTYPE) from None
+
+
+def stream_handle(t: torch.Tensor) -> Optional[int]:
+    return torch.cuda.current_stream(t.device).cuda_stream if t.is_cuda else None
+
+
+def _desc(t: Optional[torch.Tensor]) -> _lib.TensorDescC:
+    d = _lib.TensorDescC()
+    if t is None:
+        d.data = None
+        d.rank = 0
+        d.elem_size = 0
+        return d
+    if t.dim() > _lib.MAX_RANK:
+        raise ShapeError(f"tensor rank {t.dim()} exceeds {_lib.MAX_RANK}", _lib.CAWQ_ERR_INVALID_SHAPE)
+    d.data = t.data_ptr() if t.numel() > 0 else None
+    d.rank = t.dim()
+    for i, s in enumerate(t.shape):
+        d.shape[i] = s
+    d.elem_size = t.element_size()
+    return d
+
+
+def _require_cuda(*tensors: Optional[torch.Tensor]) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise CubeAwqError("cube_awq_b200 computes on an sm_100 GPU only; got a CPU tensor "
+                               "(there is no CPU fallback)", _lib.CAWQ_ERR_UNSUPPORTED)
+
+
+@dataclass
+class ShapeConfig:
+    """Mirror of the reference ShapeConfig (awq_kernel_gemm.rs:35-79)."""
+
+    m: int
+    k: int
+    n: int
+    tile_m: int
+    tile_n: int
+    inner_k: int
+    line_size: int = 4
+    m_valid: int = -1
+
+    def __post_init__(self):
+        if self.m_valid < 0:
+            self.m_valid = self.m
+
+    @classmethod
+    def new(cls, m: int, n: int, k: int, m_tile_size: int, n_tile_size: int,
+            inner_k_size: int) -> "ShapeConfig":
+        """ShapeConfig::new — note the (m, n, k) argument order of the reference."""
+        return cls(m=m, k=k, n=n, tile_m=m_tile_size, tile_n=n_tile_size, inner_k=inner_k_size)
+
+    @classmethod
+    def new_with_valid_m(cls, m: int, n: int, k: int, m_tile_size: int, n_tile_size: int,
+                         inner_k_size: int, m_valid: int) -> "ShapeConfig":
+        return cls(m=m, k=k, n=n, tile_m=m_tile_size, tile_n=n_tile_size,
+                   inner_k=inner_k_size, m_valid=m_valid)
+
+    def to_c(self) -> _lib.ShapeConfigC:
+        return _lib.ShapeConfigC(self.m, self.k, self.n, self.tile_m, self.tile_n, self.inner_k,
+                                 self.line_size, self.m_valid)
+
+
+def validate_launch_params(shape: ShapeConfig, group_size: int) -> None:
+    """Prefill-kernel rules (awq_kernel_gemm.rs:89-162); raises ShapeError."""
+    c = shape.to_c()
+    check(_lib.lib().cawq_validate_launch_params(ctypes.byref(c), group_size))
+
+
+def validate_decode_launch_params(shape: ShapeConfig, group_size: int) -> None:
+    """Decode-kernel rules (awq_kernel_gemm.rs:164-171); raises ShapeError."""
+    c = shape.to_c()
+    check(_lib.lib().cawq_validate_decode_launch_params(ctypes.byref(c), group_size))
+
+
+def select_tile_m(m: int) -> int:
+    """awq_gemm.rs:30-42, including the AWQ_GEMM_FORCE_TILE_M override."""
+    return int(_lib.lib().cawq_select_tile_m(m))
+
+
+def select_tile_n(n: int) -> int:
+    """awq_gemm.rs:44-52."""
+    return int(_lib.lib().cawq_select_tile_n(n))
+
+
+def awq_gemm_linear(input: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                    scales: torch.Tensor, output: torch.Tensor, shape: Optional[ShapeConfig],
+                    group_size: int, bias: Optional[torch.Tensor] = None) -> None:
+    """awq_gemm_linear (awq_kernel_gemm.rs:626-771): output = input · deq(W) (+ bias).
+
+    Same shape asserts and messages, m_valid resolution and decode/prefill rule
+    check as the reference; one fused launch on the current stream. Rows at
+    or beyond the resolved m_valid are left untouched, as in the reference.
+    """
+    _require_cuda(input, qweight, qzeros, scales, output, bias)
+    for name, t in (("input", input), ("qweight", qweight), ("qzeros", qzeros),
+                    ("scales", scales), ("output", output), ("bias", bias)):
+        if t is not None and not t.is_contiguous():
+            raise ShapeError(f"{name} must be contiguous (row-major)", _lib.CAWQ_ERR_INVALID_SHAPE)
+    args = _lib.GemmArgsC()
+    args.input = _desc(input)
+    args.qweight = _desc(qweight)
+    args.qzeros = _desc(qzeros)
+    args.scales = _desc(scales)
+    args.bias = _desc(bias)
+    args.output = _desc(output)
+    args.dtype = cawq_dtype(input.dtype)
+    args.group_size = group_size
+    c = shape.to_c() if shape is not None else None
+    check(_lib.lib().cawq_awq_gemm_linear(ctypes.byref(args),
+                                          ctypes.byref(c) if c is not None else None,
+                                          stream_handle(input)))
+
+
+def dequantize_native(q_weight: torch.Tensor, q_zeros: torch.Tensor, q_scales: torch.Tensor,
+                      output: torch.Tensor, group_size: int, order: str = "natural") -> None:
+    """dequantize_native (awq_kernel.rs:63-111): output[K, N] = (q - z) * s in F.
+
+    Natural nibble order as the reference kernel reads it; ``order="awq"`` is
+    an extension that reads the GEMM's AutoAWQ order instead.
+    """
+    _require_cuda(q_weight, q_zeros, q_scales, output)
+    lib = _lib.lib()
+    st = lib.cawq_dequantize_native(
+        ctypes.byref(_desc(q_weight)), ctypes.byref(_desc(q_zeros)), ctypes.byref(_desc(q_scales)),
+        ctypes.byref(_desc(output)), group_size, cawq_dtype(output.dtype), _order(order),
+        stream_handle(output))
+    check(st)
+
+
+def dequantize_awq(weight: torch.Tensor, zeros: torch.Tensor, scales: torch.Tensor,
+                   group_size: int, order: str = "natural") -> torch.Tensor:
+    """dequantize_awq (kernel/mod.rs:9-51): allocates and returns out[K, N]."""
+    if weight.dtype not in _PACKED:
+        raise DTypeError("assertion failed: matches!(w_primitive.dtype(), DType::I32 | DType::U32)",
+                         _lib.CAWQ_ERR_DTYPE)
+    if zeros.dtype not in _PACKED:
+        raise DTypeError("assertion failed: matches!(z_primitive.dtype(), DType::I32 | DType::U32)",
+                         _lib.CAWQ_ERR_DTYPE)
+    h = weight.shape[0]
+    w = scales.shape[-1]
+    out = torch.empty((h, w), dtype=scales.dtype, device=scales.device)
+    dequantize_native(weight, zeros, scales, out, group_size, order=order)
+    return out
+
+
+def _order(order: str) -> int:
+    if order == "awq":
+        return _lib.CAWQ_ORDER_AWQ
+    if order == "natural":
+        return _lib.CAWQ_ORDER_NATURAL
+    raise ValueError(f"order must be 'awq' or 'natural', got {order!r}")
+
+
+def gemm(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+         group_size: int, bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+         out_dtype: Optional[torch.dtype] = None, order: str = "awq",
+         plan: Optional[dict] = None) -> torch.Tensor:
+    """Hot-path fused GEMM (cawq_gemm): out[rows, N] = x[rows, K] · deq(W) (+ bias).
+
+    ``x`` is [rows, K] (contiguous); ``out`` may be a [rows, >= N] view with a
+    unit column stride (its row stride becomes ``ld_out``). ``out_dtype`` is
+    x.dtype or float32 (fp32 partial sums). ``plan`` pins a kernel (see
+    :func:`plan_get`).
+    """
+    _require_cuda(x, qweight, qzeros, scales, bias, out)
+    if x.dim() != 2 or not x.is_contiguous():
+        raise ShapeError("x must be a contiguous [rows, K] tensor", _lib.CAWQ_ERR_INVALID_SHAPE)
+    rows, k = x.shape
+    n = qweight.shape[1] * 8
+    odt = out_dtype or x.dtype
+    if out is None:
+        out = torch.empty((rows, n), dtype=odt, device=x.device)
+    if out.dtype != odt or out.dim() != 2 or out.shape[0] != rows or out.shape[1] < n or \
+            (rows > 0 and out.stride(1) != 1):
+        raise ShapeError("out must be a [rows, >= N] tensor with unit column stride",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    for name, t in (("qweight", qweight), ("qzeros", qzeros), ("scales", scales), ("bias", bias)):
+        if t is not None and not t.is_contiguous():
+            raise ShapeError(f"{name} must be contiguous", _lib.CAWQ_ERR_INVALID_SHAPE)
+    if qweight.dtype not in _PACKED:
+        raise DTypeError("qweight must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+    if qzeros.dtype not in _PACKED:
+        raise DTypeError("qzeros must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+    if scales.dtype != x.dtype or (bias is not None and bias.dtype != x.dtype):
+        raise DTypeError("scales and bias must have the input's float dtype (F)", _lib.CAWQ_ERR_DTYPE)
+    if qweight.shape[0] != k:
+        raise ShapeError("input last dim (K) must match qweight rows", _lib.CAWQ_ERR_INVALID_SHAPE)
+    groups = scales.shape[0]
+    if groups == 0 or k % groups != 0 or qzeros.shape[0] != groups or scales.shape[1] != n or \
+            qzeros.shape[1] * 8 != n:
+        raise ShapeError("qzeros must be [K/g, N/8] and scales [K/g, N]", _lib.CAWQ_ERR_INVALID_SHAPE)
+    if group_size * groups != k:
+        raise ShapeError("group_size must equal K / scales rows", _lib.CAWQ_ERR_INVALID_SHAPE)
+    lib = _lib.lib()
+    ld_out = out.stride(0) if rows > 0 else n
+    args = (x.data_ptr(), qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+            bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, k, n, group_size,
+            cawq_dtype(x.dtype), cawq_dtype(odt), _order(order), ld_out)
+    if plan is None:
+        check(lib.cawq_gemm(*args, stream_handle(x)))
+    else:
+        p = _plan_c(plan)
+        check(lib.cawq_gemm_with_plan(*args, ctypes.byref(p), stream_handle(x)))
+    return out
+
+
+def _plan_c(plan: dict) -> _lib.PlanC:
+    p = _lib.PlanC()
+    p.path = int(plan.get("path", 0))
+    p.split = int(plan.get("split", 0))
+    p.warps = int(plan.get("warps", 0))
+    p.tile_n = int(plan.get("tile_n", 0))
+    p.stages = int(plan.get("stages", 0))
+    return p
+
+
+PATHS = {"auto": _lib.CAWQ_PATH_AUTO, "decode": _lib.CAWQ_PATH_DECODE,
+         "prefill": _lib.CAWQ_PATH_PREFILL, "generic": _lib.CAWQ_PATH_GENERIC}
+
+
+def plan_get(rows: int, k: int, n: int, group_size: int, dtype: torch.dtype) -> dict:
+    """The kernel choice cawq_gemm would make for this problem (needs a GPU)."""
+    p = _lib.PlanC()
+    check(_lib.lib().cawq_plan_get(rows, k, n, group_size, cawq_dtype(dtype), ctypes.byref(p)))
+    return p.as_dict()
+
+
+def plan_set(rows: int, k: int, n: int, group_size: int, dtype: torch.dtype, plan: dict) -> None:
+    p = _plan_c(plan)
+    check(_lib.lib().cawq_plan_set(rows, k, n, group_size, cawq_dtype(dtype), ctypes.byref(p)))
+
+
+def plan_cache_clear() -> None:
+    _lib.lib().cawq_plan_cache_clear()
+
+
+def autotune(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+             group_size: int, out: Optional[torch.Tensor] = None) -> dict:
+    """Times every candidate kernel on these buffers and caches the fastest."""
+    _require_cuda(x, qweight, qzeros, scales, out)
+    rows, k = x.shape
+    n = qweight.shape[1] * 8
+    if out is None:
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    p = _lib.PlanC()
+    check(_lib.lib().cawq_autotune(x.data_ptr(), qweight.data_ptr(), qzeros.data_ptr(),
+                                   scales.data_ptr(), out.data_ptr(), rows, k, n, group_size,
+                                   cawq_dtype(x.dtype), ctypes.byref(p), stream_handle(x)))
+    return p.as_dict()
+
+
+def device_error(reset: bool = True) -> int:
+    """Device-side error word (bit 0: a bounded wait timed out). Synchronises."""
+    w = ctypes.c_uint32(0)
+    check(_lib.lib().cawq_device_error(1 if reset else 0, ctypes.byref(w)))
+    return int(w.value)
+
+
+def version() -> str:
+    return _lib.lib().cawq_version().decode()

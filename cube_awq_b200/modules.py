@@ -1,0 +1,157 @@
+"""Module API: the counterpart of the reference's ``src/modules``.
+
+``AWQGEMMLinearConfig(d_in, d_out, g).with_bias(b).build(device)`` and
+``AWQLinearConfig(d_in, d_out, g).build(device)`` keep the reference's names,
+argument meaning, parameter shapes and assert messages
+(src/modules/awq_gemm.rs:54-233, src/modules/awq_dequantize.rs:9-109).
+Parameters are plain torch tensors (the reference's Burn ``Param`` wrapper and
+state loading are not part of this path); assign real AWQ tensors to
+``qweight``, ``qzeros``, ``scales`` and ``bias`` after ``build``.
+"""
+
+from __future__ import annotations
+
+import copy
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .errors import CubeAwqError, DTypeError, ShapeError
+from .kernel import _PACKED, dequantize_awq, gemm
+
+AWQ_PACK_FACTOR = 8  # awq_gemm.rs:12
+TILE_N_BASE = 32     # awq_gemm.rs:13
+INNER_K = 64         # awq_gemm.rs:16
+
+
+def _shape_assert(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ShapeError(msg, _lib.CAWQ_ERR_INVALID_SHAPE)
+
+
+class AWQGEMMLinearConfig:
+    """awq_gemm.rs:54-125."""
+
+    def __init__(self, d_input: int, d_output: int, group_size: int):
+        self.d_input = d_input
+        self.d_output = d_output
+        self.group_size = group_size
+        self.bias = False
+
+    def with_bias(self, bias: bool) -> "AWQGEMMLinearConfig":
+        c = copy.copy(self)
+        c.bias = bool(bias)
+        return c
+
+    def build(self, device="cuda", dtype: torch.dtype = torch.float32) -> "AWQGEMMLinear":
+        """awq_gemm.rs:77-124: asserts, then [K, N/8] / [K/g, N/8] / [K/g, N] / [N] params."""
+        _shape_assert(self.group_size > 0, "group_size must be > 0")
+        _shape_assert(self.d_output % AWQ_PACK_FACTOR == 0,
+                      f"d_output must be divisible by {AWQ_PACK_FACTOR}")
+        _shape_assert(self.d_output % TILE_N_BASE == 0,
+                      f"d_output must be divisible by TILE_N ({TILE_N_BASE})")
+        _shape_assert(self.d_input % INNER_K == 0, f"d_input must be divisible by INNER_K ({INNER_K})")
+        _shape_assert(self.d_input % self.group_size == 0, "d_input must be divisible by group_size")
+        d_out_packed = self.d_output // AWQ_PACK_FACTOR
+        num_groups = self.d_input // self.group_size
+        qweight = torch.empty((self.d_input, d_out_packed), dtype=torch.int32, device=device)
+        qzeros = torch.empty((num_groups, d_out_packed), dtype=torch.int32, device=device)
+        scales = torch.empty((num_groups, self.d_output), dtype=dtype, device=device)
+        bias = torch.zeros((self.d_output,), dtype=dtype, device=device) if self.bias else None
+        return AWQGEMMLinear(qweight, qzeros, scales, bias)
+
+
+class AWQGEMMLinear:
+    """awq_gemm.rs:127-233: fused dequant-GEMM layer (AutoAWQ order)."""
+
+    def __init__(self, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                 bias: Optional[torch.Tensor] = None):
+        self.qweight = qweight
+        self.qzeros = qzeros
+        self.scales = scales
+        self.bias = bias
+
+    def group_size(self) -> int:
+        """awq_gemm.rs:136-140: K / scale rows."""
+        return self.qweight.shape[0] // self.scales.shape[0]
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        """awq_gemm.rs:146-232: [..., K] -> [..., N]; bias fused after the K sum."""
+        _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
+        k = input.shape[-1]
+        _shape_assert(k > 0, "input last dim (K) must be > 0")
+        _shape_assert(input.numel() % k == 0, "input elements must be divisible by K")
+        m = input.numel() // k
+        x = input.reshape(m, k)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        _shape_assert(k == self.qweight.shape[0], "input last dim (K) must match qweight rows")
+        if self.qweight.dtype not in _PACKED:
+            raise DTypeError("qweight must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+        if self.qzeros.dtype not in _PACKED:
+            raise DTypeError("qzeros must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+        out = gemm(x, self.qweight, self.qzeros, self.scales, self.group_size(), bias=self.bias,
+                   order="awq")
+        return out.reshape(*input.shape[:-1], out.shape[-1])
+
+    __call__ = forward
+
+
+class AWQLinearConfig:
+    """awq_dequantize.rs:9-42."""
+
+    def __init__(self, d_input: int, d_output: int, group_size: int):
+        self.d_input = d_input
+        self.d_output = d_output
+        self.group_size = group_size
+
+    def build(self, device="cuda", dtype: torch.dtype = torch.float32) -> "AWQLinear":
+        # awq_dequantize.rs:26-28: bare assert! (message = the condition)
+        _shape_assert(self.d_output % 8 == 0, "assertion failed: self.d_output % 8 == 0")
+        if self.group_size == 0:
+            raise ShapeError("attempt to calculate the remainder with a divisor of zero",
+                             _lib.CAWQ_ERR_INVALID_SHAPE)
+        _shape_assert(self.d_input % self.group_size == 0,
+                      "assertion failed: self.d_input % self.group_size == 0")
+        _shape_assert(self.d_output % 32 == 0, "assertion failed: self.d_output % 32 == 0")
+        d_out = self.d_output // 8
+        g_input = self.d_input // self.group_size
+        return AWQLinear(
+            torch.empty((self.d_input, d_out), dtype=torch.int32, device=device),
+            torch.empty((g_input, d_out), dtype=torch.int32, device=device),
+            torch.empty((g_input, self.d_output), dtype=dtype, device=device))
+
+
+class AWQLinear:
+    """awq_dequantize.rs:44-109: dequantize (natural nibble order) / forward."""
+
+    def __init__(self, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor):
+        self.qweight = qweight
+        self.qzeros = qzeros
+        self.scales = scales
+
+    def group_size(self) -> int:
+        """awq_dequantize.rs:52-56: K / scale rows."""
+        return self.qweight.shape[0] // self.scales.shape[0]
+
+    def dequantize(self) -> torch.Tensor:
+        """awq_dequantize.rs:62-72: the full-precision [K, N] weight in F."""
+        return dequantize_awq(self.qweight, self.qzeros, self.scales, self.group_size())
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        """awq_dequantize.rs:74-108: input[M, K] · dequantize() -> [M, N].
+
+        The reference dequantizes into a [K, N] tensor and runs a separate
+        matmul; here the same natural-order weights are dequantized inside the
+        fused GEMM, with fp32 accumulation. Rank-2 input only, as in the
+        reference (a rank-3 input fails with RankMismatch there, :283-300).
+        """
+        if input.dim() != 2:
+            raise CubeAwqError(
+                f"RankMismatch: AWQLinear.forward takes a rank-2 [M, K] input, got rank {input.dim()}",
+                _lib.CAWQ_ERR_INVALID_SHAPE)
+        x = input if input.is_contiguous() else input.contiguous()
+        return gemm(x, self.qweight, self.qzeros, self.scales, self.group_size(), order="natural")
+
+    __call__ = forward

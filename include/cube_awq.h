@@ -1,0 +1,290 @@
+/*
+ * cube_awq.h — C ABI of libcube_awq.so, the B200 (sm_100a) implementation of
+ * the AWQ INT4 hot path of joshuawm/cube-awq:
+ *
+ *   - the fused INT4 dequant-GEMM  Y[M,N] = X[M,K] · ((Q - Z) · S)[K,N]
+ *     (reference: src/kernel/awq_kernel_gemm.rs `gemm_awq` / `gemm_awq_decode`),
+ *   - the standalone dequantize kernel
+ *     (reference: src/kernel/awq_kernel.rs `dequantize_awq_symmetric`).
+ *
+ * Tensor format (AutoAWQ, exactly as the reference reads it):
+ *   qweight u32 [K, N/8], qzeros u32 [K/g, N/8], scales F [K/g, N], bias F [N].
+ *   Logical column c of a packed u32 is stored in nibble
+ *     CAWQ_ORDER_AWQ:     [0,4,1,5,2,6,3,7][c % 8]   (GEMM, awq_kernel_gemm.rs:10-30)
+ *     CAWQ_ORDER_NATURAL: c % 8                      (dequantize, awq_kernel.rs:9-19)
+ *   Dequantized value = (float(q) - float(z)) * s, computed in F.
+ *
+ * Conventions of every entry point:
+ *   - All tensors are caller-allocated device memory, row-major and dense.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Launches are
+ *     asynchronous; the calls never synchronise the device.
+ *   - Nothing here aborts the process: failures return a cawq_status and the
+ *     calling thread's cawq_last_error() holds a message. Shape-rule messages
+ *     are the reference's assert! texts verbatim.
+ *   - The GPU entry points need an sm_100 device; on anything else they return
+ *     CAWQ_ERR_UNSUPPORTED. There is no CPU fallback.
+ */
+#ifndef CUBE_AWQ_H_
+#define CUBE_AWQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CAWQ_VERSION_MAJOR 0
+#define CAWQ_VERSION_MINOR 1
+#define CAWQ_MAX_RANK 8
+
+typedef enum cawq_status {
+  CAWQ_OK = 0,
+  CAWQ_ERR_INVALID_SHAPE = 1, /* a shape rule of the reference failed        */
+  CAWQ_ERR_DTYPE = 2,         /* unsupported dtype or packed element size    */
+  CAWQ_ERR_ALIGNMENT = 3,     /* pointer alignment the call needs is missing */
+  CAWQ_ERR_CUDA = 4,          /* CUDA runtime/driver error                   */
+  CAWQ_ERR_NCCL = 5,          /* collective failure (tensor-parallel layer)  */
+  CAWQ_ERR_TIMEOUT = 6,       /* a bounded device-side wait gave up          */
+  CAWQ_ERR_UNSUPPORTED = 7,   /* valid request, but no sm_100 device         */
+  CAWQ_ERR_NULL_POINTER = 8,  /* a required pointer argument was NULL        */
+  CAWQ_ERR_INVALID_ARGUMENT = 9
+} cawq_status;
+
+/* F of the reference: activations, scales, bias, dequantized weights. */
+typedef enum cawq_dtype { CAWQ_F32 = 0, CAWQ_F16 = 1, CAWQ_BF16 = 2 } cawq_dtype;
+
+typedef enum cawq_order { CAWQ_ORDER_AWQ = 0, CAWQ_ORDER_NATURAL = 1 } cawq_order;
+
+/* Kernel families the planner can choose (cawq_plan.path). */
+typedef enum cawq_path {
+  CAWQ_PATH_AUTO = 0,
+  CAWQ_PATH_DECODE = 1,  /* memory-bound small-M kernel (M <= 16)          */
+  CAWQ_PATH_PREFILL = 2, /* tcgen05/TMEM tensor-core kernel (large M)      */
+  CAWQ_PATH_GENERIC = 3  /* CUDA-core kernel for any shape the rules allow */
+} cawq_path;
+
+/*
+ * Mirror of the reference's ShapeConfig (awq_kernel_gemm.rs:35-79). The
+ * tile fields are the reference's launch tiles; they take part in validation
+ * exactly as in the reference. The B200 kernels choose their own tiles
+ * (cawq_plan), so the fields do not change the arithmetic.
+ */
+typedef struct cawq_shape_config {
+  size_t m, k, n;
+  size_t tile_m;    /* 8 | 16 | 32 in the reference   */
+  size_t tile_n;    /* 32 | 64 | 128                  */
+  size_t inner_k;   /* 32 | 64                        */
+  size_t line_size; /* 4                              */
+  size_t m_valid;
+} cawq_shape_config;
+
+/* A device buffer with its row-major shape (mirrors TensorHandleRef). */
+typedef struct cawq_tensor_desc {
+  const void* data;
+  int rank;
+  size_t shape[CAWQ_MAX_RANK];
+  size_t elem_size; /* bytes per element */
+} cawq_tensor_desc;
+
+/* Arguments of cawq_awq_gemm_linear. */
+typedef struct cawq_gemm_args {
+  cawq_tensor_desc input;   /* [.., M, K]  F                           */
+  cawq_tensor_desc qweight; /* [K, N/8]    32-bit                      */
+  cawq_tensor_desc qzeros;  /* [K/g, N/8]  32-bit                      */
+  cawq_tensor_desc scales;  /* [K/g, N]    F                           */
+  cawq_tensor_desc bias;    /* [N] F, or data == NULL for no bias      */
+  cawq_tensor_desc output;  /* [.., M, N]  F (written)                 */
+  cawq_dtype dtype;         /* F                                       */
+  size_t group_size;
+} cawq_gemm_args;
+
+/* A kernel choice for one (M, K, N, g, dtype) problem. */
+typedef struct cawq_plan {
+  int path;      /* cawq_path                                            */
+  int split;     /* decode: CTAs per cluster splitting K (1..16)         */
+  int warps;     /* decode: warps per CTA                                */
+  int tile_n;    /* prefill: CTA tile N (64..256)                        */
+  int stages;    /* pipeline stages                                      */
+  int reserved[3];
+} cawq_plan;
+
+/* ----------------------------------------------------------------------- */
+/* Library and device                                                      */
+/* ----------------------------------------------------------------------- */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* cawq_last_error(void);
+
+/* Version string, e.g. "cube_awq 0.1 sm_100a". */
+const char* cawq_version(void);
+
+/* 1 if `device` is an sm_100 GPU this library has code for, else 0. */
+int cawq_device_supported(int device);
+
+/*
+ * Reads (and with reset != 0 clears) the device-side error word of the
+ * current device: bit 0 = a bounded wait inside a kernel timed out.
+ * Synchronises the device.
+ */
+cawq_status cawq_device_error(int reset, uint32_t* word);
+
+/* ----------------------------------------------------------------------- */
+/* Shape rules (host only; no GPU needed)                                  */
+/* ----------------------------------------------------------------------- */
+
+/* Replaces ShapeConfig::new (awq_kernel_gemm.rs:48-57); note the m, n, k order. */
+cawq_status cawq_shape_config_new(size_t m, size_t n, size_t k, size_t tile_m,
+                                  size_t tile_n, size_t inner_k,
+                                  cawq_shape_config* out);
+
+/* Replaces ShapeConfig::new_with_valid_m (awq_kernel_gemm.rs:59-78). */
+cawq_status cawq_shape_config_new_with_valid_m(size_t m, size_t n, size_t k,
+                                               size_t tile_m, size_t tile_n,
+                                               size_t inner_k, size_t m_valid,
+                                               cawq_shape_config* out);
+
+/* Replaces validate_launch_params (awq_kernel_gemm.rs:160-162). */
+cawq_status cawq_validate_launch_params(const cawq_shape_config* shape,
+                                        size_t group_size);
+
+/* Replaces validate_decode_launch_params (awq_kernel_gemm.rs:164-171). */
+cawq_status cawq_validate_decode_launch_params(const cawq_shape_config* shape,
+                                               size_t group_size);
+
+/* Replaces select_tile_m / select_tile_n (awq_gemm.rs:30-52), including the
+ * AWQ_GEMM_FORCE_TILE_M override (awq_gemm.rs:20-28). */
+size_t cawq_select_tile_m(size_t m);
+size_t cawq_select_tile_n(size_t n);
+
+/* ----------------------------------------------------------------------- */
+/* Fused AWQ GEMM                                                          */
+/* ----------------------------------------------------------------------- */
+
+/*
+ * Replaces awq_gemm_linear<R, F> (awq_kernel_gemm.rs:626-771): the same
+ * rank/shape asserts with the same messages, the same m_valid resolution
+ * (:675-681) and decode/prefill rule validation (:691-696), then one fused
+ * launch. `shape` may be NULL: the module's tile choice (awq_gemm.rs:205-207)
+ * is then used for validation. Bias, when present, is added in the epilogue
+ * after the full K reduction (awq_gemm.rs:225-228).
+ */
+cawq_status cawq_awq_gemm_linear(const cawq_gemm_args* args,
+                                 const cawq_shape_config* shape, void* stream);
+
+/*
+ * Hot-path form of the same GEMM with plain pointers, the call that
+ * AWQGEMMLinear::forward (awq_gemm.rs:146-232) makes after flattening:
+ *   out[rows, N] = x[rows, K] · deq(qweight, qzeros, scales) (+ bias)
+ * x, scales and bias are `dtype`; out is `out_dtype` (dtype, or CAWQ_F32 for
+ * the fp32 partial sums of a row-parallel shard). `order` selects the nibble
+ * order (CAWQ_ORDER_AWQ as gemm_awq; CAWQ_ORDER_NATURAL gives the fused form
+ * of AWQLinear::forward, awq_dequantize.rs:74-108). `ld_out` is the row
+ * stride of out in elements (0 = N), so a column shard can write into its
+ * slice of a wider output. Module rules apply (awq_gemm.rs:77-95, and the
+ * kernel rules of awq_kernel_gemm.rs:89-158 with the module's tiles).
+ */
+cawq_status cawq_gemm(const void* x, const uint32_t* qweight,
+                      const uint32_t* qzeros, const void* scales,
+                      const void* bias, void* out, size_t rows, size_t k,
+                      size_t n, size_t group_size, cawq_dtype dtype,
+                      cawq_dtype out_dtype, cawq_order order, size_t ld_out,
+                      void* stream);
+
+/*
+ * Same as cawq_gemm with an explicit plan (path / split / tiles); used by the
+ * autotuner and by tests that pin a kernel. Returns CAWQ_ERR_INVALID_ARGUMENT
+ * if the plan cannot run this problem.
+ */
+cawq_status cawq_gemm_with_plan(const void* x, const uint32_t* qweight,
+                                const uint32_t* qzeros, const void* scales,
+                                const void* bias, void* out, size_t rows,
+                                size_t k, size_t n, size_t group_size,
+                                cawq_dtype dtype, cawq_dtype out_dtype,
+                                cawq_order order, size_t ld_out,
+                                const cawq_plan* plan, void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* Planner / autotuner                                                     */
+/* ----------------------------------------------------------------------- */
+
+/* The plan cawq_gemm would use now (cache hit, else the static heuristic). */
+cawq_status cawq_plan_get(size_t rows, size_t k, size_t n, size_t group_size,
+                          cawq_dtype dtype, cawq_plan* plan);
+
+/* Pins a plan for this problem in the process-wide cache. */
+cawq_status cawq_plan_set(size_t rows, size_t k, size_t n, size_t group_size,
+                          cawq_dtype dtype, const cawq_plan* plan);
+
+/* Clears the process-wide plan cache. */
+void cawq_plan_cache_clear(void);
+
+/*
+ * Times every candidate plan for this problem on `stream` with the given
+ * device buffers (they are read, and `out` is overwritten), stores the
+ * fastest in the cache and returns it. Synchronises the stream.
+ */
+cawq_status cawq_autotune(const void* x, const uint32_t* qweight,
+                          const uint32_t* qzeros, const void* scales,
+                          void* out, size_t rows, size_t k, size_t n,
+                          size_t group_size, cawq_dtype dtype,
+                          cawq_plan* best, void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* Standalone dequantize                                                   */
+/* ----------------------------------------------------------------------- */
+
+/*
+ * Replaces dequantize_native<R, E> (awq_kernel.rs:63-111) and its caller
+ * dequantize_awq (kernel/mod.rs:9-51): out[K, N] = (q - z) * s in `dtype`,
+ * natural nibble order as the reference kernel reads it (CAWQ_ORDER_AWQ is an
+ * extension). The element-size asserts of awq_kernel.rs:73-84 and the
+ * out_width % 32 assert of :87 are reproduced with the same messages.
+ */
+cawq_status cawq_dequantize_native(const cawq_tensor_desc* qweight,
+                                   const cawq_tensor_desc* qzeros,
+                                   const cawq_tensor_desc* scales,
+                                   const cawq_tensor_desc* output,
+                                   size_t group_size, cawq_dtype dtype,
+                                   cawq_order order, void* stream);
+
+/* Plain-pointer form: out[k, n] from qweight[k, n/8], qzeros[k/g, n/8],
+ * scales[k/g, n]. */
+cawq_status cawq_dequantize(const uint32_t* qweight, const uint32_t* qzeros,
+                            const void* scales, void* out, size_t k, size_t n,
+                            size_t group_size, cawq_dtype dtype,
+                            cawq_order order, void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* Tensor-parallel helpers (no reference counterpart: the reference is     */
+/* single-device; these give the shard arithmetic of the sharded layers)   */
+/* ----------------------------------------------------------------------- */
+
+/*
+ * Column-parallel (N split): rank `rank` of `world` owns output columns
+ * [*n_begin, *n_begin + *n_len). Requires N % (32 * world) == 0.
+ */
+cawq_status cawq_tp_column_shard(size_t n, int world, int rank,
+                                 size_t* n_begin, size_t* n_len);
+
+/*
+ * Row-parallel (K split on group boundaries): rank owns K rows
+ * [*k_begin, *k_begin + *k_len). Requires (K / g) % world == 0.
+ */
+cawq_status cawq_tp_row_shard(size_t k, size_t group_size, int world, int rank,
+                              size_t* k_begin, size_t* k_len);
+
+/*
+ * Gathers `world` column shards stored rank-major as src[world][rows][n/world]
+ * into dst[rows][n] (the layout an all-gather of [rows, n/world] slices
+ * produces, turned back into row-major). Element size from dtype.
+ */
+cawq_status cawq_tp_interleave_columns(const void* src, void* dst, size_t rows,
+                                       size_t n, int world, cawq_dtype dtype,
+                                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUBE_AWQ_H_ */

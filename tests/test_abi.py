@@ -1,0 +1,78 @@
+"""The C ABI library loads without a GPU and exports what the header declares."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+import cube_awq_b200 as cawq
+from cube_awq_b200 import _lib
+from conftest import REPO
+
+
+def _declared():
+    with open(os.path.join(REPO, "include", "cube_awq.h")) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(cawq_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declarations_are_exported():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    declared = _declared()
+    assert len(declared) >= 20
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/cube_awq.h but not exported"
+    assert sorted(_lib.EXPORTED) == declared
+
+
+def test_only_c_abi_symbols_are_exported():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    syms = [l.split()[-1] for l in out.splitlines() if " T " in l]
+    assert syms and all(s.startswith("cawq_") for s in syms), syms
+
+
+def test_version_and_no_device_on_cpu_box():
+    assert cawq.version().startswith("cube_awq")
+    import torch
+    if not torch.cuda.is_available():
+        assert _lib.lib().cawq_device_supported(0) == 0
+
+
+def test_gpu_entry_points_refuse_without_sm100():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    lib = _lib.lib()
+    st = lib.cawq_dequantize(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
+                             ctypes.c_void_p(16), 32, 32, 32, _lib.CAWQ_F32, _lib.CAWQ_ORDER_NATURAL,
+                             None)
+    assert st in (_lib.CAWQ_ERR_CUDA, _lib.CAWQ_ERR_UNSUPPORTED)
+    assert _lib.last_error()
+
+
+@pytest.mark.parametrize("n,world", [(57344, 8), (12288, 4), (4096, 2), (64, 2)])
+def test_column_shards_tile_n(n, world):
+    lib = _lib.lib()
+    spans = []
+    for r in range(world):
+        b, l = ctypes.c_size_t(), ctypes.c_size_t()
+        assert lib.cawq_tp_column_shard(n, world, r, ctypes.byref(b), ctypes.byref(l)) == 0
+        spans.append((b.value, l.value))
+    assert spans[0][0] == 0 and sum(l for _, l in spans) == n
+    assert all(spans[i][0] + spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+
+
+def test_row_shards_follow_group_boundaries():
+    lib = _lib.lib()
+    b, l = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.cawq_tp_row_shard(28672, 128, 8, 3, ctypes.byref(b), ctypes.byref(l)) == 0
+    assert (b.value, l.value) == (3 * 3584, 3584) and b.value % 128 == 0
+    assert lib.cawq_tp_row_shard(4096, 128, 3, 0, ctypes.byref(b), ctypes.byref(l)) == \
+        _lib.CAWQ_ERR_INVALID_SHAPE
+    assert "world" in _lib.last_error()
+    assert lib.cawq_tp_column_shard(4096, 3, 0, ctypes.byref(b), ctypes.byref(l)) == \
+        _lib.CAWQ_ERR_INVALID_SHAPE

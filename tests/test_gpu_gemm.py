@@ -1,0 +1,160 @@
+"""Fused GEMM parity on the GPU against the oracle and the reference's tests.
+
+* closed-form KATs of awq_kernel_gemm.rs:1119-1391 through awq_gemm_linear,
+  with the reference harness's ShapeConfig (run_kernel, :870-960);
+* module fixtures of awq_gemm.rs:408-604 through AWQGEMMLinear.forward;
+* seeded random problems on every kernel path and plan, f32 / f16 / bf16,
+  against the exact (fp64) oracle with max|y - y_ref| <= tol * ||y_ref||_inf
+  (tol: f32 1e-3, f16 5e-3, bf16 1e-2; see helpers.GEMM_TOL).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cube_awq_b200 as cawq
+import oracle
+from helpers import (GEMM_TOL, as_f64, kat_expected, load_json, load_npz, max_rel_err,
+                     random_awq, to_numpy, to_torch, uniform_kat_tensors)
+
+pytestmark = pytest.mark.gpu
+
+KATS = load_json("kat_gemm_uniform.json")
+PATH_DECODE, PATH_GENERIC = 1, 3
+
+
+def _harness_shape(kat):
+    # run_kernel (awq_kernel_gemm.rs:881-899): tile_m 32, inner_k 64 or 32
+    k, n, gs = kat["k"], kat["n"], kat["group_size"]
+    inner_k = 64 if (k >= 64 and k % 64 == 0 and gs >= 64 and gs % 64 == 0) else 32
+    tile_n = 128 if (n >= 128 and n % 128 == 0) else 64 if (n >= 64 and n % 64 == 0) else 32
+    return cawq.ShapeConfig.new(kat["b"] * kat["m"], n, k, 32, tile_n, inner_k)
+
+
+@pytest.mark.parametrize("kat", KATS, ids=[k["name"] for k in KATS])
+def test_kernel_kats(cuda_device, kat):
+    x, qw, qz, sc = uniform_kat_tensors(kat)
+    out = torch.full((x.shape[0], kat["n"]), float("nan"), device=cuda_device)
+    cawq.awq_gemm_linear(to_torch(x, "f32", cuda_device), to_torch(qw, "u32", cuda_device),
+                         to_torch(qz, "u32", cuda_device), to_torch(sc, "f32", cuda_device), out,
+                         _harness_shape(kat), kat["group_size"])
+    got = out.cpu().numpy()
+    assert np.abs(got - kat_expected(kat, x)).max() <= kat["tol"]
+
+
+MODULE_FIXTURES = [
+    "module_forward_b2_m32_k64_n32_g32.npz",
+    "module_forward_bias_b2_m32_k64_n32_g32.npz",
+    "module_forward_decode_b2_m1_k64_n32_g64.npz",
+    "module_forward_4d_1x16x14_k64_n32_g32.npz",
+]
+
+
+@pytest.mark.parametrize("name", MODULE_FIXTURES)
+def test_module_forward_fixtures(cuda_device, name):
+    f = load_npz(name)
+    bias = f.get("bias")
+    layer = cawq.AWQGEMMLinear(to_torch(f["qweight"], "u32", cuda_device),
+                               to_torch(f["qzeros"], "u32", cuda_device),
+                               to_torch(f["scales"], "f32", cuda_device),
+                               None if bias is None else to_torch(bias, "f32", cuda_device))
+    y = layer.forward(to_torch(f["x"], "f32", cuda_device))
+    assert list(y.shape) == list(f["expected"].shape)
+    got = y.cpu().numpy()
+    assert np.abs(got - f["expected"]).max() <= float(f["tol"])
+    assert max_rel_err(got, f["expected"]) <= 1e-3
+
+
+def test_module_handles_non_divisible_m(cuda_device):
+    # awq_gemm.rs:505-515
+    f = load_npz("module_forward_b2_m32_k64_n32_g32.npz")
+    layer = cawq.AWQGEMMLinear(to_torch(f["qweight"], "u32", cuda_device),
+                               to_torch(f["qzeros"], "u32", cuda_device),
+                               to_torch(f["scales"], "f32", cuda_device))
+    y = layer.forward(torch.zeros(1, 14, 64, device=cuda_device))
+    assert list(y.shape) == [1, 14, 32]
+    assert float(y.abs().max()) == 0.0
+
+
+def _run(cuda_device, dtype, rows, k, n, g, plan=None, bias=False, order="awq", out_dtype=None,
+         seed=0):
+    x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed)
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dtype]
+    y = cawq.gemm(to_torch(x, dtype, cuda_device), to_torch(qw, "u32", cuda_device),
+                  to_torch(qz, "u32", cuda_device), to_torch(s, dtype, cuda_device), g,
+                  bias=to_torch(b, dtype, cuda_device) if bias else None, order=order,
+                  plan=plan, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    got = as_f64(to_numpy(y, dtype if y.dtype == tdt else "f32"), dtype if y.dtype == tdt else "f32")
+    ref = oracle.gemm_f64(x, qw, qz, s, g, bias=b if bias else None, dtype=dtype, order=order,
+                          deq_round=False)
+    return got, ref, (x, qw, qz, s, b)
+
+
+DECODE_SHAPES = [(128, 256, 32), (512, 384, 64), (1024, 4096, 128), (4096, 4160, 128),
+                 (11008, 512, 128), (3584, 4608, 64)]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rows", [1, 2, 5, 8, 9, 16])
+@pytest.mark.parametrize("k,n,g", DECODE_SHAPES)
+def test_decode_default_plan_parity(cuda_device, dtype, rows, k, n, g):
+    got, ref, _ = _run(cuda_device, dtype, rows, k, n, g)
+    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("split", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("warps", [4, 8])
+@pytest.mark.parametrize("stages", [2, 4])
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+def test_decode_every_plan(cuda_device, split, warps, stages, dtype):
+    plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages}
+    got, ref, _ = _run(cuda_device, dtype, 3, 2048, 1024, 128, plan=plan)
+    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("rows,k,n,g", [(1, 64, 32, 32), (7, 256, 96, 32), (33, 512, 256, 64),
+                                        (130, 256, 4096, 128)])
+def test_generic_path_parity(cuda_device, dtype, rows, k, n, g):
+    got, ref, _ = _run(cuda_device, dtype, rows, k, n, g, plan={"path": PATH_GENERIC})
+    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("path", [PATH_DECODE, PATH_GENERIC])
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_bias_natural_order_and_fp32_out(cuda_device, path, dtype):
+    plan = {"path": path, "split": 4, "warps": 8, "stages": 2} if path == PATH_DECODE else {"path": path}
+    got, ref, _ = _run(cuda_device, dtype, 4, 1024, 512, 64, plan=plan, bias=True, order="natural",
+                       out_dtype=torch.float32)
+    assert max_rel_err(got, ref) <= (GEMM_TOL["f32"] if dtype == "f32" else 2e-3)
+
+
+def test_column_slice_output_ld(cuda_device):
+    # a column shard writing into its slice of a wider output (ld_out = 1024)
+    x, qw, qz, s, _ = random_awq(512, 256, 128, "f16", 2, seed=4)
+    full = torch.zeros(2, 1024, dtype=torch.float16, device=cuda_device)
+    cawq.gemm(to_torch(x, "f16", cuda_device), to_torch(qw, "u32", cuda_device),
+              to_torch(qz, "u32", cuda_device), to_torch(s, "f16", cuda_device), 128,
+              out=full[:, 256:512])
+    ref = oracle.gemm_f64(x, qw, qz, s, 128, dtype="f16", deq_round=False)
+    got = full.float().cpu().numpy()
+    assert max_rel_err(got[:, 256:512], ref) <= GEMM_TOL["f16"]
+    assert float(full[:, :256].abs().max()) == 0.0 and float(full[:, 512:].abs().max()) == 0.0
+
+
+def test_cfg1_decode_full_size_f32(cuda_device):
+    # M=1, K=N=4096, g=128, f32, against the reference numerics
+    got, ref, (x, qw, qz, s, _) = _run(cuda_device, "f32", 1, 4096, 4096, 128, seed=0x5EED)
+    assert max_rel_err(got, ref) <= 1e-3
+    ref_numerics = oracle.gemm_ref(x, qw, qz, s, 128, dtype="f32").astype(np.float64)
+    assert max_rel_err(got, ref_numerics) <= 1e-3
+    assert cawq.device_error() == 0
+
+
+def test_f16_distance_to_reference_numerics_is_reported(cuda_device):
+    # The reference accumulates in f16; this build in fp32. Both are compared
+    # with the exact sum: the fused kernel must be at least as close.
+    got, ref, (x, qw, qz, s, _) = _run(cuda_device, "f16", 1, 4096, 1024, 128, seed=3)
+    ref16 = oracle.gemm_ref(x, qw, qz, s, 128, dtype="f16").astype(np.float64)
+    assert max_rel_err(got, ref) <= max_rel_err(ref16, ref) + 1e-3
