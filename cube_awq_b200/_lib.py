@@ -72,7 +72,7 @@ class PlanC(ctypes.Structure):
 
     def as_dict(self) -> dict:
         return {"path": self.path, "split": self.split, "warps": self.warps,
-                "tile_n": self.tile_n, "stages": self.stages}
+                "tile_n": self.tile_n, "stages": self.stages, "pdl": self.reserved[0] == 0}
 
 
 _lib = None

@@ -301,9 +301,18 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
   if (ld_out < n) return fail(CAWQ_ERR_INVALID_SHAPE, "ld_out must be >= n");
   if (module_rules) {
     if (!(k > 0)) return fail(CAWQ_ERR_INVALID_SHAPE, "input last dim (K) must be > 0");
-    if (rows > 0) {
-      cawq_status st = validate_module(rows, k, n, g);
-      if (st != CAWQ_OK) return st;
+    if (order == CAWQ_ORDER_AWQ) {
+      // AWQGEMMLinear (awq_gemm.rs:77-95 and the kernel rules it launches with)
+      if (rows > 0) {
+        cawq_status st = validate_module(rows, k, n, g);
+        if (st != CAWQ_OK) return st;
+      }
+    } else {
+      // AWQLinear (awq_dequantize.rs:25-28): its forward never runs the GEMM rules
+      if (n % 8 != 0) return fail(CAWQ_ERR_INVALID_SHAPE, "assertion failed: self.d_output % 8 == 0");
+      if (g == 0 || k % g != 0)
+        return fail(CAWQ_ERR_INVALID_SHAPE, "assertion failed: self.d_input % self.group_size == 0");
+      if (n % 32 != 0) return fail(CAWQ_ERR_INVALID_SHAPE, "assertion failed: self.d_output % 32 == 0");
     }
   }
   if (rows == 0) return CAWQ_OK;
@@ -523,10 +532,10 @@ CAWQ_API cawq_status cawq_autotune(const void* x, const uint32_t* qweight, const
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   GemmProblem p = {x, qweight, qzeros, scales, nullptr, out, rows, k, n, g, n,
                    dtype, dtype, CAWQ_ORDER_AWQ, s};
-  cawq_plan cands[96];
+  cawq_plan cands[160];
   int nc = 0, c2 = 0;
-  if (rows <= 16) decode_candidates(p, dev, cands, &nc, 64);
-  prefill_candidates(p, dev, cands + nc, &c2, 96 - nc - 1);
+  if (rows <= 16) decode_candidates(p, dev, cands, &nc, 128);
+  prefill_candidates(p, dev, cands + nc, &c2, 160 - nc - 1);
   nc += c2;
   cands[nc++] = generic_plan();
   cudaEvent_t e0, e1;

@@ -9,13 +9,19 @@
 // kernel turns nibbles into tensor-core operands with two instructions per
 // pair of weights and lets mma.sync accumulate in fp32:
 //
-//   * Tiles. A CTA owns 128 output columns (16 packed words per k row) and a
-//     slice of K. A cluster of `split` CTAs shares one column tile and splits
-//     K; their partial sums are added through distributed shared memory, so
-//     no global scratch is needed.
-//   * Loads. Each warp streams its own k range through a ring of TMA stages:
-//     a 64-row x 16-word weight box (64-byte swizzle) and the matching
-//     64-column slice of X (128-byte swizzle), both landing on one mbarrier.
+//   * Tiles. A CTA owns a band of `strips` x 128 output columns and a slice
+//     of K. Each strip is handled by two consumer warps, one per 64-column half
+//     (one packed word per lane). A cluster of `split` CTAs shares one band and
+//     splits K; partial sums are added across the cluster through distributed
+//     shared memory, so no global scratch is needed.
+//   * Loads. One producer warp streams 64-row stages through a TMA ring: one
+//     128-byte-row weight box (128-byte swizzle) per pair of strips, back to
+//     back, so every k row is requested as one contiguous run, plus the scale
+//     and zero rows of the
+//     stage's groups (bulk copies) and the matching slice of X (128-byte
+//     swizzle). Weights, scales and zeros do not depend on the previous kernel
+//     in the stream, so they are requested before griddepcontrol.wait; X
+//     after it (programmatic dependent launch).
 //   * Operands. The MMA is swapped: A = W^T (16 output columns x 16 k),
 //     B = X^T (16 k x 8 rows of X). Two packed words from k rows r, r' are
 //     byte-interleaved (prmt) so one lop3 yields the f16 pair
@@ -23,7 +29,8 @@
 //     place as 1024 + 16 q. bf16 (and f32 inputs, split into bf16 hi + lo)
 //     use 128 + q with a shift. No per-weight subtraction or scaling.
 //   * Group fold. Within a quantization group, sum_k x (c + q) is accumulated
-//     by the MMA; when the group ends each output adds
+//     by the MMA, and sum_k x by one more MMA with an all-ones A. When the
+//     group ends each output adds
 //         s' * (D - c' * sum_k x)      (c' = offset + zero, s' = scale)
 //     in fp32. This equals sum_k x (q - z) s up to fp32 rounding.
 //
@@ -36,174 +43,262 @@
 
 namespace cawq {
 
-constexpr int kDecTileCols = 128;  // output columns per CTA
-constexpr int kDecTileWords = 16;  // packed words per k row in a CTA tile
+constexpr int kDecTileCols = 128;  // output columns per strip (consumer warp)
+constexpr int kDecTileWords = 16;  // packed words per k row in a strip
+constexpr int kDecBoxWords = 32;   // packed words per k row in a weight box (2 strips)
 constexpr int kDecStageRows = 64;  // k rows per TMA stage (4 MMA steps)
 constexpr int kDecMaxWarps = 8;
-constexpr int kDecMaxStages = 4;
+constexpr int kDecMaxStages = 8;
 
+// Shared-memory layout of one ring slot:
+//   [X tile: XB rows x 64 k, 128B swizzle][W: strips/2 x 64 rows x 128 B, 128B swizzle]
+//   [S: gps rows x band columns, F][Z: gps rows x band/8 words]
+// gps = quantization groups a 64-row stage can touch.
 template <int DT, int MT>
 struct DecodeLayout {
   using T = typename DType<DT>::T;
-  static constexpr int XB = 8 * MT;                               // X rows per tile
+  static constexpr int XB = 8 * MT;
   static constexpr int kXBytes = XB * kDecStageRows * (int)sizeof(T);
-  static constexpr int kWBytes = kDecStageRows * kDecTileWords * 4;  // 4096
-  static constexpr int kSlot = kXBytes + kWBytes;                  // multiple of 1024
-  static constexpr int kRedBytes = kDecMaxWarps * XB * kDecTileCols * 4;
-  static size_t smem_bytes(int warps, int stages) {
-    size_t ring = (size_t)warps * stages * kSlot;
-    size_t red = (size_t)warps * XB * kDecTileCols * 4;
+  static constexpr int kWBytes = kDecStageRows * kDecTileWords * 4;  // 4096 per strip
+  // groups a 64-row window starting at a multiple of 64 can touch (g % 16 == 0)
+  static __host__ __device__ int gps(uint32_t g) {
+    if (64 % g == 0) return (int)(64 / g);
+    if (g % 64 == 0) return 1;
+    return (int)(64 / g) + 2;
+  }
+  static __host__ __device__ size_t s_off(int strips) {
+    return (size_t)kXBytes + (size_t)strips * kWBytes;
+  }
+  static __host__ __device__ size_t s_row_bytes(int strips) {
+    return (size_t)strips * kDecTileCols * sizeof(T);
+  }
+  static __host__ __device__ size_t z_off(int strips, uint32_t g) {
+    return s_off(strips) + gps(g) * s_row_bytes(strips);
+  }
+  static __host__ __device__ size_t z_row_bytes(int strips) {
+    return (size_t)strips * kDecTileWords * 4;
+  }
+  static __host__ __device__ size_t slot_bytes(int strips, uint32_t g) {
+    const size_t raw = z_off(strips, g) + gps(g) * z_row_bytes(strips);
+    return (raw + 1023) / 1024 * 1024;
+  }
+  static size_t smem_bytes(int strips, int stages, uint32_t g) {
+    size_t ring = slot_bytes(strips, g) * stages;
+    size_t red = (size_t)strips * XB * kDecTileCols * 4;
     size_t body = ring > red ? ring : red;
-    return 1024 /* alignment slack */ + body + (size_t)warps * stages * 8;
+    return 1024 /* alignment slack */ + body + (size_t)stages * 16;
   }
 };
 
+// Consumer warps per CTA (strips x 2 halves), bounded by the register file:
+// about 80 registers per thread for 8-row X tiles, 128 for 16.
+__host__ __device__ constexpr int dec_max_consumers(int mt) { return mt == 1 ? 16 : 8; }
+
 // Physical k row (0..15 within a 16-row step) that lane quad position t uses
-// for fragment slot i (0..3). Chosen so the four rows a half-warp reads fall
-// in four different bank groups under the 64-byte swizzle.
-__device__ __forceinline__ int dec_row(int t, int i) {
-  const int base = (i & 1) * 2 + (i >> 1) * 8;  // {0, 2, 8, 10}
-  return base + (t & 1) + 4 * (t >> 1);
-}
+// for fragment slot i (0..3). The four rows one load instruction touches,
+// {2t + (i & 1) + 8 (i >> 1)}, differ in bits 1-2, so under the 128-byte
+// swizzle their 32-byte column pieces land in four different bank groups;
+// and the k pairs of one fragment register, (2t, 2t+1) and (2t+8, 2t+9), are
+// adjacent, so X^T fragments are single 32-bit loads.
+__device__ __forceinline__ int dec_row(int t, int i) { return 2 * t + (i & 1) + 8 * (i >> 1); }
 
 // prmt selectors: bytes (b of word a, b of word b) -> result bytes 0 and 2.
 __device__ __forceinline__ uint32_t dec_sel(int b) {
   return static_cast<uint32_t>(b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12));
 }
 
-template <int DT, int ODT, int ORDER, int MT>
-__global__ void __launch_bounds__(kDecMaxWarps * 32)
+template <int DT, int ODT, int ORDER, int MT, bool GA>
+__global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                   const uint32_t* __restrict__ qz, const typename DType<DT>::T* __restrict__ sc,
                   const typename DType<DT>::T* __restrict__ bias,
                   typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
-                  uint32_t g, uint32_t ld_out, uint32_t split, uint32_t nstage_ring) {
+                  uint32_t g, uint32_t ld_out, uint32_t split, uint32_t nstage_ring,
+                  uint32_t strips_u) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
   constexpr bool kF16Mma = (DT == kF16);
   constexpr int XB = L::XB;
+  // A operand of the "ones" MMA: sum_k x[b][k] for every row b of X comes out
+  // of the tensor core with the same accumulation as the weight MMAs.
+  constexpr uint32_t kOnes = kF16Mma ? 0x3C003C00u : 0x3F803F80u;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
-  const int nwarps = blockDim.x >> 5;
+  const int strips = static_cast<int>(strips_u);
+  const int consumers = 2 * strips;  // warps 0..consumers-1; the producer follows
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;
   const int t = lane & 3;
 
   const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
-  const uint32_t tile = blockIdx.x / split;
-  const uint32_t p0 = tile * kDecTileWords;
+  const uint32_t band = blockIdx.x / split;
+  const uint32_t pband = band * strips * kDecTileWords;  // first packed column of the band
   const uint32_t npk = n >> 3;
   const uint32_t steps = k >> 4;
   const uint32_t nst_total = (steps + 3) >> 2;
   const uint32_t c_beg = (uint32_t)((uint64_t)nst_total * rank / split);
   const uint32_t c_end = (uint32_t)((uint64_t)nst_total * (rank + 1) / split);
-  const uint32_t w_beg = c_beg + (c_end - c_beg) * warp / nwarps;
-  const uint32_t w_end = c_beg + (c_end - c_beg) * (warp + 1) / nwarps;
-  const int nst = static_cast<int>(w_end - w_beg);
+  const int nst = static_cast<int>(c_end - c_beg);
+  const uint32_t end_step = c_end * 4 < steps ? c_end * 4 : steps;
   const int NS = static_cast<int>(nstage_ring);
+  const size_t slot = L::slot_bytes(strips, g);
+  const int gps = L::gps(g);
 
-  const size_t ring_bytes = (size_t)nwarps * NS * L::kSlot;
-  const size_t red_bytes = (size_t)nwarps * XB * kDecTileCols * 4;
-  uint8_t* ring = smem + (size_t)warp * NS * L::kSlot;
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + (ring_bytes > red_bytes ? ring_bytes : red_bytes)) +
-      warp * NS;
+  const size_t ring_bytes = slot * NS;
+  const size_t red_bytes = (size_t)strips * XB * kDecTileCols * 4;
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + (ring_bytes > red_bytes ? ring_bytes : red_bytes));
+  uint64_t* empty = full + NS;
 
-  auto issue = [&](int j) {
-    const int slot = j % NS;
-    uint8_t* dst = ring + (size_t)slot * L::kSlot;
-    const int kr = static_cast<int>((w_beg + j) * kDecStageRows);
-    mbar_arrive_expect_tx(&bars[slot], L::kSlot);
-    if constexpr (DT == kF32) {
-      tma_load_2d(dst, &tm_x, kr, 0, &bars[slot]);
-      tma_load_2d(dst + XB * 128, &tm_x, kr + 32, 0, &bars[slot]);
-    } else {
-      tma_load_2d(dst, &tm_x, kr, 0, &bars[slot]);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], static_cast<uint32_t>(consumers));
     }
-    tma_load_2d(dst + L::kXBytes, &tm_w, static_cast<int>(p0), kr, &bars[slot]);
-  };
-
-  if (lane == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(&bars[s], 1);
     fence_mbarrier_init();
-    fence_proxy_async_smem();
-    for (int j = 0; j < NS && j < nst; ++j) issue(j);
   }
-  __syncwarp();
+  __syncthreads();
 
-  float D[MT][8][4];
-  float tot[MT][8][4];
+  bool ok = true;
+  if (warp == consumers) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      // valid columns of the band (the bulk copies must stay inside a row)
+      const uint32_t bcol0 = pband * 8;
+      const uint32_t vcols = min((uint32_t)(strips * kDecTileCols), n - min(n, bcol0));
+      const uint32_t ngroups = k / g;
+      const uint32_t tx = static_cast<uint32_t>(L::kXBytes + strips * L::kWBytes) +
+                          (uint32_t)gps * (vcols * (uint32_t)sizeof(T) + vcols / 2);
+      auto issue_weights = [&](int j) {
+        const int sl = j % NS;
+        uint8_t* dst = smem + sl * slot;
+        const int kr = static_cast<int>((c_beg + j) * kDecStageRows);
+        mbar_arrive_expect_tx(&full[sl], tx);
+        for (int b = 0; b < strips / 2; ++b) {
+          tma_load_2d(dst + L::kXBytes + 2 * b * L::kWBytes, &tm_w,
+                      static_cast<int>(pband + b * kDecBoxWords), kr, &full[sl]);
+        }
+        const uint32_t g0 = (uint32_t)kr / g;
+        for (int r = 0; r < gps; ++r) {
+          // rows past the last group repeat it; the fold never reads them
+          const uint32_t grp = min(g0 + r, ngroups - 1);
+          if (vcols) {
+            bulk_load_1d(dst + L::s_off(strips) + r * L::s_row_bytes(strips),
+                         sc + (size_t)grp * n + bcol0, vcols * sizeof(T), &full[sl]);
+            bulk_load_1d(dst + L::z_off(strips, g) + r * L::z_row_bytes(strips),
+                         qz + (size_t)grp * npk + pband, vcols / 2, &full[sl]);
+          }
+        }
+      };
+      auto issue_x = [&](int j) {
+        const int sl = j % NS;
+        uint8_t* dst = smem + sl * slot;
+        const int kr = static_cast<int>((c_beg + j) * kDecStageRows);
+        if constexpr (DT == kF32) {
+          tma_load_2d(dst, &tm_x, kr, 0, &full[sl]);
+          tma_load_2d(dst + XB * 128, &tm_x, kr + 32, 0, &full[sl]);
+        } else {
+          tma_load_2d(dst, &tm_x, kr, 0, &full[sl]);
+        }
+      };
+      const int pro = NS < nst ? NS : nst;
+      for (int j = 0; j < pro; ++j) issue_weights(j);  // independent of earlier kernels
+      pdl_wait();                                       // X may be the previous kernel's output
+      for (int j = 0; j < pro; ++j) issue_x(j);
+      for (int j = pro; j < nst && ok; ++j) {
+        const int sl = j % NS;
+        ok = mbar_wait_bounded(&empty[sl], static_cast<uint32_t>(((j / NS) - 1) & 1));
+        if (!ok) break;
+        issue_weights(j);
+        issue_x(j);
+      }
+    }
+    __syncwarp();
+    // all loads issued: the next kernel in the stream may start its prologue
+    pdl_launch_dependents();
+  }
+
+  float tot[MT][4][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) D[m][j][e] = tot[m][j][e] = 0.f;
-  float xacc[MT];
-#pragma unroll
-  for (int m = 0; m < MT; ++m) xacc[m] = 0.f;
+      for (int e = 0; e < 4; ++e) tot[m][j][e] = 0.f;
 
-  // scale / zero of the current group for this lane's 16 columns
-  const uint32_t pc = p0 + 2 * gq;
-  const bool col_valid = pc < npk;
-  float s_reg[16];
-  uint32_t z_reg[2];
-  auto load_sz = [&](uint32_t grp) {
-    if (col_valid) {
-      const uint2 zz = __ldg(reinterpret_cast<const uint2*>(qz + (size_t)grp * npk + pc));
-      z_reg[0] = zz.x;
-      z_reg[1] = zz.y;
-      const T* sp = sc + (size_t)grp * n + (size_t)pc * 8;
+  // this warp's strip and 64-column half
+  const int strip = warp % strips;
+  const int half = (warp / strips) & 1;
+  const int word = 8 * half + gq;  // packed word of this lane inside the strip
+
+  if (warp < consumers) {
+    // -------------------------------------------------------- consumers
+    uint32_t woff[4];  // weight rows dec_row(t, i) of a step, this lane's word
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = dec_row(t, i);
+      const int bw = 16 * (strip & 1) + word;  // word inside the 128-byte box row
+      woff[i] = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + r * 128 +
+                ((((bw >> 2) ^ (r & 7))) << 4) + ((bw & 3) << 2);
+    }
+    // X^T fragment of row 8m + gq: the k pairs (2t, 2t+1) and (2t+8, 2t+9) of a
+    // step are adjacent in the 128B-swizzled X tile, so each is one load.
+    uint32_t xrow[MT];  // byte offset of the row
+    uint32_t x7[MT];    // its swizzle phase
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const int xr = 8 * m + gq;
+      xrow[m] = xr * 128;
+      x7[m] = static_cast<uint32_t>(xr & 7);
+    }
+    // scales of this lane's 8 columns and its zero word inside the stage rows
+    const uint32_t s_lane = (uint32_t)(strip * kDecTileCols + 8 * word) * (uint32_t)sizeof(T);
+    const uint32_t z_lane = (uint32_t)(strip * kDecTileWords + word) * 4;
+
+    float D[MT][4][4];
+    float Dx[MT][4];  // sum_k x over the current group (ones MMA)
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) D[m][j][e] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) Dx[m][e] = 0.f;
+    }
+
+    // tot += s' * (D - c' * sum_k x) with this group's scales / zeros from the
+    // stage's shared-memory rows, then D = 0 (see the file comment)
+    auto fold = [&](const uint8_t* srow, const uint8_t* zrow) {
+      float s_reg[8];
       if constexpr (DT == kF32) {
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const float4 f = __ldg(reinterpret_cast<const float4*>(sp) + v);
+        for (int v = 0; v < 2; ++v) {
+          const float4 f = *reinterpret_cast<const float4*>(srow + s_lane + 16 * v);
           s_reg[4 * v + 0] = f.x; s_reg[4 * v + 1] = f.y;
           s_reg[4 * v + 2] = f.z; s_reg[4 * v + 3] = f.w;
         }
       } else {
+        const uint4 raw = *reinterpret_cast<const uint4*>(srow + s_lane);
+        const T* h = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-        for (int v = 0; v < 2; ++v) {
-          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(sp) + v);
-          const T* h = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) s_reg[8 * v + c] = DType<DT>::to_f32(h[c]);
-        }
+        for (int c = 0; c < 8; ++c) s_reg[c] = DType<DT>::to_f32(h[c]);
       }
-    } else {
-      z_reg[0] = z_reg[1] = 0u;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) s_reg[c] = 0.f;
-    }
-  };
-
-  auto fold = [&]() {
-    float X[MT][2];
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      float v = xacc[m];
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 2);
-      X[m][0] = __shfl_sync(0xffffffffu, v, (2 * t) * 4);
-      X[m][1] = __shfl_sync(0xffffffffu, v, (2 * t + 1) * 4);
-      xacc[m] = 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
+      const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + z_lane);
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const int j = u * 4 + b;
-        const float zl = static_cast<float>((z_reg[u] >> (8 * b)) & 15u);
-        const float zh = static_cast<float>((z_reg[u] >> (8 * b + 4)) & 15u);
-        const float sl = s_reg[u * 8 + col_of_nibble(2 * b, ORDER)];
-        float sh = s_reg[u * 8 + col_of_nibble(2 * b + 1, ORDER)];
+        // nibble -> float by the 2^23 exponent trick (no integer conversion)
+        const float zl = __uint_as_float(0x4B000000u | ((zw >> (8 * b)) & 15u)) - 8388608.f;
+        const float zh = __uint_as_float(0x4B000000u | ((zw >> (8 * b + 4)) & 15u)) - 8388608.f;
+        const float sl = s_reg[col_of_nibble(2 * b, ORDER)];
+        float sh = s_reg[col_of_nibble(2 * b + 1, ORDER)];
         float cl, ch;
         if constexpr (kF16Mma) {
           cl = 1024.f + zl;
-          ch = 1024.f + 16.f * zh;
+          ch = fmaf(16.f, zh, 1024.f);
           sh *= 0.0625f;
         } else {
           cl = 128.f + zl;
@@ -211,180 +306,181 @@ __global__ void __launch_bounds__(kDecMaxWarps * 32)
         }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          tot[m][j][0] = fmaf(sl, fmaf(-cl, X[m][0], D[m][j][0]), tot[m][j][0]);
-          tot[m][j][1] = fmaf(sl, fmaf(-cl, X[m][1], D[m][j][1]), tot[m][j][1]);
-          tot[m][j][2] = fmaf(sh, fmaf(-ch, X[m][0], D[m][j][2]), tot[m][j][2]);
-          tot[m][j][3] = fmaf(sh, fmaf(-ch, X[m][1], D[m][j][3]), tot[m][j][3]);
-          D[m][j][0] = D[m][j][1] = D[m][j][2] = D[m][j][3] = 0.f;
+          tot[m][b][0] = fmaf(sl, fmaf(-cl, Dx[m][0], D[m][b][0]), tot[m][b][0]);
+          tot[m][b][1] = fmaf(sl, fmaf(-cl, Dx[m][1], D[m][b][1]), tot[m][b][1]);
+          tot[m][b][2] = fmaf(sh, fmaf(-ch, Dx[m][0], D[m][b][2]), tot[m][b][2]);
+          tot[m][b][3] = fmaf(sh, fmaf(-ch, Dx[m][1], D[m][b][3]), tot[m][b][3]);
+          D[m][b][0] = D[m][b][1] = D[m][b][2] = D[m][b][3] = 0.f;
         }
       }
-    }
-  };
-
-  bool ok = true;
-  int cur_grp = -1;
-  if (nst > 0) {
-    cur_grp = static_cast<int>((w_beg * kDecStageRows) / g);
-    load_sz(static_cast<uint32_t>(cur_grp));
-  }
-
-  for (int j = 0; j < nst; ++j) {
-    const int slot = j % NS;
-    if (ok) ok = mbar_wait_bounded(&bars[slot], static_cast<uint32_t>((j / NS) & 1));
-    ok = __all_sync(0xffffffffu, ok);  // keep the warp convergent for the shuffles
-    const uint32_t xbase = smem_u32(ring + (size_t)slot * L::kSlot);
-    const uint32_t wbase = xbase + L::kXBytes;
-    const uint32_t stage = w_beg + j;
-#pragma unroll 1
-    for (int s = 0; s < 4; ++s) {
-      const uint32_t step = stage * 4 + s;
-      if (!ok || step >= steps) break;
-      const int grp = static_cast<int>((step * 16) / g);
-      if (grp != cur_grp) {
-        fold();
-        cur_grp = grp;
-        load_sz(static_cast<uint32_t>(grp));
-      }
-      // ---- weights: rows dec_row(t, i) of this step, words 2gq, 2gq+1
-      uint32_t wv[4][2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = s * 16 + dec_row(t, i);
-        const uint32_t addr = wbase + r * 64 + ((((gq >> 1) ^ ((r >> 1) & 3))) << 4) + ((gq & 1) << 3);
-        asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];"
-                     : "=r"(wv[i][0]), "=r"(wv[i][1])
-                     : "r"(addr));
-      }
-      // ---- X^T fragments for rows 8m + gq
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) Dx[m][e] = 0.f;
+    };
+
+    // one 16-row step: X fragments, the ones MMA, dequantize and multiply
+    auto step_mma = [&](const uint8_t* sbase, int s) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        wv[i] = *reinterpret_cast<const uint32_t*>(sbase + woff[i] + s * 2048);
       uint32_t bh[MT][2], bl[MT][2];
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
-        const int xr = 8 * m + gq;
-        float xv[4];
-        uint16_t raw16[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int kk = s * 16 + dec_row(t, i);
+        for (int h2 = 0; h2 < 2; ++h2) {
           if constexpr (DT == kF32) {
-            const int h = kk >> 5, kq = kk & 31;
-            const uint32_t a = xbase + h * XB * 128 + xr * 128 + (((kq >> 2) ^ (xr & 7)) << 4) + ((kq & 3) << 2);
-            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xv[i]) : "r"(a));
+            // two 32-k boxes; k = 16s + 8h2 + 2t lies in box s >> 1
+            const uint32_t ch2 = (uint32_t)(4 * (s & 1) + 2 * h2 + (t >> 1));
+            const float2 xv = *reinterpret_cast<const float2*>(
+                sbase + (s >> 1) * XB * 128 + xrow[m] + ((ch2 ^ x7[m]) << 4) + 8 * (t & 1));
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(xv.x, xv.y);
+            const __nv_bfloat162 lo =
+                __floats2bfloat162_rn(xv.x - __low2float(hi), xv.y - __high2float(hi));
+            bh[m][h2] = *reinterpret_cast<const uint32_t*>(&hi);
+            bl[m][h2] = *reinterpret_cast<const uint32_t*>(&lo);
           } else {
-            const uint32_t a = xbase + xr * 128 + (((kk >> 3) ^ (xr & 7)) << 4) + ((kk & 7) << 1);
-            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(raw16[i]) : "r"(a));
+            bh[m][h2] = *reinterpret_cast<const uint32_t*>(
+                sbase + xrow[m] + ((((uint32_t)(2 * s + h2)) ^ x7[m]) << 4) + 4 * t);
           }
         }
-        if constexpr (DT == kF32) {
-          float hs = 0.f;
-#pragma unroll
-          for (int pr = 0; pr < 2; ++pr) {
-            const __nv_bfloat162 hi = __floats2bfloat162_rn(xv[2 * pr], xv[2 * pr + 1]);
-            const float h0 = __low2float(hi), h1 = __high2float(hi);
-            const __nv_bfloat162 lo = __floats2bfloat162_rn(xv[2 * pr] - h0, xv[2 * pr + 1] - h1);
-            bh[m][pr] = *reinterpret_cast<const uint32_t*>(&hi);
-            bl[m][pr] = *reinterpret_cast<const uint32_t*>(&lo);
-            hs += (h0 + __low2float(lo)) + (h1 + __high2float(lo));
-          }
-          xacc[m] += hs;
-        } else {
-          bh[m][0] = static_cast<uint32_t>(raw16[0]) | (static_cast<uint32_t>(raw16[1]) << 16);
-          bh[m][1] = static_cast<uint32_t>(raw16[2]) | (static_cast<uint32_t>(raw16[3]) << 16);
-          float hs = 0.f;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if constexpr (DT == kF16) {
-              hs += __half2float(__ushort_as_half(raw16[i]));
-            } else {
-              hs += __bfloat162float(__ushort_as_bfloat16(raw16[i]));
-            }
-          }
-          xacc[m] += hs;
-        }
+        mma_16816<!kF16Mma>(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1]);
+        if constexpr (DT == kF32)
+          mma_16816<true>(Dx[m], kOnes, kOnes, kOnes, kOnes, bl[m][0], bl[m][1]);
       }
-      // ---- dequantize into A fragments and multiply
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t p01 = prmt(wv[0][u], wv[1][u], dec_sel(b));
-          const uint32_t p23 = prmt(wv[2][u], wv[3][u], dec_sel(b));
-          uint32_t a0, a1, a2, a3;
-          if constexpr (kF16Mma) {
-            a0 = lop3_and_or(p01, 0x000F000Fu, 0x64006400u);
-            a1 = lop3_and_or(p01, 0x00F000F0u, 0x64006400u);
-            a2 = lop3_and_or(p23, 0x000F000Fu, 0x64006400u);
-            a3 = lop3_and_or(p23, 0x00F000F0u, 0x64006400u);
-          } else {
-            a0 = lop3_and_or(p01, 0x000F000Fu, 0x43004300u);
-            a1 = lop3_and_or(p01 >> 4, 0x000F000Fu, 0x43004300u);
-            a2 = lop3_and_or(p23, 0x000F000Fu, 0x43004300u);
-            a3 = lop3_and_or(p23 >> 4, 0x000F000Fu, 0x43004300u);
-          }
-#pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            mma_16816<!kF16Mma>(D[m][u * 4 + b], a0, a1, a2, a3, bh[m][0], bh[m][1]);
-            if constexpr (DT == kF32) {
-              mma_16816<true>(D[m][u * 4 + b], a0, a1, a2, a3, bl[m][0], bl[m][1]);
-            }
-          }
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0 && ok && j + NS < nst) {
-      fence_proxy_async_smem();
-      issue(j + NS);
-    }
-    __syncwarp();
-  }
-  if (cur_grp >= 0) fold();
-
-  // ---- reduction: warps of this CTA, then the CTAs of the cluster
-  __syncthreads();
-  float* red = reinterpret_cast<float*>(smem);  // [nwarps][XB][128], reuses the ring
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const int j = u * 4 + b;
-        const int cl = (2 * gq + u) * 8 + col_of_nibble(2 * b, ORDER);
-        const int ch = (2 * gq + u) * 8 + col_of_nibble(2 * b + 1, ORDER);
-        float* r0 = red + ((size_t)warp * XB + 8 * m + 2 * t) * kDecTileCols;
+        const uint32_t p01 = prmt(wv[0], wv[1], dec_sel(b));
+        const uint32_t p23 = prmt(wv[2], wv[3], dec_sel(b));
+        uint32_t a0, a1, a2, a3;
+        if constexpr (kF16Mma) {
+          a0 = lop3_and_or(p01, 0x000F000Fu, 0x64006400u);
+          a1 = lop3_and_or(p01, 0x00F000F0u, 0x64006400u);
+          a2 = lop3_and_or(p23, 0x000F000Fu, 0x64006400u);
+          a3 = lop3_and_or(p23, 0x00F000F0u, 0x64006400u);
+        } else {
+          a0 = lop3_and_or(p01, 0x000F000Fu, 0x43004300u);
+          a1 = lop3_and_or(p01 >> 4, 0x000F000Fu, 0x43004300u);
+          a2 = lop3_and_or(p23, 0x000F000Fu, 0x43004300u);
+          a3 = lop3_and_or(p23 >> 4, 0x000F000Fu, 0x43004300u);
+        }
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          mma_16816<!kF16Mma>(D[m][b], a0, a1, a2, a3, bh[m][0], bh[m][1]);
+          if constexpr (DT == kF32) mma_16816<true>(D[m][b], a0, a1, a2, a3, bl[m][0], bl[m][1]);
+        }
+      }
+    };
+
+    int sl = 0;
+    uint32_t par = 0;
+    if constexpr (GA) {
+      // g is a multiple of 64: groups end on stage boundaries, so the four
+      // steps of a stage run without any branch and the fold (if any) follows.
+      const uint32_t spgs = g / kDecStageRows;  // stages per group
+      uint32_t in_grp = c_beg % spgs;           // stage index inside its group
+      for (int j = 0; j < nst; ++j) {
+        if (ok) ok = mbar_wait_bounded(&full[sl], par);
+        ok = __all_sync(0xffffffffu, ok);  // keep the warp convergent
+        if (!ok) break;
+        const uint8_t* sbase = smem + sl * slot;
+#pragma unroll
+        for (int st = 0; st < 4; ++st) step_mma(sbase, st);
+        if (++in_grp == spgs || j + 1 == nst) {
+          fold(sbase + L::s_off(strips), sbase + L::z_off(strips, g));
+          in_grp = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);
+        if (++sl == NS) {
+          sl = 0;
+          par ^= 1u;
+        }
+      }
+    } else {
+      // any g % 16 == 0: group boundaries tracked per step, without division
+      const uint32_t spg = g >> 4;  // 16-row steps per quantization group
+      uint32_t grp = (c_beg * 4) / spg;
+      uint32_t grp_end = (grp + 1) * spg;  // first step of the next group
+      for (int j = 0; j < nst; ++j) {
+        if (ok) ok = mbar_wait_bounded(&full[sl], par);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const uint8_t* sbase = smem + sl * slot;
+        const uint32_t stage = c_beg + j;
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          const uint32_t step = stage * 4 + st;
+          if (step >= end_step) break;
+          step_mma(sbase, st);
+          const uint32_t next = step + 1;
+          if (next >= end_step || next >= grp_end) {
+            const uint32_t r = grp - stage * kDecStageRows / g;  // scale row in this stage
+            fold(sbase + L::s_off(strips) + r * L::s_row_bytes(strips),
+                 sbase + L::z_off(strips, g) + r * L::z_row_bytes(strips));
+            grp += 1;
+            grp_end += spg;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);
+        if (++sl == NS) {
+          sl = 0;
+          par ^= 1u;
+        }
+      }
+    }
+  }
+
+  // ---- reduction over the CTAs of the cluster (each warp owns its columns)
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(smem);  // [strips][XB][128], reuses the ring
+  if (warp < consumers) {
+    float* base = red + ((size_t)strip * XB) * kDecTileCols;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int cl = word * 8 + col_of_nibble(2 * b, ORDER);
+        const int ch = word * 8 + col_of_nibble(2 * b + 1, ORDER);
+        float* r0 = base + (size_t)(8 * m + 2 * t) * kDecTileCols;
         float* r1 = r0 + kDecTileCols;
-        r0[cl] = tot[m][j][0];
-        r1[cl] = tot[m][j][1];
-        r0[ch] = tot[m][j][2];
-        r1[ch] = tot[m][j][3];
+        r0[cl] = tot[m][b][0];
+        r1[cl] = tot[m][b][1];
+        r0[ch] = tot[m][b][2];
+        r1[ch] = tot[m][b][3];
       }
     }
   }
   __syncthreads();
   const int rows_eff = static_cast<int>(rows < (uint32_t)XB ? rows : (uint32_t)XB);
-  for (int idx = threadIdx.x; idx < rows_eff * kDecTileCols; idx += blockDim.x) {
-    const int b = idx / kDecTileCols, c = idx % kDecTileCols;
-    float v = 0.f;
-    for (int w = 0; w < nwarps; ++w) v += red[((size_t)w * XB + b) * kDecTileCols + c];
-    red[(size_t)b * kDecTileCols + c] = v;
-  }
+  const int bcols = strips * kDecTileCols;
   if (split > 1) {
     cluster_sync_all();
   } else {
     __syncthreads();
   }
-  const int cbeg = static_cast<int>(kDecTileCols * rank / split);
-  const int cend = static_cast<int>(kDecTileCols * (rank + 1) / split);
+  const int cbeg = static_cast<int>((uint32_t)bcols * rank / split);
+  const int cend = static_cast<int>((uint32_t)bcols * (rank + 1) / split);
   const int ncols = cend - cbeg;
   for (int idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
     const int b = idx / ncols, c = cbeg + idx % ncols;
-    const uint32_t col = p0 * 8 + c;
+    const uint32_t col = pband * 8 + c;
+    const float* rp =
+        red + ((size_t)(c / kDecTileCols) * XB + b) * kDecTileCols + (c % kDecTileCols);
     float v = 0.f;
     if (split > 1) {
-      const uint32_t a = smem_u32(red + (size_t)b * kDecTileCols + c);
-      for (uint32_t q = 0; q < split; ++q) v += ld_shared_cluster_f32(map_shared_rank(a, q));
+      // every remote load first, then the sum in a fixed order
+      const uint32_t a = smem_u32(rp);
+      float part[16];
+#pragma unroll
+      for (uint32_t q = 0; q < 16; ++q)
+        part[q] = q < split ? ld_shared_cluster_f32(map_shared_rank(a, q)) : 0.f;
+#pragma unroll
+      for (uint32_t q = 0; q < 16; ++q) v += part[q];
     } else {
-      v = red[(size_t)b * kDecTileCols + c];
+      v = *rp;
     }
     if (col < n) {
       if (bias) v += DType<DT>::to_f32(bias[col]);
@@ -413,38 +509,44 @@ static bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base
 
 static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 
+static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
+  const uint32_t g = static_cast<uint32_t>(p.g);
+  const bool mt1 = decode_mt(p.rows) == 1;
+  if (p.dtype == kF32) {
+    return mt1 ? DecodeLayout<kF32, 1>::smem_bytes(plan.warps, plan.stages, g)
+               : DecodeLayout<kF32, 2>::smem_bytes(plan.warps, plan.stages, g);
+  }
+  return mt1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages, g)
+             : DecodeLayout<kF16, 2>::smem_bytes(plan.warps, plan.stages, g);
+}
+
 bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
   if (p.rows == 0 || p.rows > 16) return false;
   if (p.k % 16 != 0 || p.g % 16 != 0 || p.k % p.g != 0 || p.n % 32 != 0) return false;
   if (p.k >= (1ull << 31) || p.n >= (1ull << 31) || p.ld_out >= (1ull << 31)) return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
-  if (ax % 16 || aw % 16 || az % 8 || as % 16) return false;
+  if (ax % 16 || aw % 16 || az % 16 || as % 16) return false;
   if (plan.split < 1 || plan.split > 16 || (plan.split & (plan.split - 1))) return false;
-  if (plan.warps < 1 || plan.warps > kDecMaxWarps) return false;
+  if (plan.tile_n > 1) return false;
+  if (plan.warps < 2 || (plan.warps & 1) || 2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
+    return false;
   if (plan.stages < 1 || plan.stages > kDecMaxStages) return false;
-  const size_t tiles = (p.n + kDecTileCols - 1) / kDecTileCols;
-  if (tiles * plan.split >= (1ull << 31)) return false;
-  size_t smem = 0;
-  if (p.dtype == kF32) {
-    smem = decode_mt(p.rows) == 1 ? DecodeLayout<kF32, 1>::smem_bytes(plan.warps, plan.stages)
-                                  : DecodeLayout<kF32, 2>::smem_bytes(plan.warps, plan.stages);
-  } else {
-    smem = decode_mt(p.rows) == 1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages)
-                                  : DecodeLayout<kF16, 2>::smem_bytes(plan.warps, plan.stages);
-  }
-  return smem <= dev.smem_optin && dev.cc_major == 10;
+  const size_t bands =
+      (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps);
+  if (bands * plan.split >= (1ull << 31)) return false;
+  return decode_smem(p, plan) <= dev.smem_optin && dev.cc_major == 10;
 }
 
-template <int DT, int ODT, int ORDER, int MT>
+template <int DT, int ODT, int ORDER, int MT, bool GA>
 static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
   using OT = typename DType<ODT>::T;
   CUtensorMap tm_w, tm_x;
   const uint64_t npk = p.n / 8;
-  if (!encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kDecTileWords,
-                 kDecStageRows, CU_TENSOR_MAP_SWIZZLE_64B)) {
+  if (!encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kDecBoxWords,
+                 kDecStageRows, CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
   const CUtensorMapDataType xdt = DT == kF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -455,42 +557,66 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                  CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = decode_kernel<DT, ODT, ORDER, MT>;
-  const size_t smem = L::smem_bytes(plan.warps, plan.stages);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  if (plan.split > 8) {
+  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA>;
+  const size_t smem = decode_smem(p, plan);
+  // function attributes are per process; set each once (a repeat is harmless)
+  static size_t smem_set = 0;
+  static bool nonportable_set = false;
+  cudaError_t e;
+  if (smem > smem_set) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    smem_set = smem;
+  }
+  if (plan.split > 8 && !nonportable_set) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
+    nonportable_set = true;
   }
-  const uint32_t tiles = static_cast<uint32_t>((p.n + kDecTileCols - 1) / kDecTileCols);
+  const uint32_t bands = static_cast<uint32_t>(
+      (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles * plan.split);
-  cfg.blockDim = dim3(plan.warps * 32);
+  cfg.gridDim = dim3(bands * plan.split);
+  cfg.blockDim = dim3((2 * plan.warps + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = p.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  int na = 0;
   if (plan.split > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = plan.split;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = plan.split;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
+  // Let this kernel's prologue (barrier set-up, weight loads) overlap the
+  // tail of the previous kernel in the stream; X is read only after
+  // griddepcontrol.wait. plan.reserved[0] = 1 launches without the overlap.
+  if (plan.reserved[0] == 0) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kern, tm_w, tm_x, p.qz, static_cast<const T*>(p.sc),
                             static_cast<const T*>(p.bias), static_cast<OT*>(p.out),
                             static_cast<uint32_t>(p.rows), static_cast<uint32_t>(p.k),
                             static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g),
                             static_cast<uint32_t>(p.ld_out), static_cast<uint32_t>(plan.split),
-                            static_cast<uint32_t>(plan.stages));
+                            static_cast<uint32_t>(plan.stages), static_cast<uint32_t>(plan.warps));
 }
 
 template <int DT, int ODT, int ORDER>
 static cudaError_t launch_decode_m(const GemmProblem& p, const cawq_plan& plan) {
-  return decode_mt(p.rows) == 1 ? launch_decode_t<DT, ODT, ORDER, 1>(p, plan)
-                                : launch_decode_t<DT, ODT, ORDER, 2>(p, plan);
+  const bool ga = p.g % kDecStageRows == 0;  // groups end on stage boundaries
+  if (decode_mt(p.rows) == 1) {
+    return ga ? launch_decode_t<DT, ODT, ORDER, 1, true>(p, plan)
+              : launch_decode_t<DT, ODT, ORDER, 1, false>(p, plan);
+  }
+  return ga ? launch_decode_t<DT, ODT, ORDER, 2, true>(p, plan)
+            : launch_decode_t<DT, ODT, ORDER, 2, false>(p, plan);
 }
 
 template <int DT, int ODT>
@@ -509,34 +635,39 @@ cudaError_t launch_decode(const GemmProblem& p, const cawq_plan& plan, const Dev
                              : launch_decode_o<kBF16, kBF16>(p, plan);
 }
 
+// plan.warps = 128-column strips per CTA (two consumer warps each),
+// plan.split = CTAs of a cluster splitting K, plan.stages = depth of the TMA ring.
 cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   cawq_plan plan = {};
   plan.path = CAWQ_PATH_DECODE;
-  plan.warps = 8;
-  plan.stages = 2;
-  const size_t tiles = (p.n + kDecTileCols - 1) / kDecTileCols;
+  plan.warps = 4;
+  const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
+  const size_t strips_total = (p.n + kDecTileCols - 1) / kDecTileCols;
+  while (plan.warps > 2 && strips_total < (size_t)plan.warps * 8) plan.warps /= 2;
+  const size_t bands = (strips_total + plan.warps - 1) / plan.warps;
   const size_t nst_total = (p.k / 16 + 3) / 4;
-  const size_t target = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148) * 2;
   int split = 1;
-  while (split < 16 && tiles * split < target && nst_total >= (size_t)split * 2 * plan.warps) split *= 2;
-  while (plan.warps > 4 && nst_total < (size_t)split * plan.warps) plan.warps /= 2;
+  while (split < 16 && bands * split < sms && nst_total >= (size_t)split * 4) split *= 2;
   plan.split = split;
+  const size_t per_cta = (nst_total + split - 1) / split;
+  plan.stages = per_cta >= 4 ? 4 : (per_cta >= 2 ? 2 : 1);
+  while (plan.stages > 1 && !decode_supports(p, plan, dev)) --plan.stages;
   return plan;
 }
 
 void decode_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
                        int max_count) {
   int c = 0;
-  for (int split = 1; split <= 16; split *= 2) {
-    for (int warps = 4; warps <= 8; warps *= 2) {
-      for (int stages = 2; stages <= 4; stages *= 2) {
+  const size_t nst_total = (p.k / 16 + 3) / 4;
+  for (int split = 2; split <= 16; split *= 2) {
+    if (nst_total < (size_t)split) break;
+    for (int warps : {2, 4, 6, 8}) {
+      for (int stages : {2, 3, 4, 6}) {
         cawq_plan pl = {};
         pl.path = CAWQ_PATH_DECODE;
         pl.split = split;
         pl.warps = warps;
         pl.stages = stages;
-        const size_t nst_total = (p.k / 16 + 3) / 4;
-        if (nst_total < (size_t)split * warps) continue;  // idle warps
         if (!decode_supports(p, pl, dev)) continue;
         if (c < max_count) out[c++] = pl;
       }

@@ -8,7 +8,7 @@
 
 #include <string>
 
-#include "../../include/cube_awq.h"
+#include "cube_awq.h"
 
 namespace cawq {
 

@@ -1,24 +1,460 @@
 // cawq_prefill.cuh — large-M fused AWQ GEMM on tcgen05 tensor cores (sm_100a).
+//
+// Y[M, N] = X[M, K] · ((Q - Z) · S)[K, N] for f16 / bf16 activations.
+// Replaces gemm_awq (src/kernel/awq_kernel_gemm.rs:181-439), the reference's
+// M > 8 kernel, which computes on CUDA cores with scalar FMA.
+//
+// One CTA computes a 128 x 256 output tile; K advances in 64-row stages
+// through a 3-deep shared-memory ring. Warp roles (320 threads):
+//   warp 0     TMA producer: X tile (128 x 64, 128B swizzle, K-major), the
+//              packed weight tile (64 x 32 words, 128B swizzle), and the
+//              scale and zero rows of the stage's group, on one mbarrier.
+//   warp 1     allocates 256 TMEM columns; one thread issues
+//              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x 4
+//              per stage and commits each stage back to the producer.
+//   warps 2-9  dequantize the packed stage into the B operand: per packed
+//              word, lop3 makes (1024 + q) f16 pairs of adjacent columns,
+//              then (q - z) * s is formed in F exactly as the reference does
+//              (one rounding), and 16 bytes land in the canonical MN-major
+//              128B-swizzled layout. After the last stage they read the fp32
+//              accumulator from TMEM (tcgen05.ld), add bias and store.
+//
+// The weights therefore enter the MMA bit-identical to the reference's
+// dequantized values; the products are exact and the sum is fp32.
 #pragma once
 
 #include "cawq_common.cuh"
 
 namespace cawq {
 
-bool prefill_supports(const GemmProblem&, const cawq_plan&, const DeviceInfo&) { return false; }
+constexpr int kPfBM = 128;
+constexpr int kPfBN = 256;
+constexpr int kPfBK = 64;
+constexpr int kPfStages = 3;
+constexpr int kPfDqWarps = 8;                       // dequant / epilogue warps
+constexpr int kPfThreads = 64 + 32 * kPfDqWarps;    // + producer + MMA warp
 
-cudaError_t launch_prefill(const GemmProblem&, const cawq_plan&, const DeviceInfo&) {
+struct PrefillLayout {
+  static constexpr int kX = kPfBM * kPfBK * 2;      // 16384
+  static constexpr int kB = kPfBK * kPfBN * 2;      // 32768
+  static constexpr int kW = kPfBK * kPfBN / 8 * 4;  // 8192
+  static constexpr int kS = kPfBN * 2;              // 512
+  static constexpr int kZ = kPfBN / 8 * 4;          // 128
+  static constexpr int kStage = ((kX + kB + kW + kS + kZ) + 1023) / 1024 * 1024;
+  static constexpr int kBars = 1024;  // barriers + TMEM slot
+  static constexpr size_t kSmem = 1024 + (size_t)kStage * kPfStages + kBars;
+};
+
+// ------------------------------------------------------- tcgen05 helpers
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, A K-major, B MN-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int m, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (0u << 15) |
+         (1u << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int DT>
+struct PfHalf2;
+template <>
+struct PfHalf2<kF16> {
+  static constexpr uint32_t kMagic = 0x64006400u;  // f16 1024
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+};
+template <>
+struct PfHalf2<kBF16> {
+  static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+};
+
+// Four (1024 + nibble) pairs of adjacent logical columns of one packed word.
+template <int DT, int ORDER>
+__device__ __forceinline__ void pf_pairs(uint32_t q, uint32_t (&t)[4]) {
+  constexpr uint32_t M = PfHalf2<DT>::kMagic;
+  if constexpr (ORDER == kOrderAwq) {
+    // logical (2i, 2i+1) live in nibbles (i, i+4)
+    t[0] = lop3_and_or(q, 0x000F000Fu, M);
+    t[1] = lop3_and_or(q >> 4, 0x000F000Fu, M);
+    t[2] = lop3_and_or(q >> 8, 0x000F000Fu, M);
+    t[3] = lop3_and_or(q >> 12, 0x000F000Fu, M);
+  } else {
+    // logical (2i, 2i+1) live in nibbles (2i, 2i+1) = both halves of byte i
+    const uint32_t q4 = q >> 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t sel = (uint32_t)(i | (i << 4) | ((4 + i) << 8) | ((4 + i) << 12));
+      t[i] = lop3_and_or(prmt(q, q4, sel), 0x000F000Fu, M);
+    }
+  }
+}
+
+template <int DT, int ODT, int ORDER>
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
+                   const typename DType<DT>::T* __restrict__ bias,
+                   typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
+                   uint32_t g, uint32_t ld_out) {
+  using L = PrefillLayout;
+  using H = PfHalf2<DT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)L::kStage * kPfStages);
+  uint64_t* bready = full + kPfStages;
+  uint64_t* empty = bready + kPfStages;
+  uint64_t* acc_full = empty + kPfStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t n0 = blockIdx.x * kPfBN;
+  const uint32_t m0 = blockIdx.y * kPfBM;
+  const int KT = static_cast<int>(k / kPfBK);
+
+  auto stage_base = [&](int s) { return smem + (size_t)s * L::kStage; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 32 * kPfDqWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kPfBN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int s = kt % kPfStages, u = kt / kPfStages;
+        if (u > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((u - 1) & 1));
+        if (!ok) break;
+        uint8_t* b = stage_base(s);
+        const int grp = static_cast<int>((uint32_t)kt * kPfBK / g);
+        mbar_arrive_expect_tx(&full[s], L::kX + L::kW + L::kS + L::kZ);
+        tma_load_2d(b, &tm_x, kt * kPfBK, static_cast<int>(m0), &full[s]);
+        tma_load_2d(b + L::kX + L::kB, &tm_w, static_cast<int>(n0 / 8), kt * kPfBK, &full[s]);
+        tma_load_2d(b + L::kX + L::kB + L::kW, &tm_s, static_cast<int>(n0), grp, &full[s]);
+        tma_load_2d(b + L::kX + L::kB + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp,
+                    &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, kPfBM, kPfBN);
+      bool ok = true;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int s = kt % kPfStages, u = kt / kPfStages;
+        ok = mbar_wait_bounded(&full[s], (uint32_t)(u & 1)) &&
+             mbar_wait_bounded(&bready[s], (uint32_t)(u & 1));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t xa = smem_u32(stage_base(s));
+        const uint32_t ba = xa + L::kX;
+#pragma unroll
+        for (int j = 0; j < kPfBK / 16; ++j) {
+          const uint64_t ad = umma_desc_sw128(xa + 32 * j, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(ba + 2048 * j, 8192, 1024);
+          umma_f16(tmem, ad, bd, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------- dequant, then epilogue
+    const int dw = warp - 2;   // 0..7
+    const int q4 = lane >> 3;  // quarter of the warp -> row offset 2*q4
+    const int l = lane & 7;    // packed word l + 8a, a = 0..3
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kPfStages, u = kt / kPfStages;
+      if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)(u & 1));
+      if (ok && u > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((u - 1) & 1));
+      if (ok) {
+        uint8_t* b = stage_base(s);
+        uint8_t* bsm = b + L::kX;
+        const uint8_t* wsm = b + L::kX + L::kB;
+        const uint8_t* srow = b + L::kX + L::kB + L::kW;
+        const uint32_t* zrow = reinterpret_cast<const uint32_t*>(srow + L::kS);
+        uint32_t sp[4][4], zp[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const int w = l + 8 * a;
+          const uint4 sv = *reinterpret_cast<const uint4*>(srow + w * 16);
+          sp[a][0] = sv.x; sp[a][1] = sv.y; sp[a][2] = sv.z; sp[a][3] = sv.w;
+          pf_pairs<DT, ORDER>(zrow[w], zp[a]);
+        }
+        // 16 row sets of 4 rows (8-row atom x parity); each warp takes 2
+#pragma unroll
+        for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
+          const int sidx = kPfDqWarps * pass + dw;
+          const int row = (sidx >> 1) * 8 + (sidx & 1) + 2 * q4;  // 0..63
+          const int r8 = row & 7;
+          uint32_t qv[4];
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            const int w = l + 8 * a;
+            qv[a] = *reinterpret_cast<const uint32_t*>(wsm + row * 128 + (((w >> 2) ^ r8) << 4) +
+                                                       ((w & 3) << 2));
+          }
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            uint32_t t[4];
+            pf_pairs<DT, ORDER>(qv[a], t);
+            uint4 v;
+            v.x = H::mul(H::sub(t[0], zp[a][0]), sp[a][0]);
+            v.y = H::mul(H::sub(t[1], zp[a][1]), sp[a][1]);
+            v.z = H::mul(H::sub(t[2], zp[a][2]), sp[a][2]);
+            v.w = H::mul(H::sub(t[3], zp[a][3]), sp[a][3]);
+            *reinterpret_cast<uint4*>(bsm + a * 8192 + (row >> 3) * 1024 + r8 * 128 +
+                                      ((l ^ r8) << 4)) = v;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bready[s]);
+    }
+    // ---- epilogue: TMEM -> registers -> global
+    if (ok) ok = mbar_wait_bounded(acc_full, 0u);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+    tc_fence_after();
+    const int lq = warp & 3;      // TMEM lane quarter this warp may access
+    const int half = dw >> 2;     // which 128 of the 256 columns
+    const uint32_t row = m0 + 32 * lq + lane;
+    if (ok) {
+#pragma unroll 1
+      for (int c = half * 4; c < half * 4 + 4; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + 32 * c, v);
+        const uint32_t col0 = n0 + 32 * c;
+        if (row < rows && col0 < n) {
+          if (bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += DType<DT>::to_f32(bias[col0 + i]);
+          }
+          typename DType<ODT>::T* o = out + (size_t)row * ld_out + col0;
+          if constexpr (ODT == kF32) {
+            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = v[i];
+            }
+          } else {
+            using OT = typename DType<ODT>::T;
+            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 pk;
+                OT* h = reinterpret_cast<OT*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) h[e] = DType<ODT>::from_f32(v[i + e]);
+                *reinterpret_cast<uint4*>(o + i) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = DType<ODT>::from_f32(v[i]);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPfBN);
+  }
+}
+
+// ------------------------------------------------------------------ host
+static bool pf_encode(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                      uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  const uint32_t estr[2] = {1, 1};
+  return fn(map, static_cast<int>(dt), 2, const_cast<void*>(base), dims, strides, box, estr,
+            static_cast<int>(CU_TENSOR_MAP_INTERLEAVE_NONE), static_cast<int>(swz),
+            static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B),
+            static_cast<int>(CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)) == 0;
+}
+
+bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
+  (void)plan;
+  if (dev.cc_major != 10 || dev.smem_optin < PrefillLayout::kSmem) return false;
+  if (p.dtype != kF16 && p.dtype != kBF16) return false;
+  if (p.rows == 0 || p.k % kPfBK != 0 || p.g % kPfBK != 0 || p.k % p.g != 0 || p.n % 32 != 0)
+    return false;
+  if (p.k >= (1ull << 31) || p.n >= (1ull << 31) || p.rows >= (1ull << 31) ||
+      p.ld_out >= (1ull << 31))
+    return false;
+  if ((p.rows + kPfBM - 1) / kPfBM > 65535) return false;
+  const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
+  const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
+  return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
+}
+
+template <int DT, int ODT, int ORDER>
+static cudaError_t launch_prefill_t(const GemmProblem& p) {
+  using T = typename DType<DT>::T;
+  using OT = typename DType<ODT>::T;
+  const CUtensorMapDataType xdt =
+      DT == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tx, tw, ts, tz;
+  const uint64_t npk = p.n / 8, groups = p.k / p.g;
+  if (!pf_encode(&tx, xdt, p.x, p.k, p.rows, p.k * 2, kPfBK, kPfBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !pf_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kPfBN / 8, kPfBK,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !pf_encode(&ts, xdt, p.sc, p.n, groups, p.n * 2, kPfBN, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !pf_encode(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qz, npk, groups, npk * 4, kPfBN / 8, 1,
+                 CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return cudaErrorInvalidValue;
+  }
+  auto kern = prefill_kernel<DT, ODT, ORDER>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(PrefillLayout::kSmem));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  dim3 grid(static_cast<uint32_t>((p.n + kPfBN - 1) / kPfBN),
+            static_cast<uint32_t>((p.rows + kPfBM - 1) / kPfBM));
+  kern<<<grid, kPfThreads, PrefillLayout::kSmem, p.stream>>>(
+      tx, tw, ts, tz, static_cast<const T*>(p.bias), static_cast<OT*>(p.out),
+      static_cast<uint32_t>(p.rows), static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n),
+      static_cast<uint32_t>(p.g), static_cast<uint32_t>(p.ld_out));
+  return cudaGetLastError();
+}
+
+template <int DT, int ODT>
+static cudaError_t launch_prefill_o(const GemmProblem& p) {
+  return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural>(p)
+                                  : launch_prefill_t<DT, ODT, kOrderAwq>(p);
+}
+
+cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan&, const DeviceInfo&) {
+  if (p.dtype == kF16) {
+    return p.out_dtype == kF32 ? launch_prefill_o<kF16, kF32>(p) : launch_prefill_o<kF16, kF16>(p);
+  }
+  if (p.dtype == kBF16) {
+    return p.out_dtype == kF32 ? launch_prefill_o<kBF16, kF32>(p)
+                               : launch_prefill_o<kBF16, kBF16>(p);
+  }
   return cudaErrorNotSupported;
 }
 
 cawq_plan prefill_default_plan(const GemmProblem&, const DeviceInfo&) {
   cawq_plan pl = {};
   pl.path = CAWQ_PATH_PREFILL;
+  pl.tile_n = kPfBN;
+  pl.stages = kPfStages;
   return pl;
 }
 
-void prefill_candidates(const GemmProblem&, const DeviceInfo&, cawq_plan*, int* count, int) {
-  *count = 0;
+void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
+                        int max_count) {
+  int c = 0;
+  cawq_plan pl = prefill_default_plan(p, dev);
+  if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
+  *count = c;
 }
 
 }  // namespace cawq

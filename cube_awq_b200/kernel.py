@@ -255,6 +255,7 @@ def _plan_c(plan: dict) -> _lib.PlanC:
     p.warps = int(plan.get("warps", 0))
     p.tile_n = int(plan.get("tile_n", 0))
     p.stages = int(plan.get("stages", 0))
+    p.reserved[0] = 0 if plan.get("pdl", True) else 1
     return p
 
 

@@ -103,10 +103,12 @@ typedef struct cawq_gemm_args {
 typedef struct cawq_plan {
   int path;      /* cawq_path                                            */
   int split;     /* decode: CTAs per cluster splitting K (1..16)         */
-  int warps;     /* decode: warps per CTA                                */
-  int tile_n;    /* prefill: CTA tile N (64..256)                        */
+  int warps;     /* decode: 128-column strips per CTA (even, 2..8)      */
+  int tile_n;    /* prefill: CTA tile N; decode: 0                       */
   int stages;    /* pipeline stages                                      */
-  int reserved[3];
+  int reserved[3]; /* reserved[0] = 1: launch without programmatic
+                      dependent launch (no overlap with the previous
+                      kernel of the stream); others must be 0          */
 } cawq_plan;
 
 /* ----------------------------------------------------------------------- */
@@ -181,8 +183,10 @@ cawq_status cawq_awq_gemm_linear(const cawq_gemm_args* args,
  * order (CAWQ_ORDER_AWQ as gemm_awq; CAWQ_ORDER_NATURAL gives the fused form
  * of AWQLinear::forward, awq_dequantize.rs:74-108). `ld_out` is the row
  * stride of out in elements (0 = N), so a column shard can write into its
- * slice of a wider output. Module rules apply (awq_gemm.rs:77-95, and the
- * kernel rules of awq_kernel_gemm.rs:89-158 with the module's tiles).
+ * slice of a wider output. The rules of the module that owns each order
+ * apply: CAWQ_ORDER_AWQ follows AWQGEMMLinear (awq_gemm.rs:77-95 plus the
+ * kernel rules of awq_kernel_gemm.rs:89-158 with the module's tiles);
+ * CAWQ_ORDER_NATURAL follows AWQLinear (awq_dequantize.rs:25-28).
  */
 cawq_status cawq_gemm(const void* x, const uint32_t* qweight,
                       const uint32_t* qzeros, const void* scales,

@@ -20,7 +20,7 @@ from helpers import (GEMM_TOL, as_f64, kat_expected, load_json, load_npz, max_re
 pytestmark = pytest.mark.gpu
 
 KATS = load_json("kat_gemm_uniform.json")
-PATH_DECODE, PATH_GENERIC = 1, 3
+PATH_DECODE, PATH_PREFILL, PATH_GENERIC = 1, 2, 3
 
 
 def _harness_shape(kat):
@@ -92,7 +92,8 @@ def _run(cuda_device, dtype, rows, k, n, g, plan=None, bias=False, order="awq", 
 
 
 DECODE_SHAPES = [(128, 256, 32), (512, 384, 64), (1024, 4096, 128), (4096, 4160, 128),
-                 (11008, 512, 128), (3584, 4608, 64)]
+                 (11008, 512, 128), (3584, 4608, 64), (1024, 256, 16), (960, 384, 48),
+                 (1280, 512, 80)]
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -104,13 +105,41 @@ def test_decode_default_plan_parity(cuda_device, dtype, rows, k, n, g):
 
 
 @pytest.mark.parametrize("split", [1, 2, 4, 8, 16])
-@pytest.mark.parametrize("warps", [4, 8])
-@pytest.mark.parametrize("stages", [2, 4])
-@pytest.mark.parametrize("dtype", ["f32", "f16"])
-def test_decode_every_plan(cuda_device, split, warps, stages, dtype):
+@pytest.mark.parametrize("warps", [2, 4, 6, 8])
+@pytest.mark.parametrize("stages", [1, 2, 3, 4])
+@pytest.mark.parametrize("rows,dtype", [(3, "f32"), (3, "f16"), (11, "f16")])
+def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype):
+    # warps = 128-column strips per CTA (two consumer warps each), split = CTAs
+    # of a cluster along K; N = 1184 leaves the last band of every strip count
+    # partly out of range
+    if rows > 8 and 2 * warps > 8:
+        pytest.skip("more warps than a 16-row tile allows")
     plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages}
-    got, ref, _ = _run(cuda_device, dtype, 3, 2048, 1024, 128, plan=plan)
+    got, ref, _ = _run(cuda_device, dtype, rows, 2048, 1184, 128, plan=plan)
     assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("pdl", [True, False])
+@pytest.mark.parametrize("rows", [1, 12])
+def test_decode_chain_with_and_without_programmatic_launch(cuda_device, pdl, rows):
+    # Two dependent GEMMs back to back on one stream: the second reads the
+    # first one's output as X (programmatic dependent launch must wait for it).
+    k, n, g = 2048, 2048, 128
+    x, qw, qz, s, _ = random_awq(k, n, g, "f16", rows, seed=21)
+    _, qw2, qz2, s2, _ = random_awq(n, k, g, "f16", rows, seed=22)
+    plan = {"path": PATH_DECODE, "split": 4, "warps": 4, "stages": 2, "pdl": pdl}
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    y1 = torch.empty(rows, n, dtype=torch.float16, device=cuda_device)
+    y2 = torch.empty(rows, k, dtype=torch.float16, device=cuda_device)
+    for _ in range(3):
+        cawq.gemm(t(x, "f16"), t(qw, "u32"), t(qz, "u32"), t(s, "f16"), g, out=y1, plan=plan)
+        cawq.gemm(y1, t(qw2, "u32"), t(qz2, "u32"), t(s2, "f16"), g, out=y2, plan=plan)
+    torch.cuda.synchronize()
+    y1n = y1.cpu().numpy()
+    ref1 = oracle.gemm_f64(x, qw, qz, s, g, dtype="f16", deq_round=False)
+    assert max_rel_err(y1n.astype(np.float64), ref1) <= GEMM_TOL["f16"]
+    ref2 = oracle.gemm_f64(y1n, qw2, qz2, s2, g, dtype="f16", deq_round=False)
+    assert max_rel_err(y2.float().cpu().numpy(), ref2) <= GEMM_TOL["f16"]
 
 
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
@@ -158,3 +187,62 @@ def test_f16_distance_to_reference_numerics_is_reported(cuda_device):
     got, ref, (x, qw, qz, s, _) = _run(cuda_device, "f16", 1, 4096, 1024, 128, seed=3)
     ref16 = oracle.gemm_ref(x, qw, qz, s, 128, dtype="f16").astype(np.float64)
     assert max_rel_err(got, ref) <= max_rel_err(ref16, ref) + 1e-3
+
+
+PREFILL_SHAPES = [(17, 128, 256, 64), (128, 512, 512, 128), (200, 512, 768, 128),
+                  (37, 1024, 4160, 64), (513, 2048, 1024, 128), (1000, 1024, 800, 128),
+                  (256, 4096, 4096, 128)]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("rows,k,n,g", PREFILL_SHAPES)
+def test_prefill_tcgen05_parity(cuda_device, dtype, rows, k, n, g):
+    # The tensor-core path dequantizes in F exactly as the reference does, so
+    # it is compared with the oracle that rounds the weights to F.
+    x, qw, qz, s, _ = random_awq(k, n, g, dtype, rows, seed=rows + n)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16}[dtype]
+    y = cawq.gemm(to_torch(x, dtype, cuda_device), to_torch(qw, "u32", cuda_device),
+                  to_torch(qz, "u32", cuda_device), to_torch(s, dtype, cuda_device), g,
+                  plan={"path": PATH_PREFILL})
+    torch.cuda.synchronize()
+    got = as_f64(to_numpy(y, dtype), dtype)
+    ref = oracle.gemm_f64(x, qw, qz, s, g, dtype=dtype, deq_round=True)
+    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_prefill_bias_natural_order_fp32_out_and_ld(cuda_device, dtype):
+    rows, k, n, g = 300, 1024, 512, 128
+    x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed=9)
+    full = torch.zeros(rows, 2 * n, dtype=torch.float32, device=cuda_device)
+    cawq.gemm(to_torch(x, dtype, cuda_device), to_torch(qw, "u32", cuda_device),
+              to_torch(qz, "u32", cuda_device), to_torch(s, dtype, cuda_device), g,
+              bias=to_torch(b, dtype, cuda_device), out=full[:, n:], out_dtype=torch.float32,
+              order="natural", plan={"path": PATH_PREFILL})
+    torch.cuda.synchronize()
+    ref = oracle.gemm_f64(x, qw, qz, s, g, bias=b, dtype=dtype, order="natural", deq_round=True)
+    got = full.cpu().numpy()
+    assert max_rel_err(got[:, n:], ref) <= 2e-3
+    assert float(np.abs(got[:, :n]).max()) == 0.0
+
+
+def test_planner_picks_prefill_for_large_m(cuda_device):
+    assert cawq.plan_get(2048, 4096, 4096, 128, torch.float16)["path"] == PATH_PREFILL
+    assert cawq.plan_get(1, 4096, 4096, 128, torch.float16)["path"] == PATH_DECODE
+    assert cawq.plan_get(2048, 4096, 4096, 128, torch.float32)["path"] == PATH_GENERIC
+
+
+def test_prefill_full_size_sampled_rows(cuda_device):
+    # M = 2048 on the 4096 x 4096 layer; 64 sampled rows checked
+    from cube_awq_b200 import synth
+    k, n, g, m = 4096, 4096, 128, 2048
+    w = synth.make_weights(k, n, g, torch.float16, cuda_device, seed=77)
+    xt = synth.make_input(m, k, torch.float16, cuda_device, seed=78)
+    y = cawq.gemm(xt, w.qweight, w.qzeros, w.scales, g)
+    torch.cuda.synchronize()
+    rows = np.arange(0, m, 32)
+    x = xt.cpu().numpy()[rows]
+    ref = oracle.gemm_f64(x, w.qweight.cpu().numpy(), w.qzeros.cpu().numpy(),
+                          w.scales.cpu().numpy(), g, dtype="f16", deq_round=True)
+    assert max_rel_err(y.float().cpu().numpy()[rows], ref) <= GEMM_TOL["f16"]
+    assert cawq.device_error() == 0
