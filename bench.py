@@ -14,8 +14,14 @@ launches of one token, replayed as a CUDA graph.
            with the step's activations copied host->device from pinned memory
            and the step's outputs copied back, inside the timed region
   roofline: the decode kernel's algorithmic bytes per launch / its average
-           launch duration (CUDA events on the launching stream), against the
-           measured HBM copy bandwidth of MEASURED_PEAKS.json
+           launch duration over the timed region (CUDA events on the stream
+           the graph runs on; every launch in it is a decode kernel), against
+           the measured HBM copy bandwidth of MEASURED_PEAKS.json
+  prefill_m2048: BASELINE configs[2] at M = 2048 (f16), TFLOP/s per linear
+           against the measured dense bf16 tensor peak
+
+--workload prefill prints one line for the prefill measurement alone (for
+profiling), --no-autotune uses the planner's default plans.
 
 --impl reference runs the CPU restatement of the reference's arithmetic (the
 reference itself is Rust/CubeCL on wgpu and cannot run on this machine) on the
@@ -52,7 +58,11 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--rows", type=int, default=1)
-    ap.add_argument("--no-extras", action="store_true", help="skip the M sweep and CPU baseline")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the M sweep, the prefill numbers and the CPU baseline")
+    ap.add_argument("--no-autotune", action="store_true", help="use the default plans")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--prefill-rows", type=int, default=2048)
     return ap.parse_args()
 
 
@@ -167,8 +177,11 @@ def run_ours(a, rank, local_rank, world):
     # one autotune per distinct shape (setup, untimed); plans are then cached
     plans = {}
     for name, k, n, layer in layers[0]:
-        plans[name] = cawq.autotune(xs[name], layer.qweight, layer.qzeros, layer.scales, GROUP,
-                                    out=ys[name])
+        if a.no_autotune:
+            plans[name] = cawq.plan_get(rows, k, n, GROUP, dt)
+        else:
+            plans[name] = cawq.autotune(xs[name], layer.qweight, layer.qzeros, layer.scales,
+                                        GROUP, out=ys[name])
 
     def step():
         for lin in layers:
@@ -200,18 +213,26 @@ def run_ours(a, rank, local_rank, world):
         graph.replay()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches_per_step = a.layers * len(LLAMA2_7B)
     with ClockSampler(local_rank) as clocks:
         barrier()
-        e0.record()
-        for _ in range(a.steps):
-            graph.replay()
-        e1.record()
+        torch.cuda.nvtx.range_push("cawq_timed")
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(a.steps):
+                graph.replay()
+            e1.record(stream)
         e1.synchronize()
+        torch.cuda.nvtx.range_pop()
         barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1)) / a.steps
+    ms_local = e0.elapsed_time(e1) / a.steps
+    ms = max_over_ranks(ms_local)
     value = step_bytes * world / (ms * 1e-3) / 1e9
+    # roofline: every launch of the timed region is a decode kernel; its
+    # average duration there (launches overlap only by their prologues)
+    achieved = (step_bytes / launches_per_step) / (ms_local * 1e-3 / launches_per_step) / 1e9
 
-    # ---- roofline: per-launch CUDA events on the launching stream
+    # ---- per-linear launches, each bracketed by events (diagnostic only)
     n_prof = max(1, min(a.steps, 20))
     evs = []
     cur = torch.cuda.current_stream(dev)
@@ -225,13 +246,8 @@ def run_ours(a, rank, local_rank, world):
                 evs.append((weight_bytes(k, n), s0, s1, name))
     torch.cuda.synchronize()
     per_name = {}
-    tot_b, tot_ms = 0, 0.0
     for b, s0, s1, name in evs:
-        t = s0.elapsed_time(s1)
-        tot_b += b
-        tot_ms += t
-        per_name.setdefault(name, []).append(t)
-    achieved = tot_b / (tot_ms * 1e-3) / 1e9
+        per_name.setdefault(name, []).append(s0.elapsed_time(s1))
     peaks, peaks_kind = measured_peaks()
     traffic = profile_traffic()
 
@@ -296,6 +312,7 @@ def run_ours(a, rank, local_rank, world):
                              "gb_per_s": round(step_bytes / (t * 1e-3) / 1e9, 1)}
             del g2
         extras["decode_sweep_m"] = sweep
+        extras["prefill_m2048"] = prefill_numbers(a, dev, peaks)
 
     if world > 1:
         del graph
@@ -316,20 +333,86 @@ def run_ours(a, rank, local_rank, world):
                    "graph": "one CUDA graph per step (128 launches)",
                    "plans": plans, "parallelism": f"replica x{world} (weak, no data-path collective)"},
         "tokens_per_s": round(world * 1e3 / ms, 1),
-        "us_per_linear": {k: round(statistics.median(v) * 1e3, 2) for k, v in per_name.items()},
+        "us_per_linear_isolated": {k: round(statistics.median(v) * 1e3, 2)
+                                   for k, v in per_name.items()},
         "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                 "api": "AWQGEMMLinear.forward x 128, no graph"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": traffic, "peak_kind": peaks_kind,
-                     "kernel": "cawq::decode_kernel (per-launch events, 20 steps x 128 launches)"},
+                     "algorithmic_bytes_per_launch": step_bytes // launches_per_step,
+                     "kernel": "cawq::decode_kernel, average over the timed region "
+                               f"({launches_per_step} launches per step)"},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
-        "gpu_launches": a.steps * a.layers * len(LLAMA2_7B),
+        "gpu_launches": a.steps * launches_per_step,
     }
     line.update(extras)
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ prefill
+def prefill_numbers(a, dev, peaks, reps=10, copies=3):
+    """configs[2] at M = prefill_rows, f16: TFLOP/s of each Llama-2-7B linear,
+    graph-timed over `copies` distinct weight sets (flops = 2 M N K)."""
+    import torch
+
+    import cube_awq_b200 as cawq
+    from cube_awq_b200 import synth
+    m, dt = a.prefill_rows, torch.float16
+    out = {}
+    stream = torch.cuda.Stream(dev)
+    for j, (name, k, n) in enumerate(LLAMA2_7B):
+        ws = [synth.make_weights(k, n, GROUP, dt, dev, seed=900 + 10 * j + c) for c in range(copies)]
+        x = synth.make_input(m, k, dt, dev, seed=950 + j)
+        y = torch.empty(m, n, dtype=dt, device=dev)
+        plan = cawq.plan_get(m, k, n, GROUP, dt)
+        for w in ws:
+            cawq.gemm(x, w.qweight, w.qzeros, w.scales, GROUP, out=y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for w in ws:
+                    cawq.gemm(x, w.qweight, w.qzeros, w.scales, GROUP, out=y)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+        tflops = 2.0 * m * n * k / (us * 1e-6) / 1e12
+        out[name] = {"us": round(us, 2), "tflops": round(tflops, 1),
+                     "frac_of_measured_bf16_peak": round(tflops / peaks["bf16_tflops"], 4),
+                     "path": plan["path"]}
+        del g, ws
+    return out
+
+
+def run_prefill_only(a, rank, local_rank, world):
+    import torch
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    peaks, kind = measured_peaks()
+    res = prefill_numbers(a, dev, peaks, reps=a.steps, copies=3)
+    if rank != 0:
+        return
+    tot_flops = sum(2.0 * a.prefill_rows * n * k for _, k, n in LLAMA2_7B)
+    tot_us = sum(r["us"] for r in res.values())
+    tf = tot_flops / (tot_us * 1e-6) / 1e12
+    print(json.dumps({"metric": "AWQ GEMM prefill TFLOP/s (Llama-2-7B AWQ linears, f16)",
+                      "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": 1,
+                      "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+                      "config": {"workload": f"configs[2] prefill M={a.prefill_rows}, g128",
+                                 "rows_m": a.prefill_rows},
+                      "per_linear": res, "peak": peaks["bf16_tflops"], "peak_kind": kind,
+                      "frac": round(tf / peaks["bf16_tflops"], 4)}), flush=True)
 
 
 # ------------------------------------------------------- CPU baseline
@@ -400,6 +483,8 @@ def main():
     rank, local_rank, world = dist_env()
     if a.impl == "reference":
         run_reference(a, rank, world)
+    elif a.workload == "prefill":
+        run_prefill_only(a, rank, local_rank, world)
     else:
         run_ours(a, rank, local_rank, world)
 
