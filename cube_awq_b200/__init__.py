@@ -21,6 +21,7 @@ from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, a
                      plan_get, plan_set, select_tile_m, select_tile_n, validate_decode_launch_params,
                      validate_launch_params, version)
 from .modules import AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear, AWQLinearConfig
+from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
 
 import os as _os
 
@@ -29,6 +30,7 @@ if _os.path.exists(_lib.LIB_PATH):
 
 __all__ = [
     "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
+    "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
     "dequantize_awq", "dequantize_native", "device_error", "gemm", "plan_cache_clear",

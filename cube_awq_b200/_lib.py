@@ -44,7 +44,11 @@ EXPORTED = (
     "cawq_plan_get", "cawq_plan_set", "cawq_plan_cache_clear", "cawq_autotune",
     "cawq_dequantize_native", "cawq_dequantize",
     "cawq_tp_column_shard", "cawq_tp_row_shard", "cawq_tp_interleave_columns",
+    "cawq_tp_unique_id", "cawq_tp_init", "cawq_tp_destroy", "cawq_tp_info",
+    "cawq_gemm_colpar", "cawq_gemm_rowpar",
 )
+
+CAWQ_TP_ID_BYTES = 128
 
 
 class ShapeConfigC(ctypes.Structure):
@@ -129,6 +133,19 @@ def _declare(L) -> None:
     L.cawq_tp_row_shard.restype = st
     L.cawq_tp_interleave_columns.argtypes = [vp, vp, sz, sz, i, i, vp]
     L.cawq_tp_interleave_columns.restype = st
+    L.cawq_tp_unique_id.argtypes = [ctypes.c_char_p]
+    L.cawq_tp_unique_id.restype = st
+    L.cawq_tp_init.argtypes = [i, i, ctypes.c_char_p, i, ctypes.POINTER(vp)]
+    L.cawq_tp_init.restype = st
+    L.cawq_tp_destroy.argtypes = [vp]
+    L.cawq_tp_destroy.restype = st
+    L.cawq_tp_info.argtypes = [vp, ctypes.POINTER(i), ctypes.POINTER(i)]
+    L.cawq_tp_info.restype = st
+    tp_args = [vp, vp, u32p, u32p, vp, vp, vp, vp, sz, sz, sz, sz, i, vp]
+    L.cawq_gemm_colpar.argtypes = tp_args
+    L.cawq_gemm_colpar.restype = st
+    L.cawq_gemm_rowpar.argtypes = tp_args
+    L.cawq_gemm_rowpar.restype = st
 
 
 def lib():

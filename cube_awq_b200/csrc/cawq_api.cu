@@ -3,8 +3,11 @@
 // dispatch to the sm_100a kernels in cawq_kernels.cu.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -12,6 +15,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 
 #include "cawq_internal.h"
@@ -685,5 +689,234 @@ CAWQ_API cawq_status cawq_tp_interleave_columns(const void* src, void* dst, size
   cudaError_t e = launch_interleave_columns(src, dst, rows, n, world, dtype_size(dtype),
                                             static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "interleave launch");
+  return CAWQ_OK;
+}
+
+// ------------------------------------------------------ tensor parallel
+// NCCL is loaded at run time (libnccl.so.2; in a process that already holds
+// torch's copy, that one), so libcube_awq.so links no NCCL.
+namespace {
+
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      api.why = "libnccl.so.2 not found";
+      return;
+    }
+    auto sym = [&](const char* name) { return dlsym(h, name); };
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+    api.init_rank_config =
+        reinterpret_cast<decltype(api.init_rank_config)>(sym("ncclCommInitRankConfig"));
+    api.destroy = reinterpret_cast<decltype(api.destroy)>(sym("ncclCommDestroy"));
+    api.abort = reinterpret_cast<decltype(api.abort)>(sym("ncclCommAbort"));
+    api.async_error = reinterpret_cast<decltype(api.async_error)>(sym("ncclCommGetAsyncError"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.ok = api.get_unique_id && api.init_rank_config && api.destroy && api.abort &&
+             api.async_error && api.all_gather && api.all_reduce && api.error_string;
+    if (!api.ok) api.why = "libnccl.so.2 lacks a required symbol";
+  });
+  return api;
+}
+
+cawq_status nccl_fail(ncclResult_t r, const char* where) {
+  const NcclApi& a = nccl();
+  return fail(CAWQ_ERR_NCCL, fmt("%s: %s", where, a.ok ? a.error_string(r) : a.why.c_str()));
+}
+
+ncclDataType_t nccl_type(int dt) {
+  return dt == CAWQ_F32 ? ncclFloat32 : dt == CAWQ_F16 ? ncclFloat16 : ncclBfloat16;
+}
+
+}  // namespace
+
+struct cawq_tp_comm {
+  ncclComm_t comm = nullptr;
+  int world = 0, rank = 0, device = -1;
+  int timeout_ms = 60000;
+};
+
+// A non-blocking communicator returns ncclInProgress while it sets up; wait
+// for the result, at most the communicator's timeout, then abort it.
+static cawq_status nccl_settle(cawq_tp_comm* c, ncclResult_t r, const char* where) {
+  const NcclApi& a = nccl();
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, where);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t q = a.async_error(c->comm, &st);
+    if (q != ncclSuccess) return nccl_fail(q, where);
+    if (st == ncclSuccess) return CAWQ_OK;
+    if (st != ncclInProgress) return nccl_fail(st, where);
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0)
+                        .count();
+    if (ms > c->timeout_ms) {
+      return fail(CAWQ_ERR_TIMEOUT, fmt("%s: NCCL did not finish within %d ms", where,
+                                        c->timeout_ms));
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
+CAWQ_API cawq_status cawq_tp_unique_id(uint8_t* id) {
+  if (!id) return fail(CAWQ_ERR_NULL_POINTER, "id must be non-null");
+  static_assert(sizeof(ncclUniqueId) == CAWQ_TP_ID_BYTES, "NCCL unique id size");
+  const NcclApi& a = nccl();
+  if (!a.ok) return fail(CAWQ_ERR_NCCL, a.why);
+  ncclUniqueId u;
+  ncclResult_t r = a.get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  std::memcpy(id, &u, sizeof(u));
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_tp_init(int world, int rank, const uint8_t* id, int timeout_ms,
+                                  cawq_tp_comm** comm) {
+  if (!id || !comm) return fail(CAWQ_ERR_NULL_POINTER, "id and comm must be non-null");
+  *comm = nullptr;
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(CAWQ_ERR_INVALID_ARGUMENT, "rank must be in [0, world)");
+  DeviceInfo dev;
+  cawq_status st = require_sm100(&dev);
+  if (st != CAWQ_OK) return st;
+  const NcclApi& a = nccl();
+  if (!a.ok) return fail(CAWQ_ERR_NCCL, a.why);
+  auto* c = new cawq_tp_comm();
+  c->world = world;
+  c->rank = rank;
+  c->device = dev.device;
+  c->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = a.init_rank_config(&c->comm, world, u, rank, &cfg);
+  st = nccl_settle(c, r, "ncclCommInitRankConfig");
+  if (st != CAWQ_OK) {
+    if (c->comm) a.abort(c->comm);
+    delete c;
+    return st;
+  }
+  *comm = c;
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_tp_destroy(cawq_tp_comm* comm) {
+  if (!comm) return CAWQ_OK;
+  const NcclApi& a = nccl();
+  cawq_status st = CAWQ_OK;
+  if (comm->comm) {
+    ncclResult_t r = a.destroy(comm->comm);
+    if (r == ncclInProgress) st = nccl_settle(comm, r, "ncclCommDestroy");
+    else if (r != ncclSuccess) st = nccl_fail(r, "ncclCommDestroy");
+  }
+  delete comm;
+  return st;
+}
+
+CAWQ_API cawq_status cawq_tp_info(const cawq_tp_comm* comm, int* world, int* rank) {
+  if (!comm || !world || !rank) return fail(CAWQ_ERR_NULL_POINTER, "arguments must be non-null");
+  *world = comm->world;
+  *rank = comm->rank;
+  return CAWQ_OK;
+}
+
+static cawq_status tp_check(const cawq_tp_comm* comm) {
+  if (!comm || !comm->comm) return fail(CAWQ_ERR_NULL_POINTER, "comm must be an initialised communicator");
+  int d = -1;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (d != comm->device)
+    return fail(CAWQ_ERR_INVALID_ARGUMENT,
+                fmt("current device %d is not the communicator's device %d", d, comm->device));
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_gemm_colpar(const cawq_tp_comm* comm, const void* x,
+                                      const uint32_t* qweight, const uint32_t* qzeros,
+                                      const void* scales, const void* bias, void* out,
+                                      void* gather, size_t rows, size_t k, size_t n,
+                                      size_t group_size, cawq_dtype dtype, void* stream) {
+  cawq_status st = tp_check(comm);
+  if (st != CAWQ_OK) return st;
+  if (!valid_dtype(dtype)) return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
+  size_t n0 = 0, nl = 0;
+  if ((st = cawq_tp_column_shard(n, comm->world, comm->rank, &n0, &nl)) != CAWQ_OK) return st;
+  if (rows == 0) return CAWQ_OK;
+  if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+  if (!gather) {
+    if (rows != 1) return fail(CAWQ_ERR_NULL_POINTER, "gather workspace is required when rows > 1");
+    gather = out;  // [world][1][n/world] is [1][n]
+  }
+  const size_t es = dtype_size(dtype);
+  const size_t count = rows * nl;
+  void* mine = static_cast<uint8_t*>(gather) + comm->rank * count * es;
+  st = gemm_common(x, qweight, qzeros, scales, bias, mine, rows, k, nl, group_size, dtype, dtype,
+                   CAWQ_ORDER_AWQ, nl, nullptr, stream, true);
+  if (st != CAWQ_OK) return st;
+  const NcclApi& a = nccl();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ncclResult_t r = a.all_gather(mine, gather, count, nccl_type(dtype), comm->comm, s);
+  if (r == ncclInProgress) {
+    st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllGather");
+    if (st != CAWQ_OK) return st;
+  } else if (r != ncclSuccess) {
+    return nccl_fail(r, "ncclAllGather");
+  }
+  if (gather == out) return CAWQ_OK;
+  cudaError_t e = launch_interleave_columns(gather, out, rows, n, comm->world, es, s);
+  if (e != cudaSuccess) return cuda_fail(e, "interleave launch");
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x,
+                                      const uint32_t* qweight, const uint32_t* qzeros,
+                                      const void* scales, const void* bias, void* out,
+                                      float* partial, size_t rows, size_t k, size_t n,
+                                      size_t group_size, cawq_dtype dtype, void* stream) {
+  cawq_status st = tp_check(comm);
+  if (st != CAWQ_OK) return st;
+  if (!valid_dtype(dtype)) return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
+  size_t k0 = 0, kl = 0;
+  if ((st = cawq_tp_row_shard(k, group_size, comm->world, comm->rank, &k0, &kl)) != CAWQ_OK)
+    return st;
+  if (rows == 0) return CAWQ_OK;
+  if (!out || !partial) return fail(CAWQ_ERR_NULL_POINTER, "out and partial must be non-null");
+  st = gemm_common(x, qweight, qzeros, scales, nullptr, partial, rows, kl, n, group_size, dtype,
+                   CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
+  if (st != CAWQ_OK) return st;
+  const NcclApi& a = nccl();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ncclResult_t r = a.all_reduce(partial, partial, rows * n, ncclFloat32, ncclSum, comm->comm, s);
+  if (r == ncclInProgress) {
+    st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
+    if (st != CAWQ_OK) return st;
+  } else if (r != ncclSuccess) {
+    return nccl_fail(r, "ncclAllReduce");
+  }
+  if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
+  cudaError_t e = launch_rowpar_finish(partial, bias, out, rows, n, dtype, s);
+  if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
   return CAWQ_OK;
 }

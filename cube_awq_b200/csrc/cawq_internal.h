@@ -74,6 +74,8 @@ cudaError_t launch_dequant(const uint32_t* qw, const uint32_t* qz, const void* s
 
 cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, size_t n,
                                       int world, size_t elem, cudaStream_t stream);
+cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* out, size_t rows,
+                                 size_t n, int dtype, cudaStream_t stream);
 
 cudaError_t read_device_error(uint32_t* word, int reset);
 

@@ -1,6 +1,10 @@
-// cawq_tp.cuh — helper kernel of the tensor-parallel layer: turns the
-// rank-major result of an all-gather of column shards, src[world][rows][n/world],
-// back into the row-major output dst[rows][n].
+// cawq_tp.cuh — helper kernels of the tensor-parallel layers:
+//   * interleave_columns: turns the rank-major result of an all-gather of
+//     column shards, src[world][rows][n/world], back into the row-major
+//     output dst[rows][n];
+//   * rowpar_finish: out[rows][n] = F(partial + bias) after the fp32
+//     all-reduce of a row-parallel layer (the bias is added once, after the
+//     full sum, as the single-device layer does).
 #pragma once
 
 #include "cawq_common.cuh"
@@ -44,6 +48,39 @@ cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, s
     interleave_columns_kernel<uint16_t><<<(unsigned)blocks, 256, 0, stream>>>(
         static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), rows, shard_bytes / 2,
         world);
+  }
+  return cudaGetLastError();
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256)
+    rowpar_finish_kernel(const float* __restrict__ partial, const typename DType<DT>::T* bias,
+                         typename DType<DT>::T* out, size_t rows, size_t n) {
+  const size_t total = rows * n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float v = partial[i];
+    if (bias) v += DType<DT>::to_f32(bias[i % n]);
+    out[i] = DType<DT>::from_f32(v);
+  }
+}
+
+cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* out, size_t rows,
+                                 size_t n, int dtype, cudaStream_t stream) {
+  size_t blocks = (rows * n + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  if (blocks < 1) blocks = 1;
+  const unsigned b = static_cast<unsigned>(blocks);
+  if (dtype == kF32) {
+    rowpar_finish_kernel<kF32><<<b, 256, 0, stream>>>(partial, static_cast<const float*>(bias),
+                                                      static_cast<float*>(out), rows, n);
+  } else if (dtype == kF16) {
+    rowpar_finish_kernel<kF16><<<b, 256, 0, stream>>>(partial, static_cast<const __half*>(bias),
+                                                      static_cast<__half*>(out), rows, n);
+  } else {
+    rowpar_finish_kernel<kBF16><<<b, 256, 0, stream>>>(
+        partial, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), rows,
+        n);
   }
   return cudaGetLastError();
 }

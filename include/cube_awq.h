@@ -287,6 +287,67 @@ cawq_status cawq_tp_interleave_columns(const void* src, void* dst, size_t rows,
                                        size_t n, int world, cawq_dtype dtype,
                                        void* stream);
 
+/* ----------------------------------------------------------------------- */
+/* Tensor-parallel layers over NCCL (no reference counterpart)              */
+/* ----------------------------------------------------------------------- */
+
+/* Size of the NCCL unique id every rank passes to cawq_tp_init. */
+#define CAWQ_TP_ID_BYTES 128
+
+/* A communicator over `world` GPUs, one per rank (opaque). */
+typedef struct cawq_tp_comm cawq_tp_comm;
+
+/*
+ * Rank 0 creates the id and hands its CAWQ_TP_ID_BYTES bytes to every rank
+ * (any out-of-band channel). NCCL (libnccl.so.2) is loaded on first use; the
+ * library has no link-time dependency on it.
+ */
+cawq_status cawq_tp_unique_id(uint8_t* id);
+
+/*
+ * Joins the communicator on the current CUDA device. Returns
+ * CAWQ_ERR_TIMEOUT (and releases everything) if the other ranks have not
+ * joined within `timeout_ms` milliseconds (<= 0: 60 s).
+ */
+cawq_status cawq_tp_init(int world, int rank, const uint8_t* id, int timeout_ms,
+                         cawq_tp_comm** comm);
+
+/* Releases the communicator (after all work on it has finished). */
+cawq_status cawq_tp_destroy(cawq_tp_comm* comm);
+
+/* World size / rank of a communicator. */
+cawq_status cawq_tp_info(const cawq_tp_comm* comm, int* world, int* rank);
+
+/*
+ * Column-parallel layer (gate_up, qkv): this rank holds output columns
+ * [rank * N/world, (rank + 1) * N/world) — qweight [K, N/(8 world)],
+ * qzeros [K/g, N/(8 world)], scales [K/g, N/world], bias [N/world] or NULL,
+ * as cawq_tp_column_shard cuts them. x [rows, K] is replicated. Computes the
+ * local [rows, N/world] slice, all-gathers the slices over NCCL and writes
+ * the full out [rows, N]. `gather` is caller workspace of rows * N elements
+ * of `dtype`; it may be NULL when rows == 1 (the gather then runs in place
+ * in `out`). Everything is enqueued on `stream`.
+ */
+cawq_status cawq_gemm_colpar(const cawq_tp_comm* comm, const void* x, const uint32_t* qweight,
+                             const uint32_t* qzeros, const void* scales, const void* bias,
+                             void* out, void* gather, size_t rows, size_t k, size_t n,
+                             size_t group_size, cawq_dtype dtype, void* stream);
+
+/*
+ * Row-parallel layer (down, o): this rank holds K rows
+ * [rank * K/world, (rank + 1) * K/world) on group boundaries — qweight
+ * [K/world, N/8], qzeros [K/(g world), N/8], scales [K/(g world), N], as
+ * cawq_tp_row_shard cuts them — and x [rows, K/world], its columns of the
+ * input. Computes the fp32 partial [rows, N] into `partial` (caller
+ * workspace, rows * N floats), all-reduces it (sum, fp32) over NCCL, then
+ * writes out [rows, N] = partial + bias (bias [N] or NULL, added once).
+ * With dtype CAWQ_F32, out may be `partial` itself.
+ */
+cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint32_t* qweight,
+                             const uint32_t* qzeros, const void* scales, const void* bias,
+                             void* out, float* partial, size_t rows, size_t k, size_t n,
+                             size_t group_size, cawq_dtype dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
