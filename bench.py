@@ -19,6 +19,11 @@ launches of one token, replayed as a CUDA graph.
            the measured HBM copy bandwidth of MEASURED_PEAKS.json
   prefill_m2048: BASELINE configs[2] at M = 2048 (f16), TFLOP/s per linear
            against the measured dense bf16 tensor peak
+  tp_llama3_70b_mlp: BASELINE configs[4], the Llama-3-70B MLP sharded over
+           the job's GPUs (gate_up 8192->57344 column-parallel, down
+           28672->8192 row-parallel with an fp32 NCCL all-reduce, through the
+           library's own communicator), M in {1, 8, 2048}: us per MLP, max
+           over ranks (strong scaling: the layer is fixed, N GPUs share it)
 
 --workload prefill prints one line for the prefill measurement alone (for
 profiling), --no-autotune uses the planner's default plans.
@@ -313,6 +318,7 @@ def run_ours(a, rank, local_rank, world):
             del g2
         extras["decode_sweep_m"] = sweep
         extras["prefill_m2048"] = prefill_numbers(a, dev, peaks)
+        extras["tp_llama3_70b_mlp"] = tp_mlp_numbers(dev, world, max_over_ranks)
 
     if world > 1:
         del graph
@@ -393,6 +399,50 @@ def prefill_numbers(a, dev, peaks, reps=10, copies=3):
                      "path": plan["path"]}
         del g, ws
     return out
+
+
+def tp_mlp_numbers(dev, world, max_over_ranks, reps=10):
+    """configs[4] over all ranks of the job: us per MLP forward (gate_up
+    column-parallel without the gather, then down row-parallel on this rank's
+    half of the gate_up columns, as after the SiLU-and-mul), max over ranks."""
+    import torch
+
+    from cube_awq_b200 import synth, tp
+    k1, n1, k2, n2, g, dt = 8192, 57344, 28672, 8192, GROUP, torch.float16
+    comm = tp.TPComm(timeout_ms=120000)
+    w1 = synth.make_weights(k1, n1, g, dt, dev, seed=4001)
+    w2 = synth.make_weights(k2, n2, g, dt, dev, seed=4002)
+    col = tp.ColumnParallelAWQLinear(w1.qweight, w1.qzeros, w1.scales, gather_output=False,
+                                     backend="native", comm=comm)
+    row = tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend="native", comm=comm)
+    del w1, w2
+    torch.cuda.empty_cache()
+    res = {"n_gpus": world, "backend": "native NCCL (cawq_gemm_rowpar)"}
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for m in (1, 8, 2048):
+        x = synth.make_input(m, k1, dt, dev, seed=4003)
+        for _ in range(3):
+            h = col.forward(x)
+            row.forward(h[:, :k2 // world].contiguous())
+        torch.cuda.synchronize()
+        t_col = t_row = 0.0
+        for _ in range(reps):
+            e[0].record()
+            h = col.forward(x)
+            hh = h[:, :k2 // world].contiguous()
+            e[1].record()
+            row.forward(hh)
+            e[2].record()
+            e[2].synchronize()
+            t_col += e[0].elapsed_time(e[1])
+            t_row += e[1].elapsed_time(e[2])
+        t_col = max_over_ranks(t_col / reps) * 1e3
+        t_row = max_over_ranks(t_row / reps) * 1e3
+        res[f"M={m}"] = {"us": round(t_col + t_row, 2), "gate_up_colpar_us": round(t_col, 2),
+                         "down_rowpar_allreduce_us": round(t_row, 2)}
+    del col, row
+    comm.close()
+    return res
 
 
 def run_prefill_only(a, rank, local_rank, world):

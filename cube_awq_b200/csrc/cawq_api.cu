@@ -775,7 +775,12 @@ static cawq_status nccl_settle(cawq_tp_comm* c, ncclResult_t r, const char* wher
       return fail(CAWQ_ERR_TIMEOUT, fmt("%s: NCCL did not finish within %d ms", where,
                                         c->timeout_ms));
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    // an enqueue settles in microseconds; only a communicator set-up waits long
+    if (ms < 20) {
+      std::this_thread::yield();
+    } else {
+      std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
   }
 }
 
