@@ -4,15 +4,25 @@
 // Replaces gemm_awq (src/kernel/awq_kernel_gemm.rs:181-439), the reference's
 // M > 8 kernel, which computes on CUDA cores with scalar FMA.
 //
-// One CTA computes a 128 x 256 output tile; K advances in 64-row stages
-// through a 3-deep shared-memory ring. Warp roles (320 threads):
-//   warp 0     TMA producer: X tile (128 x 64, 128B swizzle, K-major), the
-//              packed weight tile (64 x 32 words, 128B swizzle), and the
-//              scale and zero rows of the stage's group, on one mbarrier.
-//   warp 1     allocates 256 TMEM columns; one thread issues
-//              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x 4
-//              per stage and commits each stage back to the producer.
-//   warps 2-9  dequantize the packed stage into the B operand: per packed
+// One CTA computes a 256 x 256 output tile as two 128-row halves that share
+// every dequantized B stage (two M=128 MMAs per k step into two TMEM
+// accumulators, all 512 columns): dequantizing, not the tensor core, is the
+// cost of this kernel, and this spends it once per 256 rows. K advances in
+// 64-row stages through three shared-memory rings:
+//   X ring (3 x 32 KB)  X tile 256 x 64, 128B swizzle, K-major; loaded by TMA,
+//                       freed by the MMA;
+//   W ring (4 x 9 KB)   packed weight tile 64 x 32 words (128B swizzle) and
+//                       the stage's scale and zero rows; loaded by TMA, freed
+//                       by the dequantize warps as soon as they have read it;
+//   B ring (2 x 32 KB)  the dequantized B operand (MN-major, 128B swizzle);
+//                       written by the dequantize warps, freed by the MMA.
+// Warp roles (96 + 32 * kPfDqWarps threads):
+//   warp 0     TMA producer of the X ring;
+//   warp 1     allocates 512 TMEM columns; one thread issues
+//              tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256, K=16) x 8
+//              per stage and commits each stage back to the X and B rings;
+//   warp 2     TMA producer of the W ring;
+//   warps 3.. dequantize the packed stage into the B operand: per packed
 //              word, lop3 makes (1024 + q) f16 pairs of adjacent columns,
 //              then (q - z) * s is formed in F exactly as the reference does
 //              (one rounding), and 16 bytes land in the canonical MN-major
@@ -27,22 +37,28 @@
 
 namespace cawq {
 
-constexpr int kPfBM = 128;
+constexpr int kPfBM = 256;   // two 128-row MMA halves
 constexpr int kPfBN = 256;
 constexpr int kPfBK = 64;
-constexpr int kPfStages = 3;
+constexpr int kPfXStages = 3;
+constexpr int kPfWStages = 4;
+constexpr int kPfBStages = 2;
+constexpr int kPfTmemCols = 2 * kPfBN;
 constexpr int kPfDqWarps = 8;                       // dequant / epilogue warps
-constexpr int kPfThreads = 64 + 32 * kPfDqWarps;    // + producer + MMA warp
+constexpr int kPfThreads = 96 + 32 * kPfDqWarps;    // + X producer, MMA, W producer
 
 struct PrefillLayout {
-  static constexpr int kX = kPfBM * kPfBK * 2;      // 16384
+  static constexpr int kX = kPfBM * kPfBK * 2;      // 32768 (two 16 KB halves)
   static constexpr int kB = kPfBK * kPfBN * 2;      // 32768
   static constexpr int kW = kPfBK * kPfBN / 8 * 4;  // 8192
   static constexpr int kS = kPfBN * 2;              // 512
   static constexpr int kZ = kPfBN / 8 * 4;          // 128
-  static constexpr int kStage = ((kX + kB + kW + kS + kZ) + 1023) / 1024 * 1024;
+  static constexpr int kWSlot = ((kW + kS + kZ) + 1023) / 1024 * 1024;
+  static constexpr size_t kOffB = (size_t)kX * kPfXStages;
+  static constexpr size_t kOffW = kOffB + (size_t)kB * kPfBStages;
+  static constexpr size_t kOffBars = kOffW + (size_t)kWSlot * kPfWStages;
   static constexpr int kBars = 1024;  // barriers + TMEM slot
-  static constexpr size_t kSmem = 1024 + (size_t)kStage * kPfStages + kBars;
+  static constexpr size_t kSmem = 1024 + kOffBars + kBars;
 };
 
 // ------------------------------------------------------- tcgen05 helpers
@@ -177,10 +193,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   using H = PfHalf2<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)L::kStage * kPfStages);
-  uint64_t* bready = full + kPfStages;
-  uint64_t* empty = bready + kPfStages;
-  uint64_t* acc_full = empty + kPfStages;
+  uint64_t* full_x = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
+  uint64_t* empty_x = full_x + kPfXStages;
+  uint64_t* full_w = empty_x + kPfXStages;
+  uint64_t* empty_w = full_w + kPfWStages;
+  uint64_t* bready = empty_w + kPfWStages;
+  uint64_t* bempty = bready + kPfBStages;
+  uint64_t* acc_full = bempty + kPfBStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -189,13 +208,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t m0 = blockIdx.y * kPfBM;
   const int KT = static_cast<int>(k / kPfBK);
 
-  auto stage_base = [&](int s) { return smem + (size_t)s * L::kStage; };
+  auto x_slot = [&](int s) { return smem + (size_t)s * L::kX; };
+  auto b_slot = [&](int s) { return smem + L::kOffB + (size_t)s * L::kB; };
+  auto w_slot = [&](int s) { return smem + L::kOffW + (size_t)s * L::kWSlot; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(&full[s], 1);
+    for (int s = 0; s < kPfXStages; ++s) {
+      mbar_init(&full_x[s], 1);
+      mbar_init(&empty_x[s], 1);
+    }
+    for (int s = 0; s < kPfWStages; ++s) {
+      mbar_init(&full_w[s], 1);
+      mbar_init(&empty_w[s], 32 * kPfDqWarps);
+    }
+    for (int s = 0; s < kPfBStages; ++s) {
       mbar_init(&bready[s], 32 * kPfDqWarps);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bempty[s], 1);
     }
     mbar_init(acc_full, 1);
     fence_mbarrier_init();
@@ -203,68 +231,86 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kPfBN);
+  if (warp == 1) tmem_alloc(tmem_slot, kPfTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
+    // ------------------------------------------------- X ring producer
     if (lane == 0) {
       bool ok = true;
       for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % kPfStages, u = kt / kPfStages;
-        if (u > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((u - 1) & 1));
+        const int s = kt % kPfXStages, u = kt / kPfXStages;
+        if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
-        uint8_t* b = stage_base(s);
-        const int grp = static_cast<int>((uint32_t)kt * kPfBK / g);
-        mbar_arrive_expect_tx(&full[s], L::kX + L::kW + L::kS + L::kZ);
-        tma_load_2d(b, &tm_x, kt * kPfBK, static_cast<int>(m0), &full[s]);
-        tma_load_2d(b + L::kX + L::kB, &tm_w, static_cast<int>(n0 / 8), kt * kPfBK, &full[s]);
-        tma_load_2d(b + L::kX + L::kB + L::kW, &tm_s, static_cast<int>(n0), grp, &full[s]);
-        tma_load_2d(b + L::kX + L::kB + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp,
-                    &full[s]);
+        mbar_arrive_expect_tx(&full_x[s], L::kX);
+        tma_load_2d(x_slot(s), &tm_x, kt * kPfBK, static_cast<int>(m0), &full_x[s]);
       }
     }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------- W ring producer
+    if (lane == 0) {
+      bool ok = true;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int s = kt % kPfWStages, u = kt / kPfWStages;
+        if (u > 0) ok = mbar_wait_bounded(&empty_w[s], (uint32_t)((u - 1) & 1));
+        if (!ok) break;
+        uint8_t* b = w_slot(s);
+        const int grp = static_cast<int>((uint32_t)kt * kPfBK / g);
+        mbar_arrive_expect_tx(&full_w[s], L::kW + L::kS + L::kZ);
+        tma_load_2d(b, &tm_w, static_cast<int>(n0 / 8), kt * kPfBK, &full_w[s]);
+        tma_load_2d(b + L::kW, &tm_s, static_cast<int>(n0), grp, &full_w[s]);
+        tma_load_2d(b + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp, &full_w[s]);
+      }
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, kPfBM, kPfBN);
+      constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, kPfBM / 2, kPfBN);
       bool ok = true;
       for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % kPfStages, u = kt / kPfStages;
-        ok = mbar_wait_bounded(&full[s], (uint32_t)(u & 1)) &&
-             mbar_wait_bounded(&bready[s], (uint32_t)(u & 1));
+        const int sx = kt % kPfXStages, ux = kt / kPfXStages;
+        const int sb = kt % kPfBStages, ub = kt / kPfBStages;
+        ok = mbar_wait_bounded(&full_x[sx], (uint32_t)(ux & 1)) &&
+             mbar_wait_bounded(&bready[sb], (uint32_t)(ub & 1));
         if (!ok) break;
         tc_fence_after();
-        const uint32_t xa = smem_u32(stage_base(s));
-        const uint32_t ba = xa + L::kX;
+        const uint32_t xa = smem_u32(x_slot(sx));
+        const uint32_t ba = smem_u32(b_slot(sb));
 #pragma unroll
         for (int j = 0; j < kPfBK / 16; ++j) {
-          const uint64_t ad = umma_desc_sw128(xa + 32 * j, 16, 1024);
           const uint64_t bd = umma_desc_sw128(ba + 2048 * j, 8192, 1024);
-          umma_f16(tmem, ad, bd, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t ad = umma_desc_sw128(xa + h * (L::kX / 2) + 32 * j, 16, 1024);
+            umma_f16(tmem + h * kPfBN, ad, bd, idesc, (kt > 0 || j > 0) ? 1u : 0u);
+          }
         }
-        umma_commit(&empty[s]);
+        umma_commit(&empty_x[sx]);
+        umma_commit(&bempty[sb]);
       }
       if (ok) umma_commit(acc_full);
     }
+    __syncwarp();
   } else {
     // ------------------------------------------- dequant, then epilogue
-    const int dw = warp - 2;   // 0..7
+    const int dw = warp - 3;   // 0..7
     const int q4 = lane >> 3;  // quarter of the warp -> row offset 2*q4
     const int l = lane & 7;    // packed word l + 8a, a = 0..3
     bool ok = true;
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kPfStages, u = kt / kPfStages;
-      if (ok) ok = mbar_wait_bounded(&full[s], (uint32_t)(u & 1));
-      if (ok && u > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((u - 1) & 1));
+      const int sw = kt % kPfWStages, uw = kt / kPfWStages;
+      const int sb = kt % kPfBStages, ub = kt / kPfBStages;
+      if (ok) ok = mbar_wait_bounded(&full_w[sw], (uint32_t)(uw & 1));
+      if (ok && ub > 0) ok = mbar_wait_bounded(&bempty[sb], (uint32_t)((ub - 1) & 1));
       if (ok) {
-        uint8_t* b = stage_base(s);
-        uint8_t* bsm = b + L::kX;
-        const uint8_t* wsm = b + L::kX + L::kB;
-        const uint8_t* srow = b + L::kX + L::kB + L::kW;
+        uint8_t* bsm = b_slot(sb);
+        const uint8_t* wsm = w_slot(sw);
+        const uint8_t* srow = wsm + L::kW;
         const uint32_t* zrow = reinterpret_cast<const uint32_t*>(srow + L::kS);
         uint32_t sp[4][4], zp[4][4];
 #pragma unroll
@@ -275,22 +321,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           pf_pairs<DT, ORDER>(zrow[w], zp[a]);
         }
         // 16 row sets of 4 rows (8-row atom x parity); each warp takes 2
+        uint32_t qv[16 / kPfDqWarps][4];
 #pragma unroll
         for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
           const int sidx = kPfDqWarps * pass + dw;
           const int row = (sidx >> 1) * 8 + (sidx & 1) + 2 * q4;  // 0..63
           const int r8 = row & 7;
-          uint32_t qv[4];
 #pragma unroll
           for (int a = 0; a < 4; ++a) {
             const int w = l + 8 * a;
-            qv[a] = *reinterpret_cast<const uint32_t*>(wsm + row * 128 + (((w >> 2) ^ r8) << 4) +
-                                                       ((w & 3) << 2));
+            qv[pass][a] = *reinterpret_cast<const uint32_t*>(wsm + row * 128 +
+                                                             (((w >> 2) ^ r8) << 4) + ((w & 3) << 2));
           }
+        }
+        // the W slot has been read: the producer may refill it
+        mbar_arrive(&empty_w[sw]);
+#pragma unroll
+        for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
+          const int sidx = kPfDqWarps * pass + dw;
+          const int row = (sidx >> 1) * 8 + (sidx & 1) + 2 * q4;
+          const int r8 = row & 7;
 #pragma unroll
           for (int a = 0; a < 4; ++a) {
             uint32_t t[4];
-            pf_pairs<DT, ORDER>(qv[a], t);
+            pf_pairs<DT, ORDER>(qv[pass][a], t);
             uint4 v;
             v.x = H::mul(H::sub(t[0], zp[a][0]), sp[a][0]);
             v.y = H::mul(H::sub(t[1], zp[a][1]), sp[a][1]);
@@ -300,22 +354,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                       ((l ^ r8) << 4)) = v;
           }
         }
+      } else {
+        mbar_arrive(&empty_w[sw]);
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bready[s]);
+      mbar_arrive(&bready[sb]);
     }
     // ---- epilogue: TMEM -> registers -> global
     if (ok) ok = mbar_wait_bounded(acc_full, 0u);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
     tc_fence_after();
     const int lq = warp & 3;      // TMEM lane quarter this warp may access
-    const int half = dw >> 2;     // which 128 of the 256 columns
-    const uint32_t row = m0 + 32 * lq + lane;
+    // the warps of one lane quarter split the 16 chunks of 32 accumulator
+    // columns (8 per 128-row half)
+    constexpr int kChunks = 16 / (kPfDqWarps / 4);
+    const int part = dw >> 2;
     if (ok) {
 #pragma unroll 1
-      for (int c = half * 4; c < half * 4 + 4; ++c) {
+      for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
+        const int h = cc >> 3, c = cc & 7;
+        const uint32_t row = m0 + 128 * h + 32 * lq + lane;
         float v[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + 32 * c, v);
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
         const uint32_t col0 = n0 + 32 * c;
         if (row < rows && col0 < n) {
           if (bias) {
@@ -356,7 +416,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kPfBN);
+    tmem_dealloc(tmem, kPfTmemCols);
   }
 }
 
@@ -445,7 +505,7 @@ cawq_plan prefill_default_plan(const GemmProblem&, const DeviceInfo&) {
   cawq_plan pl = {};
   pl.path = CAWQ_PATH_PREFILL;
   pl.tile_n = kPfBN;
-  pl.stages = kPfStages;
+  pl.stages = kPfBStages;
   return pl;
 }
 

@@ -246,3 +246,22 @@ def test_prefill_full_size_sampled_rows(cuda_device):
                           w.scales.cpu().numpy(), g, dtype="f16", deq_round=True)
     assert max_rel_err(y.float().cpu().numpy()[rows], ref) <= GEMM_TOL["f16"]
     assert cawq.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_prefill_is_deterministic_at_full_size(cuda_device, dtype):
+    # The tensor-core path has no atomics: repeated launches on the same
+    # inputs must agree bit for bit (a pipeline race would show up here).
+    from cube_awq_b200 import synth
+    k, n, g, m = 4096, 4096, 128, 2048
+    w = synth.make_weights(k, n, g, dtype, cuda_device, seed=81)
+    x = synth.make_input(m, k, dtype, cuda_device, seed=82)
+    plan = {"path": PATH_PREFILL}
+    y0 = cawq.gemm(x, w.qweight, w.qzeros, w.scales, g, plan=plan)
+    for _ in range(8):
+        y = cawq.gemm(x, w.qweight, w.qzeros, w.scales, g, plan=plan)
+        assert torch.equal(y, y0)
+    yg = cawq.gemm(x, w.qweight, w.qzeros, w.scales, g, plan={"path": PATH_GENERIC})
+    torch.cuda.synchronize()
+    rel = (y0.float() - yg.float()).abs().max() / yg.float().abs().max()
+    assert float(rel) <= GEMM_TOL["f16" if dtype == torch.float16 else "bf16"]
