@@ -13,7 +13,7 @@
 //                       freed by the MMA;
 //   W ring (4 x 9 KB)   packed weight tile 64 x 32 words (128B swizzle) and
 //                       the stage's scale and zero rows; loaded by TMA, freed
-//                       by the dequantize warps as soon as they have read it;
+//                       by the dequantize warps once they have used it;
 //   B ring (2 x 32 KB)  the dequantized B operand (MN-major, 128B swizzle);
 //                       written by the dequantize warps, freed by the MMA.
 // Warp roles (96 + 32 * kPfDqWarps threads):
@@ -334,8 +334,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                                              (((w >> 2) ^ r8) << 4) + ((w & 3) << 2));
           }
         }
-        // the W slot has been read: the producer may refill it
-        mbar_arrive(&empty_w[sw]);
 #pragma unroll
         for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
           const int sidx = kPfDqWarps * pass + dw;
@@ -354,6 +352,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                       ((l ^ r8) << 4)) = v;
           }
         }
+        // Only now may the producer refill the W slot: an mbarrier arrive
+        // does not wait for shared-memory loads still in flight, so it must
+        // follow the instructions that consume them (else the next TMA write
+        // can overtake a read).
+        mbar_arrive(&empty_w[sw]);
       } else {
         mbar_arrive(&empty_w[sw]);
       }
