@@ -187,6 +187,24 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
+// Split cluster barrier: arrive (release) early, wait (acquire) where needed.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 16-byte store into another CTA's shared memory; its mbarrier `remote_bar`
+// (same cluster) counts the bytes on arrival.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a, float b, float c,
+                                            float d, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      ::"r"(remote_addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
+      : "memory");
+}
+
 // Address of the same shared variable in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t local_addr, uint32_t rank) {
   uint32_t r;

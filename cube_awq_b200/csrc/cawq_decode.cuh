@@ -82,11 +82,13 @@ struct DecodeLayout {
     const size_t raw = z_off(strips, g) + gps(g) * z_row_bytes(strips);
     return (raw + 1023) / 1024 * 1024;
   }
+  // split-K receive buffer: [source rank][XB rows][band columns / split] fp32
+  static __host__ __device__ size_t recv_bytes(int strips) {
+    return (size_t)XB * strips * kDecTileCols * 4;
+  }
   static size_t smem_bytes(int strips, int stages, uint32_t g) {
-    size_t ring = slot_bytes(strips, g) * stages;
-    size_t red = (size_t)strips * XB * kDecTileCols * 4;
-    size_t body = ring > red ? ring : red;
-    return 1024 /* alignment slack */ + body + (size_t)stages * 16;
+    return 1024 /* alignment slack */ + slot_bytes(strips, g) * stages + recv_bytes(strips) +
+           (size_t)(2 * stages + 1) * 8;
   }
 };
 
@@ -148,19 +150,27 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   const int gps = L::gps(g);
 
   const size_t ring_bytes = slot * NS;
-  const size_t red_bytes = (size_t)strips * XB * kDecTileCols * 4;
-  uint64_t* full =
-      reinterpret_cast<uint64_t*>(smem + (ring_bytes > red_bytes ? ring_bytes : red_bytes));
+  float* recv = reinterpret_cast<float*>(smem + ring_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes + L::recv_bytes(strips));
   uint64_t* empty = full + NS;
+  uint64_t* recv_bar = empty + NS;  // the peers' partial sums have landed
+  const uint32_t rows_eff = rows < (uint32_t)XB ? rows : (uint32_t)XB;
+  const uint32_t bcols = static_cast<uint32_t>(strips * kDecTileCols);
+  const uint32_t ncols = bcols / split;  // columns of the band this CTA sums (multiple of 8)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], static_cast<uint32_t>(consumers));
     }
+    mbar_init(recv_bar, 1);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rows_eff * ncols * 4);
     fence_mbarrier_init();
   }
   __syncthreads();
+  // Peers push into this CTA's receive buffer only after every CTA of the
+  // cluster has passed this point (the matching wait precedes the pushes).
+  if (split > 1) cluster_arrive_release();
 
   bool ok = true;
   if (warp == consumers) {
@@ -433,61 +443,80 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     }
   }
 
-  // ---- reduction over the CTAs of the cluster (each warp owns its columns)
-  __syncthreads();
-  float* red = reinterpret_cast<float*>(smem);  // [strips][XB][128], reuses the ring
+  // ---- split-K sums. CTA q of the cluster owns columns [q ncols, (q+1) ncols)
+  // of the band: every CTA stores its partial sums of those columns into
+  // slot [its rank] of q's receive buffer (st.async to distributed shared
+  // memory, counted on q's recv_bar), then sums its own columns over the
+  // slots in rank order. One wait, no cluster-wide barrier at the end.
+  if (split == 1) {
+    if (warp < consumers) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const uint32_t row = static_cast<uint32_t>(8 * m + 2 * t + e);
+          if (row >= rows_eff) continue;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+              const uint32_t col = pband * 8 + strip * kDecTileCols + 8 * word +
+                                   col_of_nibble(2 * b + hi, ORDER);
+              if (col < n) {
+                float v = tot[m][b][2 * hi + e];
+                if (bias) v += DType<DT>::to_f32(bias[col]);
+                out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
+              }
+            }
+          }
+        }
+      }
+    }
+    return;
+  }
+  cluster_wait_acquire();  // every peer's recv_bar is initialised
   if (warp < consumers) {
-    float* base = red + ((size_t)strip * XB) * kDecTileCols;
+    const uint32_t bar_local = smem_u32(recv_bar);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const int cl = word * 8 + col_of_nibble(2 * b, ORDER);
-        const int ch = word * 8 + col_of_nibble(2 * b + 1, ORDER);
-        float* r0 = base + (size_t)(8 * m + 2 * t) * kDecTileCols;
-        float* r1 = r0 + kDecTileCols;
-        r0[cl] = tot[m][b][0];
-        r1[cl] = tot[m][b][1];
-        r0[ch] = tot[m][b][2];
-        r1[ch] = tot[m][b][3];
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t row = static_cast<uint32_t>(8 * m + 2 * t + e);
+        if (row >= rows_eff) continue;
+        float v[8];  // this lane's 8 consecutive columns, natural order
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          v[col_of_nibble(2 * b, ORDER)] = tot[m][b][e];
+          v[col_of_nibble(2 * b + 1, ORDER)] = tot[m][b][2 + e];
+        }
+        const uint32_t col8 = static_cast<uint32_t>(strip * kDecTileCols + 8 * word);
+        const uint32_t q = col8 / ncols;
+        float* dst = recv + ((size_t)rank * XB + row) * ncols + (col8 - q * ncols);
+        if (q == rank) {
+          reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+          reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+          const uint32_t ra = map_shared_rank(smem_u32(dst), q);
+          const uint32_t rb = map_shared_rank(bar_local, q);
+          st_async_v4(ra, v[0], v[1], v[2], v[3], rb);
+          st_async_v4(ra + 16, v[4], v[5], v[6], v[7], rb);
+        }
       }
     }
   }
+  // the peers' bytes (bounded wait), and this CTA's own stores
+  if (!mbar_wait_bounded(recv_bar, 0u)) ok = false;
   __syncthreads();
-  const int rows_eff = static_cast<int>(rows < (uint32_t)XB ? rows : (uint32_t)XB);
-  const int bcols = strips * kDecTileCols;
-  if (split > 1) {
-    cluster_sync_all();
-  } else {
-    __syncthreads();
-  }
-  const int cbeg = static_cast<int>((uint32_t)bcols * rank / split);
-  const int cend = static_cast<int>((uint32_t)bcols * (rank + 1) / split);
-  const int ncols = cend - cbeg;
-  for (int idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
-    const int b = idx / ncols, c = cbeg + idx % ncols;
-    const uint32_t col = pband * 8 + c;
-    const float* rp =
-        red + ((size_t)(c / kDecTileCols) * XB + b) * kDecTileCols + (c % kDecTileCols);
+  for (uint32_t idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
+    const uint32_t row = idx / ncols, c = idx - row * ncols;
+    const uint32_t col = pband * 8 + rank * ncols + c;
     float v = 0.f;
-    if (split > 1) {
-      // every remote load first, then the sum in a fixed order
-      const uint32_t a = smem_u32(rp);
-      float part[16];
-#pragma unroll
-      for (uint32_t q = 0; q < 16; ++q)
-        part[q] = q < split ? ld_shared_cluster_f32(map_shared_rank(a, q)) : 0.f;
-#pragma unroll
-      for (uint32_t q = 0; q < 16; ++q) v += part[q];
-    } else {
-      v = *rp;
-    }
+    for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
     if (col < n) {
       if (bias) v += DType<DT>::to_f32(bias[col]);
-      out[(size_t)b * ld_out + col] = DType<ODT>::from_f32(v);
+      out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
     }
   }
-  if (split > 1) cluster_sync_all();
 }
 
 // ------------------------------------------------------------------ host
