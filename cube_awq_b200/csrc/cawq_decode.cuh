@@ -254,15 +254,22 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       woff[i] = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + r * 128 +
                 ((((bw >> 2) ^ (r & 7))) << 4) + ((bw & 3) << 2);
     }
-    // X^T fragment of row 8m + gq: the k pairs (2t, 2t+1) and (2t+8, 2t+9) of a
-    // step are adjacent in the 128B-swizzled X tile, so each is one load.
-    uint32_t xrow[MT];  // byte offset of the row
-    uint32_t x7[MT];    // its swizzle phase
+    // X^T fragments. 16-bit X: one ldmatrix.x4 per 8-row block of X loads the
+    // fragments of two steps; lane L gives the address of row 8m + (L & 7),
+    // 16-byte k chunk 4p + (L >> 3) of step pair p, under the tile's 128-byte
+    // swizzle. f32 X: each k pair is loaded directly and split into bf16 hi/lo.
+    uint32_t xrow[MT];    // byte offset of row 8m + gq (f32 X)
+    uint32_t x7[MT];      // its swizzle phase
+    uint32_t xld[MT][2];  // ldmatrix row addresses, step pairs 0 and 1 (16-bit X)
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       const int xr = 8 * m + gq;
       xrow[m] = xr * 128;
       x7[m] = static_cast<uint32_t>(xr & 7);
+      const int lr = lane & 7, li = lane >> 3;
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+        xld[m][p] = static_cast<uint32_t>((8 * m + lr) * 128 + (((4 * p + li) ^ lr) << 4));
     }
     // scales of this lane's 8 columns and its zero word inside the stage rows
     const uint32_t s_lane = (uint32_t)(strip * kDecTileCols + 8 * word) * (uint32_t)sizeof(T);
@@ -281,8 +288,13 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     }
 
     // tot += s' * (D - c' * sum_k x) with this group's scales / zeros from the
-    // stage's shared-memory rows, then D = 0 (see the file comment)
-    auto fold = [&](const uint8_t* srow, const uint8_t* zrow) {
+    // stage's shared-memory rows (see the file comment). c' = offset + zero is
+    // built by the same magic-number lop3 as the weights: for f16 the lo
+    // nibble gives 1024 + z and the hi nibble, in place, 1024 + 16 z; for
+    // bf16 both give 128 + z. With `clear` the accumulators restart at 0;
+    // else the next group's first MMA overwrites them.
+    auto fold = [&](const uint8_t* srow, const uint8_t* zrow, auto clear_tag) {
+      constexpr bool kClear = decltype(clear_tag)::value;
       float s_reg[8];
       if constexpr (DT == kF32) {
 #pragma unroll
@@ -298,64 +310,91 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         for (int c = 0; c < 8; ++c) s_reg[c] = DType<DT>::to_f32(h[c]);
       }
       const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + z_lane);
+      float cz[8];  // c' of nibble p of zw
+      if constexpr (kF16Mma) {
+        const uint32_t z8 = zw >> 8;
+        const uint32_t q[4] = {lop3_and_or(zw, 0x000F000Fu, 0x64006400u),   // nibbles 0, 4
+                               lop3_and_or(zw, 0x00F000F0u, 0x64006400u),   // 1, 5 (x16)
+                               lop3_and_or(z8, 0x000F000Fu, 0x64006400u),   // 2, 6
+                               lop3_and_or(z8, 0x00F000F0u, 0x64006400u)};  // 3, 7 (x16)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[i]));
+          cz[i] = f.x;
+          cz[i + 4] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t q = lop3_and_or(zw >> (4 * i), 0x000F000Fu, 0x43004300u);
+          cz[i] = __uint_as_float(q << 16);             // nibble i
+          cz[i + 4] = __uint_as_float(q & 0xFFFF0000u);  // nibble i + 4
+        }
+      }
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        // nibble -> float by the 2^23 exponent trick (no integer conversion)
-        const float zl = __uint_as_float(0x4B000000u | ((zw >> (8 * b)) & 15u)) - 8388608.f;
-        const float zh = __uint_as_float(0x4B000000u | ((zw >> (8 * b + 4)) & 15u)) - 8388608.f;
         const float sl = s_reg[col_of_nibble(2 * b, ORDER)];
         float sh = s_reg[col_of_nibble(2 * b + 1, ORDER)];
-        float cl, ch;
-        if constexpr (kF16Mma) {
-          cl = 1024.f + zl;
-          ch = fmaf(16.f, zh, 1024.f);
-          sh *= 0.0625f;
-        } else {
-          cl = 128.f + zl;
-          ch = 128.f + zh;
-        }
+        if constexpr (kF16Mma) sh *= 0.0625f;  // the hi nibble entered the MMA as 16 q
+        const float cl = cz[2 * b], ch = cz[2 * b + 1];
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           tot[m][b][0] = fmaf(sl, fmaf(-cl, Dx[m][0], D[m][b][0]), tot[m][b][0]);
           tot[m][b][1] = fmaf(sl, fmaf(-cl, Dx[m][1], D[m][b][1]), tot[m][b][1]);
           tot[m][b][2] = fmaf(sh, fmaf(-ch, Dx[m][0], D[m][b][2]), tot[m][b][2]);
           tot[m][b][3] = fmaf(sh, fmaf(-ch, Dx[m][1], D[m][b][3]), tot[m][b][3]);
-          D[m][b][0] = D[m][b][1] = D[m][b][2] = D[m][b][3] = 0.f;
+          if constexpr (kClear) D[m][b][0] = D[m][b][1] = D[m][b][2] = D[m][b][3] = 0.f;
         }
       }
+      if constexpr (kClear) {
 #pragma unroll
-      for (int m = 0; m < MT; ++m)
+        for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) Dx[m][e] = 0.f;
+          for (int e = 0; e < 4; ++e) Dx[m][e] = 0.f;
+      }
     };
 
-    // one 16-row step: X fragments, the ones MMA, dequantize and multiply
-    auto step_mma = [&](const uint8_t* sbase, int s) {
-      uint32_t wv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        wv[i] = *reinterpret_cast<const uint32_t*>(sbase + woff[i] + s * 2048);
-      uint32_t bh[MT][2], bl[MT][2];
+    // D += A B, or D = A B when the tag says this is a group's first step
+    auto mma = [&](float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                   uint32_t b0, uint32_t b1, auto zero_tag) {
+      if constexpr (decltype(zero_tag)::value) {
+        mma_16816_c0<!kF16Mma>(d, a0, a1, a2, a3, b0, b1);
+      } else {
+        mma_16816<!kF16Mma>(d, a0, a1, a2, a3, b0, b1);
+      }
+    };
+
+    // f32 X: the step's fragments, as bf16 hi and lo parts
+    auto x_frags_f32 = [&](const uint8_t* sbase, int s, uint32_t (&bh)[MT][2],
+                           uint32_t (&bl)[MT][2]) {
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          if constexpr (DT == kF32) {
-            // two 32-k boxes; k = 16s + 8h2 + 2t lies in box s >> 1
-            const uint32_t ch2 = (uint32_t)(4 * (s & 1) + 2 * h2 + (t >> 1));
-            const float2 xv = *reinterpret_cast<const float2*>(
-                sbase + (s >> 1) * XB * 128 + xrow[m] + ((ch2 ^ x7[m]) << 4) + 8 * (t & 1));
-            const __nv_bfloat162 hi = __floats2bfloat162_rn(xv.x, xv.y);
-            const __nv_bfloat162 lo =
-                __floats2bfloat162_rn(xv.x - __low2float(hi), xv.y - __high2float(hi));
-            bh[m][h2] = *reinterpret_cast<const uint32_t*>(&hi);
-            bl[m][h2] = *reinterpret_cast<const uint32_t*>(&lo);
-          } else {
-            bh[m][h2] = *reinterpret_cast<const uint32_t*>(
-                sbase + xrow[m] + ((((uint32_t)(2 * s + h2)) ^ x7[m]) << 4) + 4 * t);
-          }
+          // two 32-k boxes; k = 16s + 8h2 + 2t lies in box s >> 1
+          const uint32_t ch2 = (uint32_t)(4 * (s & 1) + 2 * h2 + (t >> 1));
+          const float2 xv = *reinterpret_cast<const float2*>(
+              sbase + (s >> 1) * XB * 128 + xrow[m] + ((ch2 ^ x7[m]) << 4) + 8 * (t & 1));
+          const __nv_bfloat162 hi = __floats2bfloat162_rn(xv.x, xv.y);
+          const __nv_bfloat162 lo =
+              __floats2bfloat162_rn(xv.x - __low2float(hi), xv.y - __high2float(hi));
+          bh[m][h2] = *reinterpret_cast<const uint32_t*>(&hi);
+          bl[m][h2] = *reinterpret_cast<const uint32_t*>(&lo);
         }
-        mma_16816<!kF16Mma>(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1]);
+      }
+    };
+
+    // one 16-row step with X^T fragments bh (and the bf16 lo parts bl of f32 X):
+    // the ones MMA, dequantize and multiply
+    auto step_mma = [&](const uint8_t* sbase, int s, const uint32_t (&bh)[MT][2],
+                        const uint32_t (&bl)[MT][2], auto zero_tag) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        wv[i] = *reinterpret_cast<const uint32_t*>(sbase + woff[i] + s * 2048);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        mma(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1], zero_tag);
         if constexpr (DT == kF32)
           mma_16816<true>(Dx[m], kOnes, kOnes, kOnes, kOnes, bl[m][0], bl[m][1]);
       }
@@ -377,8 +416,37 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          mma_16816<!kF16Mma>(D[m][b], a0, a1, a2, a3, bh[m][0], bh[m][1]);
+          mma(D[m][b], a0, a1, a2, a3, bh[m][0], bh[m][1], zero_tag);
           if constexpr (DT == kF32) mma_16816<true>(D[m][b], a0, a1, a2, a3, bl[m][0], bl[m][1]);
+        }
+      }
+    };
+
+    // the four steps of a stage (the first one restarts the accumulators if
+    // zero_tag says a group starts here)
+    auto stage_mma = [&](const uint8_t* sbase, auto zero_tag) {
+      using NoZero = std::integral_constant<bool, false>;
+      uint32_t bh[MT][2], bl[MT][2], bh2[MT][2];
+      if constexpr (DT == kF32) {
+        x_frags_f32(sbase, 0, bh, bl);
+        step_mma(sbase, 0, bh, bl, zero_tag);
+#pragma unroll
+        for (int st = 1; st < 4; ++st) {
+          x_frags_f32(sbase, st, bh, bl);
+          step_mma(sbase, st, bh, bl, NoZero{});
+        }
+      } else {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            ldmatrix_x4(smem_u32(sbase) + xld[m][p], bh[m][0], bh[m][1], bh2[m][0], bh2[m][1]);
+          if (p == 0) {
+            step_mma(sbase, 0, bh, bl, zero_tag);
+          } else {
+            step_mma(sbase, 2, bh, bl, NoZero{});
+          }
+          step_mma(sbase, 2 * p + 1, bh2, bl, NoZero{});
         }
       }
     };
@@ -395,10 +463,15 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         ok = __all_sync(0xffffffffu, ok);  // keep the warp convergent
         if (!ok) break;
         const uint8_t* sbase = smem + sl * slot;
-#pragma unroll
-        for (int st = 0; st < 4; ++st) step_mma(sbase, st);
+        // a group's first stage (not the CTA's first: D starts at 0 there)
+        if (in_grp == 0 && j > 0) {
+          stage_mma(sbase, std::integral_constant<bool, true>{});
+        } else {
+          stage_mma(sbase, std::integral_constant<bool, false>{});
+        }
         if (++in_grp == spgs || j + 1 == nst) {
-          fold(sbase + L::s_off(strips), sbase + L::z_off(strips, g));
+          fold(sbase + L::s_off(strips), sbase + L::z_off(strips, g),
+               std::integral_constant<bool, false>{});
           in_grp = 0;
         }
         __syncwarp();
@@ -410,6 +483,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       }
     } else {
       // any g % 16 == 0: group boundaries tracked per step, without division
+      using NoZero = std::integral_constant<bool, false>;
       const uint32_t spg = g >> 4;  // 16-row steps per quantization group
       uint32_t grp = (c_beg * 4) / spg;
       uint32_t grp_end = (grp + 1) * spg;  // first step of the next group
@@ -419,16 +493,31 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         if (!ok) break;
         const uint8_t* sbase = smem + sl * slot;
         const uint32_t stage = c_beg + j;
+        uint32_t bh[MT][2], bl[MT][2], bh2[MT][2];
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           const uint32_t step = stage * 4 + st;
           if (step >= end_step) break;
-          step_mma(sbase, st);
+          if constexpr (DT == kF32) {
+            x_frags_f32(sbase, st, bh, bl);
+            step_mma(sbase, st, bh, bl, NoZero{});
+          } else {
+            if ((st & 1) == 0) {
+#pragma unroll
+              for (int m = 0; m < MT; ++m)
+                ldmatrix_x4(smem_u32(sbase) + xld[m][st >> 1], bh[m][0], bh[m][1], bh2[m][0],
+                            bh2[m][1]);
+              step_mma(sbase, st, bh, bl, NoZero{});
+            } else {
+              step_mma(sbase, st, bh2, bl, NoZero{});
+            }
+          }
           const uint32_t next = step + 1;
           if (next >= end_step || next >= grp_end) {
             const uint32_t r = grp - stage * kDecStageRows / g;  // scale row in this stage
             fold(sbase + L::s_off(strips) + r * L::s_row_bytes(strips),
-                 sbase + L::z_off(strips, g) + r * L::z_row_bytes(strips));
+                 sbase + L::z_off(strips, g) + r * L::z_row_bytes(strips),
+                 std::integral_constant<bool, true>{});
             grp += 1;
             grp_end += spg;
           }
@@ -667,19 +756,20 @@ cudaError_t launch_decode(const GemmProblem& p, const cawq_plan& plan, const Dev
 // plan.warps = 128-column strips per CTA (two consumer warps each),
 // plan.split = CTAs of a cluster splitting K, plan.stages = depth of the TMA ring.
 cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
+  // Measured on B200 over chains of cold launches (Llama-2-7B shapes): two
+  // strips per CTA, K split until there are about two CTAs per SM, and a
+  // 6-stage ring once a CTA has that many stages.
   cawq_plan plan = {};
   plan.path = CAWQ_PATH_DECODE;
-  plan.warps = 4;
+  plan.warps = 2;
   const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
-  const size_t strips_total = (p.n + kDecTileCols - 1) / kDecTileCols;
-  while (plan.warps > 2 && strips_total < (size_t)plan.warps * 8) plan.warps /= 2;
-  const size_t bands = (strips_total + plan.warps - 1) / plan.warps;
+  const size_t bands = (p.n + 2 * kDecTileCols - 1) / (2 * kDecTileCols);
   const size_t nst_total = (p.k / 16 + 3) / 4;
   int split = 1;
-  while (split < 16 && bands * split < sms && nst_total >= (size_t)split * 4) split *= 2;
+  while (split < 16 && bands * split < 2 * sms && nst_total >= (size_t)split * 8) split *= 2;
   plan.split = split;
   const size_t per_cta = (nst_total + split - 1) / split;
-  plan.stages = per_cta >= 4 ? 4 : (per_cta >= 2 ? 2 : 1);
+  plan.stages = per_cta >= 6 ? 6 : (per_cta >= 4 ? 4 : (per_cta >= 2 ? 2 : 1));
   while (plan.stages > 1 && !decode_supports(p, plan, dev)) --plan.stages;
   return plan;
 }
