@@ -109,6 +109,53 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+// ------------------------------------------------------- tensor maps
+namespace {
+struct TensorMapEntry {
+  const void* base = nullptr;
+  uint64_t inner = 0, outer = 0, row_bytes = 0;
+  uint32_t box_inner = 0, box_outer = 0;
+  int dt = -1, swz = -1;
+  alignas(64) CUtensorMap map;
+};
+constexpr int kTensorMapCache = 64;
+thread_local TensorMapEntry t_maps[kTensorMapCache];
+}  // namespace
+
+bool encode_tiled_2d(void* map, int cu_dtype, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, int cu_swizzle) {
+  const uint64_t h = (reinterpret_cast<uintptr_t>(base) >> 8) ^ (inner * 0x9E3779B97F4A7C15ull) ^
+                     (outer << 7) ^ ((uint64_t)box_outer << 3) ^ (uint64_t)cu_dtype;
+  TensorMapEntry& e = t_maps[(h ^ (h >> 29)) % kTensorMapCache];
+  if (e.base == base && e.inner == inner && e.outer == outer && e.row_bytes == row_bytes &&
+      e.box_inner == box_inner && e.box_outer == box_outer && e.dt == cu_dtype &&
+      e.swz == cu_swizzle) {
+    std::memcpy(map, &e.map, sizeof(CUtensorMap));
+    return true;
+  }
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const uint64_t dims[2] = {inner, outer};
+  const uint64_t strides[1] = {row_bytes};
+  const uint32_t box[2] = {box_inner, box_outer};
+  const uint32_t estr[2] = {1, 1};
+  const int r = fn(map, cu_dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   static_cast<int>(CU_TENSOR_MAP_INTERLEAVE_NONE), cu_swizzle,
+                   static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B),
+                   static_cast<int>(CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+  if (r != 0) return false;
+  e.base = base;
+  e.inner = inner;
+  e.outer = outer;
+  e.row_bytes = row_bytes;
+  e.box_inner = box_inner;
+  e.box_outer = box_outer;
+  e.dt = cu_dtype;
+  e.swz = cu_swizzle;
+  std::memcpy(&e.map, map, sizeof(CUtensorMap));
+  return true;
+}
+
 // --------------------------------------------------- reference rules
 static bool multiple_of(size_t a, size_t b) { return b == 0 ? a == 0 : a % b == 0; }
 

@@ -50,6 +50,12 @@ typedef int (*EncodeTiledFn)(void*, int, uint32_t, void*, const uint64_t*, const
                              const uint32_t*, const uint32_t*, int, int, int, int);
 EncodeTiledFn encode_tiled_fn();
 
+// cuTensorMapEncodeTiled of a 2-D row-major tensor into the 128-byte map at
+// `map` (no interleave, L2 promotion 256 B, no OOB fill), through a small
+// per-thread cache keyed by every argument (a hit yields the identical map).
+bool encode_tiled_2d(void* map, int cu_dtype, const void* base, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, int cu_swizzle);
+
 // ---------------------------------------------------------- launchers
 // Each returns cudaSuccess or the launch error. `supports` functions say
 // whether a plan can run a problem (shape, dtype and alignment).

@@ -427,16 +427,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 static bool pf_encode(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
                       uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
                       CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = encode_tiled_fn();
-  if (!fn) return false;
-  const uint64_t dims[2] = {inner, outer};
-  const uint64_t strides[1] = {row_bytes};
-  const uint32_t box[2] = {box_inner, box_outer};
-  const uint32_t estr[2] = {1, 1};
-  return fn(map, static_cast<int>(dt), 2, const_cast<void*>(base), dims, strides, box, estr,
-            static_cast<int>(CU_TENSOR_MAP_INTERLEAVE_NONE), static_cast<int>(swz),
-            static_cast<int>(CU_TENSOR_MAP_L2_PROMOTION_L2_256B),
-            static_cast<int>(CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)) == 0;
+  return encode_tiled_2d(map, static_cast<int>(dt), base, inner, outer, row_bytes, box_inner,
+                         box_outer, static_cast<int>(swz));
 }
 
 bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {

@@ -248,6 +248,65 @@ def gemm(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: t
     return out
 
 
+class PreparedWeights:
+    """Validated weights of one layer and the constant part of its cawq_gemm
+    call, so a forward pass only checks the input and makes one C call. It
+    holds the tensors it was made from (``matches`` compares identity)."""
+
+    __slots__ = ("qweight", "qzeros", "scales", "bias", "k", "n", "group_size", "dtype",
+                 "code", "order", "ptrs", "device")
+
+    def __init__(self, qweight, qzeros, scales, group_size, bias=None, order="awq"):
+        _require_cuda(qweight, qzeros, scales, bias)
+        for name, t in (("qweight", qweight), ("qzeros", qzeros), ("scales", scales),
+                        ("bias", bias)):
+            if t is not None and not t.is_contiguous():
+                raise ShapeError(f"{name} must be contiguous", _lib.CAWQ_ERR_INVALID_SHAPE)
+        if qweight.dtype not in _PACKED:
+            raise DTypeError("qweight must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+        if qzeros.dtype not in _PACKED:
+            raise DTypeError("qzeros must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+        if bias is not None and bias.dtype != scales.dtype:
+            raise DTypeError("scales and bias must have the input's float dtype (F)",
+                             _lib.CAWQ_ERR_DTYPE)
+        k, n = qweight.shape[0], qweight.shape[1] * 8
+        groups = scales.shape[0]
+        if groups == 0 or k % groups != 0 or qzeros.shape[0] != groups or \
+                scales.shape[1] != n or qzeros.shape[1] * 8 != n:
+            raise ShapeError("qzeros must be [K/g, N/8] and scales [K/g, N]",
+                             _lib.CAWQ_ERR_INVALID_SHAPE)
+        if group_size * groups != k:
+            raise ShapeError("group_size must equal K / scales rows", _lib.CAWQ_ERR_INVALID_SHAPE)
+        self.qweight, self.qzeros, self.scales, self.bias = qweight, qzeros, scales, bias
+        self.k, self.n, self.group_size = k, n, group_size
+        self.dtype, self.code, self.order = scales.dtype, cawq_dtype(scales.dtype), _order(order)
+        self.ptrs = (qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+                     bias.data_ptr() if bias is not None else None)
+        self.device = scales.device
+
+    def matches(self, qweight, qzeros, scales, bias) -> bool:
+        return (self.qweight is qweight and self.qzeros is qzeros and self.scales is scales and
+                self.bias is bias)
+
+
+def gemm_prepared(w: PreparedWeights, x: torch.Tensor) -> torch.Tensor:
+    """cawq_gemm with prepared weights: x [rows, K] (contiguous, F) -> [rows, N]."""
+    if x.dtype != w.dtype:
+        raise DTypeError("scales and bias must have the input's float dtype (F)",
+                         _lib.CAWQ_ERR_DTYPE)
+    if not x.is_cuda:
+        _require_cuda(x)
+    rows, k = x.shape
+    if k != w.k:
+        raise ShapeError("input last dim (K) must match qweight rows", _lib.CAWQ_ERR_INVALID_SHAPE)
+    out = torch.empty((rows, w.n), dtype=w.dtype, device=x.device)
+    qw, qz, sc, b = w.ptrs
+    check(_lib.lib().cawq_gemm(x.data_ptr(), qw, qz, sc, b, out.data_ptr(), rows, k, w.n,
+                               w.group_size, w.code, w.code, w.order, w.n,
+                               torch.cuda.current_stream(x.device).cuda_stream))
+    return out
+
+
 def _plan_c(plan: dict) -> _lib.PlanC:
     p = _lib.PlanC()
     p.path = int(plan.get("path", 0))

@@ -18,7 +18,7 @@ import torch
 
 from . import _lib
 from .errors import CubeAwqError, DTypeError, ShapeError
-from .kernel import _PACKED, dequantize_awq, gemm
+from .kernel import PreparedWeights, dequantize_awq, gemm, gemm_prepared
 
 AWQ_PACK_FACTOR = 8  # awq_gemm.rs:12
 TILE_N_BASE = 32     # awq_gemm.rs:13
@@ -71,6 +71,7 @@ class AWQGEMMLinear:
         self.qzeros = qzeros
         self.scales = scales
         self.bias = bias
+        self._prep = None  # validated call arguments (re-made when a tensor is replaced)
 
     def group_size(self) -> int:
         """awq_gemm.rs:136-140: K / scale rows."""
@@ -87,12 +88,11 @@ class AWQGEMMLinear:
         if not x.is_contiguous():
             x = x.contiguous()
         _shape_assert(k == self.qweight.shape[0], "input last dim (K) must match qweight rows")
-        if self.qweight.dtype not in _PACKED:
-            raise DTypeError("qweight must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
-        if self.qzeros.dtype not in _PACKED:
-            raise DTypeError("qzeros must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
-        out = gemm(x, self.qweight, self.qzeros, self.scales, self.group_size(), bias=self.bias,
-                   order="awq")
+        w = self._prep
+        if w is None or not w.matches(self.qweight, self.qzeros, self.scales, self.bias):
+            w = self._prep = PreparedWeights(self.qweight, self.qzeros, self.scales,
+                                             self.group_size(), bias=self.bias, order="awq")
+        out = gemm_prepared(w, x)
         return out.reshape(*input.shape[:-1], out.shape[-1])
 
     __call__ = forward
@@ -130,6 +130,7 @@ class AWQLinear:
         self.qweight = qweight
         self.qzeros = qzeros
         self.scales = scales
+        self._prep = None  # validated call arguments (re-made when a tensor is replaced)
 
     def group_size(self) -> int:
         """awq_dequantize.rs:52-56: K / scale rows."""
@@ -152,6 +153,10 @@ class AWQLinear:
                 f"RankMismatch: AWQLinear.forward takes a rank-2 [M, K] input, got rank {input.dim()}",
                 _lib.CAWQ_ERR_INVALID_SHAPE)
         x = input if input.is_contiguous() else input.contiguous()
-        return gemm(x, self.qweight, self.qzeros, self.scales, self.group_size(), order="natural")
+        w = self._prep
+        if w is None or not w.matches(self.qweight, self.qzeros, self.scales, None):
+            w = self._prep = PreparedWeights(self.qweight, self.qzeros, self.scales,
+                                             self.group_size(), order="natural")
+        return gemm_prepared(w, x)
 
     __call__ = forward

@@ -265,3 +265,23 @@ def test_prefill_is_deterministic_at_full_size(cuda_device, dtype):
     torch.cuda.synchronize()
     rel = (y0.float() - yg.float()).abs().max() / yg.float().abs().max()
     assert float(rel) <= GEMM_TOL["f16" if dtype == torch.float16 else "bf16"]
+
+
+def test_module_sees_replaced_weights(cuda_device):
+    # AWQGEMMLinear keeps its validated call arguments between forwards; a
+    # tensor assigned to the layer afterwards must be used by the next call.
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    x, qw, qz, s, b = random_awq(512, 256, 128, "f16", 3, seed=51)
+    _, qw2, qz2, s2, _ = random_awq(512, 256, 128, "f16", 3, seed=52)
+    layer = cawq.AWQGEMMLinear(t(qw, "u32"), t(qz, "u32"), t(s, "f16"))
+    xt = t(x, "f16")
+    y1 = layer.forward(xt)
+    layer.qweight, layer.qzeros, layer.scales = t(qw2, "u32"), t(qz2, "u32"), t(s2, "f16")
+    y2 = layer.forward(xt)
+    layer.bias = t(b, "f16")
+    y3 = layer.forward(xt)
+    torch.cuda.synchronize()
+    for got, (w_, z_, s_, b_) in ((y1, (qw, qz, s, None)), (y2, (qw2, qz2, s2, None)),
+                                  (y3, (qw2, qz2, s2, b))):
+        ref = oracle.gemm_f64(x, w_, z_, s_, 128, bias=b_, dtype="f16", deq_round=False)
+        assert max_rel_err(got.float().cpu().numpy(), ref) <= GEMM_TOL["f16"]
