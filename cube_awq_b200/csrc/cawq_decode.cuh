@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   // Peers push into this CTA's receive buffer only after every CTA of the
   // cluster has passed this point (the matching wait precedes the pushes).
   if (split > 1) cluster_arrive_release();
+  __shared__ int s_issued;  // stages whose copies the producer issued
 
   bool ok = true;
   if (warp == consumers) {
@@ -218,13 +219,16 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       for (int j = 0; j < pro; ++j) issue_weights(j);  // independent of earlier kernels
       pdl_wait();                                       // X may be the previous kernel's output
       for (int j = 0; j < pro; ++j) issue_x(j);
+      int issued = pro;
       for (int j = pro; j < nst && ok; ++j) {
         const int sl = j % NS;
         ok = mbar_wait_bounded(&empty[sl], static_cast<uint32_t>(((j / NS) - 1) & 1));
         if (!ok) break;
         issue_weights(j);
         issue_x(j);
+        issued = j + 1;
       }
+      s_issued = issued;
     }
     __syncwarp();
     // all loads issued: the next kernel in the stream may start its prologue
@@ -532,6 +536,19 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     }
   }
 
+  // Before exiting, no copy this CTA issued may still be writing its shared
+  // memory. Normally every issued stage has been consumed; after a timed-out
+  // wait, wait (bounded) for the last stage issued into each slot.
+  auto drain = [&]() {
+    if (!__syncthreads_or(ok ? 0 : 1)) return;
+    if (threadIdx.x == 0) {
+      const int issued = s_issued;
+      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+        mbar_wait_bounded(&full[j % NS], static_cast<uint32_t>((j / NS) & 1));
+    }
+    __syncthreads();
+  };
+
   // ---- split-K sums. CTA q of the cluster owns columns [q ncols, (q+1) ncols)
   // of the band: every CTA stores its partial sums of those columns into
   // slot [its rank] of q's receive buffer (st.async to distributed shared
@@ -561,6 +578,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         }
       }
     }
+    drain();
     return;
   }
   cluster_wait_acquire();  // every peer's recv_bar is initialised
@@ -606,6 +624,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
     }
   }
+  drain();
 }
 
 // ------------------------------------------------------------------ host

@@ -200,7 +200,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bready = empty_w + kPfWStages;
   uint64_t* bempty = bready + kPfBStages;
   uint64_t* acc_full = bempty + kPfBStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* drain_bar = acc_full + 1;  // the MMA thread's own MMAs, on a failed run
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  __shared__ int s_x_issued, s_w_issued;  // stages each producer issued
+  bool role_ok = true;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -226,6 +229,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&bempty[s], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(drain_bar, 1);
     fence_mbarrier_init();
     fence_proxy_async_smem();
     tma_prefetch_desc(&tm_x);
@@ -241,19 +245,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ------------------------------------------------- X ring producer
     if (lane == 0) {
       bool ok = true;
+      int issued = 0;
       for (int kt = 0; kt < KT && ok; ++kt) {
         const int s = kt % kPfXStages, u = kt / kPfXStages;
         if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         mbar_arrive_expect_tx(&full_x[s], L::kX);
         tma_load_2d(x_slot(s), &tm_x, kt * kPfBK, static_cast<int>(m0), &full_x[s]);
+        issued = kt + 1;
       }
+      s_x_issued = issued;
+      role_ok = ok;
     }
     __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------------- W ring producer
     if (lane == 0) {
       bool ok = true;
+      int issued = 0;
       for (int kt = 0; kt < KT && ok; ++kt) {
         const int s = kt % kPfWStages, u = kt / kPfWStages;
         if (u > 0) ok = mbar_wait_bounded(&empty_w[s], (uint32_t)((u - 1) & 1));
@@ -264,7 +273,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tma_load_2d(b, &tm_w, static_cast<int>(n0 / 8), kt * kPfBK, &full_w[s]);
         tma_load_2d(b + L::kW, &tm_s, static_cast<int>(n0), grp, &full_w[s]);
         tma_load_2d(b + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp, &full_w[s]);
+        issued = kt + 1;
       }
+      s_w_issued = issued;
+      role_ok = ok;
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -293,7 +305,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         umma_commit(&empty_x[sx]);
         umma_commit(&bempty[sb]);
       }
-      if (ok) umma_commit(acc_full);
+      if (ok) {
+        umma_commit(acc_full);
+      } else {
+        // wait (bounded) for the MMAs already issued before giving up
+        umma_commit(drain_bar);
+        mbar_wait_bounded(drain_bar, 0u);
+      }
+      role_ok = ok;
     }
     __syncwarp();
   } else {
@@ -366,6 +385,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // ---- epilogue: TMEM -> registers -> global
     if (ok) ok = mbar_wait_bounded(acc_full, 0u);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+    role_ok = ok;
     tc_fence_after();
     const int lq = warp & 3;      // TMEM lane quarter this warp may access
     // the warps of one lane quarter split the 16 chunks of 32 accumulator
@@ -414,6 +434,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
     }
+  }
+  // No copy this CTA issued may still be writing its shared memory when it
+  // exits: after a failed (timed-out) run, wait (bounded) for the last
+  // stage issued into each ring slot.
+  if (__syncthreads_or(role_ok ? 0 : 1) && threadIdx.x == 0) {
+    const int xi = s_x_issued, wi = s_w_issued;
+    for (int j = xi > kPfXStages ? xi - kPfXStages : 0; j < xi; ++j)
+      mbar_wait_bounded(&full_x[j % kPfXStages], (uint32_t)((j / kPfXStages) & 1));
+    for (int j = wi > kPfWStages ? wi - kPfWStages : 0; j < wi; ++j)
+      mbar_wait_bounded(&full_w[j % kPfWStages], (uint32_t)((j / kPfWStages) & 1));
   }
   tc_fence_before();
   __syncthreads();
