@@ -19,6 +19,13 @@ launches of one token, replayed as a CUDA graph.
            the measured HBM copy bandwidth of MEASURED_PEAKS.json
   prefill_m2048: BASELINE configs[2] at M = 2048 (f16), TFLOP/s per linear
            against the measured dense bf16 tensor peak
+  dequantize: the standalone dequantize kernel (natural order) on configs[0]
+           (4096 x 4096 -> f32) and configs[4] (8192 x 57344 -> f16): packed
+           bytes read + output written per us, against measured HBM
+  qwen2_m_sweep: BASELINE configs[3], Qwen2-7B linears at g = 64 over
+           M = 1 .. 4096 with the planner's default choice: us per layer
+           (4 linears) and the path taken, which locates the decode /
+           prefill crossover
   tp_llama3_70b_mlp: BASELINE configs[4], the Llama-3-70B MLP sharded over
            the job's GPUs (gate_up 8192->57344 column-parallel, down
            28672->8192 row-parallel with an fp32 NCCL all-reduce, through the
@@ -318,6 +325,8 @@ def run_ours(a, rank, local_rank, world):
             del g2
         extras["decode_sweep_m"] = sweep
         extras["prefill_m2048"] = prefill_numbers(a, dev, peaks)
+        extras["dequantize"] = dequant_numbers(dev, peaks)
+        extras["qwen2_m_sweep"] = qwen2_sweep(dev)
         extras["tp_llama3_70b_mlp"] = tp_mlp_numbers(dev, world, max_over_ranks)
 
     if world > 1:
@@ -399,6 +408,90 @@ def prefill_numbers(a, dev, peaks, reps=10, copies=3):
                      "path": plan["path"]}
         del g, ws
     return out
+
+
+def _graph_us(fn, reps, stream):
+    """Device time of one fn() replayed from a CUDA graph (us)."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    e1.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def dequant_numbers(dev, peaks, reps=20):
+    """Standalone dequantize (natural order): configs[0] to f32 and configs[4]
+    to f16. Bytes = packed weights + zeros + scales read + output written."""
+    import torch
+
+    import cube_awq_b200 as cawq
+    from cube_awq_b200 import synth
+    out = {}
+    stream = torch.cuda.Stream(dev)
+    for name, k, n, dt in (("cfg0_4096x4096_f32", 4096, 4096, torch.float32),
+                           ("cfg4_8192x57344_f16", 8192, 57344, torch.float16)):
+        w = synth.make_weights(k, n, GROUP, dt, dev, seed=700)
+        o = torch.empty(k, n, dtype=dt, device=dev)
+        us = _graph_us(lambda: cawq.dequantize_native(w.qweight, w.qzeros, w.scales, o, GROUP),
+                       reps, stream)
+        nbytes = w.nbytes() + k * n * o.element_size()
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 2), "gb_per_s": round(gbs, 1),
+                     "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                     "bytes": nbytes, "l2": "output larger than L2" if k * n * o.element_size()
+                     > 126e6 else "working set fits L2 (hot)"}
+        del w, o
+    return out
+
+
+def qwen2_sweep(dev, reps=10):
+    """Qwen2-7B AWQ linears, g = 64, f16, default plans; us per
+    layer (4 launches, graph-timed, 3 weight copies rotated) per M."""
+    import torch
+
+    import cube_awq_b200 as cawq
+    from cube_awq_b200 import synth
+    shapes = (("qkv", 3584, 4608), ("o_proj", 3584, 3584), ("gate_up", 3584, 37888),
+              ("down", 18944, 3584))
+    g, dt, copies = 64, torch.float16, 3
+    stream = torch.cuda.Stream(dev)
+    ws = {name: [synth.make_weights(k, n, g, dt, dev, seed=800 + 10 * j + c) for c in range(copies)]
+          for j, (name, k, n) in enumerate(shapes)}
+    wbytes = sum(ws[name][0].nbytes() for name, _, _ in shapes)
+    res = {}
+    for m in (1, 2, 4, 8, 16, 64, 256, 1024, 4096):
+        xs = {name: synth.make_input(m, k, dt, dev, seed=850) for name, k, n in shapes}
+        ys = {name: torch.empty(m, n, dtype=dt, device=dev) for name, k, n in shapes}
+
+        def layer_steps():
+            for c in range(copies):
+                for name, k, n in shapes:
+                    w = ws[name][c]
+                    cawq.gemm(xs[name], w.qweight, w.qzeros, w.scales, g, out=ys[name])
+        us = _graph_us(layer_steps, reps, stream) / copies
+        flops = sum(2.0 * m * k * n for _, k, n in shapes)
+        paths = {name: cawq.plan_get(m, k, n, g, dt)["path"] for name, k, n in shapes}
+        res[str(m)] = {"us_per_layer": round(us, 2),
+                       "weight_gb_per_s": round(wbytes / (us * 1e-6) / 1e9, 1),
+                       "tflops": round(flops / (us * 1e-6) / 1e12, 1),
+                       "paths": sorted(set(paths.values()))}
+        del xs, ys
+    del ws
+    return res
 
 
 def tp_mlp_numbers(dev, world, max_over_ranks, reps=10):

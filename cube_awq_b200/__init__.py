@@ -26,7 +26,12 @@ from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
 import os as _os
 
 if _os.path.exists(_lib.LIB_PATH):
-    _lib.lib()  # load now; without the library every compute call raises (no CPU fallback)
+    try:
+        _lib.lib()  # load now; without the library every compute call raises (no CPU fallback)
+    except (OSError, AttributeError):
+        # a library from an older build: `python -m cube_awq_b200.build` must
+        # still be able to run; every compute call raises until it is rebuilt
+        pass
 
 __all__ = [
     "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
