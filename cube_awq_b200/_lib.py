@@ -45,8 +45,10 @@ EXPORTED = (
     "cawq_dequantize_native", "cawq_dequantize",
     "cawq_tp_column_shard", "cawq_tp_row_shard", "cawq_tp_interleave_columns",
     "cawq_tp_unique_id", "cawq_tp_init", "cawq_tp_destroy", "cawq_tp_info",
-    "cawq_gemm_colpar", "cawq_gemm_rowpar",
+    "cawq_gemm_colpar", "cawq_gemm_rowpar", "cawq_gemm_rowpar_noalloc",
 )
+
+CAWQ_ROWPAR_SCRATCH_FLOATS = 1 << 20
 
 CAWQ_TP_ID_BYTES = 128
 
@@ -146,6 +148,8 @@ def _declare(L) -> None:
     L.cawq_gemm_colpar.restype = st
     L.cawq_gemm_rowpar.argtypes = tp_args
     L.cawq_gemm_rowpar.restype = st
+    L.cawq_gemm_rowpar_noalloc.argtypes = tp_args[:7] + tp_args[8:]
+    L.cawq_gemm_rowpar_noalloc.restype = st
 
 
 def lib():

@@ -972,3 +972,42 @@ CAWQ_API cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x,
   if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
   return CAWQ_OK;
 }
+
+CAWQ_API cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const void* x,
+                                              const uint32_t* qweight, const uint32_t* qzeros,
+                                              const void* scales, const void* bias, void* out,
+                                              size_t rows, size_t k, size_t n, size_t group_size,
+                                              cawq_dtype dtype, void* stream) {
+  if (rows * n > CAWQ_ROWPAR_SCRATCH_FLOATS) {
+    return fail(CAWQ_ERR_INVALID_SHAPE,
+                fmt("rows * n = %zu exceeds the static scratch of %u floats "
+                    "(CAWQ_ROWPAR_SCRATCH_FLOATS); use cawq_gemm_rowpar with a workspace",
+                    rows * n, (unsigned)CAWQ_ROWPAR_SCRATCH_FLOATS));
+  }
+  cawq_status st = tp_check(comm);
+  if (st != CAWQ_OK) return st;
+  if (!valid_dtype(dtype)) return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
+  size_t k0 = 0, kl = 0;
+  if ((st = cawq_tp_row_shard(k, group_size, comm->world, comm->rank, &k0, &kl)) != CAWQ_OK)
+    return st;
+  if (rows == 0) return CAWQ_OK;
+  if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+  float* partial = nullptr;
+  cudaError_t e = rowpar_static_scratch(&partial);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (row-parallel scratch)");
+  st = gemm_common(x, qweight, qzeros, scales, nullptr, partial, rows, kl, n, group_size, dtype,
+                   CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
+  if (st != CAWQ_OK) return st;
+  const NcclApi& a = nccl();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ncclResult_t r = a.all_reduce(partial, partial, rows * n, ncclFloat32, ncclSum, comm->comm, s);
+  if (r == ncclInProgress) {
+    st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
+    if (st != CAWQ_OK) return st;
+  } else if (r != ncclSuccess) {
+    return nccl_fail(r, "ncclAllReduce");
+  }
+  e = launch_rowpar_finish(partial, bias, out, rows, n, dtype, s);
+  if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
+  return CAWQ_OK;
+}

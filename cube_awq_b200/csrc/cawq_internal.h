@@ -82,6 +82,9 @@ cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, s
                                       int world, size_t elem, cudaStream_t stream);
 cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* out, size_t rows,
                                  size_t n, int dtype, cudaStream_t stream);
+// Device address of the current device's static row-parallel scratch
+// (CAWQ_ROWPAR_SCRATCH_FLOATS floats).
+cudaError_t rowpar_static_scratch(float** ptr);
 
 cudaError_t read_device_error(uint32_t* word, int reset);
 

@@ -7,6 +7,8 @@
 //     full sum, as the single-device layer does).
 #pragma once
 
+#include <mutex>
+
 #include "cawq_common.cuh"
 
 namespace cawq {
@@ -83,6 +85,31 @@ cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* o
         n);
   }
   return cudaGetLastError();
+}
+
+// Fixed-size fp32 scratch of cawq_gemm_rowpar_noalloc: one per device,
+// part of the module image (no allocation at call time).
+static __device__ __align__(256) float g_rowpar_scratch[CAWQ_ROWPAR_SCRATCH_FLOATS];
+
+cudaError_t rowpar_static_scratch(float** ptr) {
+  // cudaGetSymbolAddress once per device, with that device current (the
+  // caller's current device: the communicator's).
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static float* cached[kMaxDevices] = {};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cached[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_rowpar_scratch);
+    if (e != cudaSuccess) return e;
+    cached[dev] = static_cast<float*>(p);
+  }
+  *ptr = cached[dev];
+  return cudaSuccess;
 }
 
 }  // namespace cawq

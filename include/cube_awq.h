@@ -348,6 +348,25 @@ cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint
                              void* out, float* partial, size_t rows, size_t k, size_t n,
                              size_t group_size, cawq_dtype dtype, void* stream);
 
+/*
+ * cawq_gemm_rowpar without any caller workspace and without allocating: the
+ * fp32 partial sums live in a fixed scratch array that is part of the
+ * library's device image, CAWQ_ROWPAR_SCRATCH_FLOATS floats (4 MiB) per
+ * device, so rows * n must not exceed it (else CAWQ_ERR_INVALID_SHAPE).
+ * No counterpart in the reference (which is single-device).
+ *   - Nothing in the scratch has to start at zero: the local GEMM writes
+ *     every one of the rows * n partial sums before the all-reduce reads them.
+ *   - One scratch per device: calls that overlap on a device (other streams,
+ *     or graphs replayed concurrently) race on it; order them.
+ * Other arguments and results are those of cawq_gemm_rowpar.
+ */
+#define CAWQ_ROWPAR_SCRATCH_FLOATS (1u << 20)
+cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const void* x,
+                                     const uint32_t* qweight, const uint32_t* qzeros,
+                                     const void* scales, const void* bias, void* out,
+                                     size_t rows, size_t k, size_t n, size_t group_size,
+                                     cawq_dtype dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
