@@ -430,7 +430,8 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     // zero_tag says a group starts here)
     auto stage_mma = [&](const uint8_t* sbase, auto zero_tag) {
       using NoZero = std::integral_constant<bool, false>;
-      uint32_t bh[MT][2], bl[MT][2], bh2[MT][2];
+      uint32_t bh[MT][2], bl[MT][2];
+      [[maybe_unused]] uint32_t bh2[MT][2];
       if constexpr (DT == kF32) {
         x_frags_f32(sbase, 0, bh, bl);
         step_mma(sbase, 0, bh, bl, zero_tag);
@@ -497,7 +498,8 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         if (!ok) break;
         const uint8_t* sbase = smem + sl * slot;
         const uint32_t stage = c_beg + j;
-        uint32_t bh[MT][2], bl[MT][2], bh2[MT][2];
+        uint32_t bh[MT][2], bl[MT][2];
+        [[maybe_unused]] uint32_t bh2[MT][2];
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           const uint32_t step = stage * 4 + st;

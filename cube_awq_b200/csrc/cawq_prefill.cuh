@@ -37,18 +37,20 @@
 
 namespace cawq {
 
-constexpr int kPfBM = 256;   // two 128-row MMA halves
 constexpr int kPfBN = 256;
 constexpr int kPfBK = 64;
 constexpr int kPfXStages = 3;
 constexpr int kPfWStages = 4;
 constexpr int kPfBStages = 2;
-constexpr int kPfTmemCols = 2 * kPfBN;
 constexpr int kPfDqWarps = 8;                       // dequant / epilogue warps
 constexpr int kPfThreads = 96 + 32 * kPfDqWarps;    // + X producer, MMA, W producer
+constexpr int kPfMaxSplit = 8;                      // CTAs of a cluster splitting K
 
+// HALVES = 128-row MMA halves per CTA tile (1 or 2)
+template <int HALVES>
 struct PrefillLayout {
-  static constexpr int kX = kPfBM * kPfBK * 2;      // 32768 (two 16 KB halves)
+  static constexpr int kBM = 128 * HALVES;
+  static constexpr int kX = kBM * kPfBK * 2;        // 16 KB per half
   static constexpr int kB = kPfBK * kPfBN * 2;      // 32768
   static constexpr int kW = kPfBK * kPfBN / 8 * 4;  // 8192
   static constexpr int kS = kPfBN * 2;              // 512
@@ -182,14 +184,16 @@ __device__ __forceinline__ void pf_pairs(uint32_t q, uint32_t (&t)[4]) {
   }
 }
 
-template <int DT, int ODT, int ORDER>
+template <int DT, int ODT, int ORDER, int HALVES>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                    const typename DType<DT>::T* __restrict__ bias,
                    typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
-                   uint32_t g, uint32_t ld_out) {
-  using L = PrefillLayout;
+                   uint32_t g, uint32_t ld_out, uint32_t split) {
+  using L = PrefillLayout<HALVES>;
+  constexpr int BM = L::kBM;
+  constexpr uint32_t kTmemCols = HALVES * kPfBN;
   using H = PfHalf2<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -201,15 +205,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bempty = bready + kPfBStages;
   uint64_t* acc_full = bempty + kPfBStages;
   uint64_t* drain_bar = acc_full + 1;  // the MMA thread's own MMAs, on a failed run
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* recv_bar = drain_bar + 1;  // split K: the peers' partial sums have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   __shared__ int s_x_issued, s_w_issued;  // stages each producer issued
   bool role_ok = true;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t n0 = blockIdx.x * kPfBN;
-  const uint32_t m0 = blockIdx.y * kPfBM;
+  const uint32_t m0 = blockIdx.y * BM;
+  // split K: the `split` CTAs of a cluster (along z) share one output tile;
+  // CTA `rank` runs k-stages [kt0, kt0 + KTL)
+  const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
   const int KT = static_cast<int>(k / kPfBK);
+  const int kt0 = static_cast<int>((uint64_t)KT * rank / split);
+  const int KTL = static_cast<int>((uint64_t)KT * (rank + 1) / split) - kt0;
+  const int rpo = BM / static_cast<int>(split);  // rows of the tile each CTA sums
 
   auto x_slot = [&](int s) { return smem + (size_t)s * L::kX; };
   auto b_slot = [&](int s) { return smem + L::kOffB + (size_t)s * L::kB; };
@@ -230,12 +241,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(recv_bar, 1);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rpo * kPfBN * 4);
     fence_mbarrier_init();
     fence_proxy_async_smem();
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kPfTmemCols);
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -246,13 +259,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (lane == 0) {
       bool ok = true;
       int issued = 0;
-      for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % kPfXStages, u = kt / kPfXStages;
+      for (int i = 0; i < KTL && ok; ++i) {
+        const int s = i % kPfXStages, u = i / kPfXStages;
         if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         mbar_arrive_expect_tx(&full_x[s], L::kX);
-        tma_load_2d(x_slot(s), &tm_x, kt * kPfBK, static_cast<int>(m0), &full_x[s]);
-        issued = kt + 1;
+        tma_load_2d(x_slot(s), &tm_x, (kt0 + i) * kPfBK, static_cast<int>(m0), &full_x[s]);
+        issued = i + 1;
       }
       s_x_issued = issued;
       role_ok = ok;
@@ -263,8 +276,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (lane == 0) {
       bool ok = true;
       int issued = 0;
-      for (int kt = 0; kt < KT && ok; ++kt) {
-        const int s = kt % kPfWStages, u = kt / kPfWStages;
+      for (int i = 0; i < KTL && ok; ++i) {
+        const int kt = kt0 + i;
+        const int s = i % kPfWStages, u = i / kPfWStages;
         if (u > 0) ok = mbar_wait_bounded(&empty_w[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         uint8_t* b = w_slot(s);
@@ -273,7 +287,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tma_load_2d(b, &tm_w, static_cast<int>(n0 / 8), kt * kPfBK, &full_w[s]);
         tma_load_2d(b + L::kW, &tm_s, static_cast<int>(n0), grp, &full_w[s]);
         tma_load_2d(b + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp, &full_w[s]);
-        issued = kt + 1;
+        issued = i + 1;
       }
       s_w_issued = issued;
       role_ok = ok;
@@ -282,9 +296,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, kPfBM / 2, kPfBN);
+      constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, 128, kPfBN);
       bool ok = true;
-      for (int kt = 0; kt < KT && ok; ++kt) {
+      for (int kt = 0; kt < KTL && ok; ++kt) {
         const int sx = kt % kPfXStages, ux = kt / kPfXStages;
         const int sb = kt % kPfBStages, ub = kt / kPfBStages;
         ok = mbar_wait_bounded(&full_x[sx], (uint32_t)(ux & 1)) &&
@@ -297,8 +311,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int j = 0; j < kPfBK / 16; ++j) {
           const uint64_t bd = umma_desc_sw128(ba + 2048 * j, 8192, 1024);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint64_t ad = umma_desc_sw128(xa + h * (L::kX / 2) + 32 * j, 16, 1024);
+          for (int h = 0; h < HALVES; ++h) {
+            const uint64_t ad = umma_desc_sw128(xa + h * (L::kX / HALVES) + 32 * j, 16, 1024);
             umma_f16(tmem + h * kPfBN, ad, bd, idesc, (kt > 0 || j > 0) ? 1u : 0u);
           }
         }
@@ -321,7 +335,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int q4 = lane >> 3;  // quarter of the warp -> row offset 2*q4
     const int l = lane & 7;    // packed word l + 8a, a = 0..3
     bool ok = true;
-    for (int kt = 0; kt < KT; ++kt) {
+    for (int kt = 0; kt < KTL; ++kt) {
       const int sw = kt % kPfWStages, uw = kt / kPfWStages;
       const int sb = kt % kPfBStages, ub = kt / kPfBStages;
       if (ok) ok = mbar_wait_bounded(&full_w[sw], (uint32_t)(uw & 1));
@@ -382,55 +396,130 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bready[sb]);
     }
-    // ---- epilogue: TMEM -> registers -> global
+    // ---- accumulators complete
     if (ok) ok = mbar_wait_bounded(acc_full, 0u);
     ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
     role_ok = ok;
     tc_fence_after();
-    const int lq = warp & 3;      // TMEM lane quarter this warp may access
-    // the warps of one lane quarter split the 16 chunks of 32 accumulator
-    // columns (8 per 128-row half)
-    constexpr int kChunks = 16 / (kPfDqWarps / 4);
+  }
+
+  // Split K: past this barrier every CTA of the cluster has finished its main
+  // loop (MMAs complete), so its rings may receive the peers' partial sums.
+  if (split > 1) {
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
+
+  if (warp >= 3) {
+    // ---- epilogue: TMEM -> registers (-> peers) -> global
+    const int dw = warp - 3;
+    const int lq = warp & 3;  // TMEM lane quarter this warp may access
+    // the warps of one lane quarter split the 32-column chunks of the tile
+    // (8 per 128-row half)
+    constexpr int kChunks = HALVES * 8 / (kPfDqWarps / 4);
     const int part = dw >> 2;
-    if (ok) {
+    const bool ok = role_ok;
+    auto store = [&](uint32_t row, uint32_t col0, float (&v)[32]) {
+      if (row >= rows || col0 >= n) return;
+      if (bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += DType<DT>::to_f32(bias[col0 + i]);
+      }
+      typename DType<ODT>::T* o = out + (size_t)row * ld_out + col0;
+      if constexpr (ODT == kF32) {
+        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = v[i];
+        }
+      } else {
+        using OT = typename DType<ODT>::T;
+        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 pk;
+            OT* hp = reinterpret_cast<OT*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) hp[e] = DType<ODT>::from_f32(v[i + e]);
+            *reinterpret_cast<uint4*>(o + i) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = DType<ODT>::from_f32(v[i]);
+        }
+      }
+    };
+    if (split == 1) {
+      if (ok) {
 #pragma unroll 1
-      for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
-        const int h = cc >> 3, c = cc & 7;
-        const uint32_t row = m0 + 128 * h + 32 * lq + lane;
-        float v[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
-        const uint32_t col0 = n0 + 32 * c;
-        if (row < rows && col0 < n) {
-          if (bias) {
+        for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
+          const int h = cc >> 3, c = cc & 7;
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
+          store(m0 + 128 * h + 32 * lq + lane, n0 + 32 * c, v);
+        }
+      }
+    } else {
+      // CTA q owns tile rows [q rpo, (q+1) rpo). Each CTA sends the rows it
+      // does not own to their owner (st.async into the owner's receive
+      // buffer [source slot][row][256 columns], which reuses its rings;
+      // counted on the owner's recv_bar), then sums its own rows over all
+      // CTAs in rank order (its own part read again from TMEM).
+      float* recv = reinterpret_cast<float*>(smem);
+      const uint32_t bar_local = smem_u32(recv_bar);
+      if (ok) {
+#pragma unroll 1
+        for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
+          const int h = cc >> 3, c = cc & 7;
+          const int r = 128 * h + 32 * lq + lane;  // tile row
+          const uint32_t q = static_cast<uint32_t>(r / rpo);
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
+          if (q != rank) {
+            const uint32_t slot_idx = rank < q ? rank : rank - 1;
+            const float* dst =
+                recv + ((size_t)slot_idx * rpo + (r - (int)q * rpo)) * kPfBN + 32 * c;
+            const uint32_t ra = map_shared_rank(smem_u32(dst), q);
+            const uint32_t rb = map_shared_rank(bar_local, q);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += DType<DT>::to_f32(bias[col0 + i]);
+            for (int i = 0; i < 32; i += 4) st_async_v4(ra + 4 * i, v[i], v[i + 1], v[i + 2], v[i + 3], rb);
           }
-          typename DType<ODT>::T* o = out + (size_t)row * ld_out + col0;
-          if constexpr (ODT == kF32) {
-            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+        }
+      }
+      const bool got = mbar_wait_bounded(recv_bar, 0u);
+      if (ok && __all_sync(0xffffffffu, got)) {
+#pragma unroll 1
+        for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
+          const int h = cc >> 3, c = cc & 7;
+          const int r = 128 * h + 32 * lq + lane;
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
+          if (static_cast<uint32_t>(r / rpo) != rank) continue;
+          float acc[32];
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          for (uint32_t src = 0; src < split; ++src) {
+            if (src == rank) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[i] += v[i];
             } else {
+              const uint32_t slot_idx = src < rank ? src : src - 1;
+              const float4* sp4 = reinterpret_cast<const float4*>(
+                  recv + ((size_t)slot_idx * rpo + (r - (int)rank * rpo)) * kPfBN + 32 * c);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = v[i];
-            }
-          } else {
-            using OT = typename DType<ODT>::T;
-            if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 pk;
-                OT* h = reinterpret_cast<OT*>(&pk);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) h[e] = DType<ODT>::from_f32(v[i + e]);
-                *reinterpret_cast<uint4*>(o + i) = pk;
+              for (int i = 0; i < 8; ++i) {
+                const float4 f = sp4[i];
+                acc[4 * i] += f.x;
+                acc[4 * i + 1] += f.y;
+                acc[4 * i + 2] += f.z;
+                acc[4 * i + 3] += f.w;
               }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = DType<ODT>::from_f32(v[i]);
             }
           }
+          store(m0 + r, n0 + 32 * c, acc);
         }
       }
     }
@@ -449,7 +538,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kPfTmemCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -461,30 +550,44 @@ static bool pf_encode(CUtensorMap* map, CUtensorMapDataType dt, const void* base
                          box_outer, static_cast<int>(swz));
 }
 
+// plan.warps = 128-row MMA halves per tile (1 or 2), plan.split = CTAs of a
+// cluster splitting K (1, 2, 4, 8; at most 4 with 2 halves, whose receive
+// buffers would not fit the rings otherwise).
+static int pf_halves(const cawq_plan& plan) { return plan.warps == 1 ? 1 : 2; }
+
+static size_t pf_smem(int halves) {
+  return halves == 1 ? PrefillLayout<1>::kSmem : PrefillLayout<2>::kSmem;
+}
+
 bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
-  (void)plan;
-  if (dev.cc_major != 10 || dev.smem_optin < PrefillLayout::kSmem) return false;
+  const int halves = pf_halves(plan);
+  if (plan.warps != 0 && plan.warps != 1 && plan.warps != 2) return false;
+  const int split = plan.split < 1 ? 1 : plan.split;
+  if (split > kPfMaxSplit || (split & (split - 1)) || (halves == 2 && split > 4)) return false;
+  if (dev.cc_major != 10 || dev.smem_optin < pf_smem(halves)) return false;
   if (p.dtype != kF16 && p.dtype != kBF16) return false;
   if (p.rows == 0 || p.k % kPfBK != 0 || p.g % kPfBK != 0 || p.k % p.g != 0 || p.n % 32 != 0)
     return false;
+  if ((size_t)split > p.k / kPfBK) return false;
   if (p.k >= (1ull << 31) || p.n >= (1ull << 31) || p.rows >= (1ull << 31) ||
       p.ld_out >= (1ull << 31))
     return false;
-  if ((p.rows + kPfBM - 1) / kPfBM > 65535) return false;
+  if ((p.rows + 128 * halves - 1) / (128 * halves) > 65535) return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
 }
 
-template <int DT, int ODT, int ORDER>
-static cudaError_t launch_prefill_t(const GemmProblem& p) {
+template <int DT, int ODT, int ORDER, int HALVES>
+static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
   using T = typename DType<DT>::T;
   using OT = typename DType<ODT>::T;
+  using L = PrefillLayout<HALVES>;
   const CUtensorMapDataType xdt =
       DT == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tx, tw, ts, tz;
   const uint64_t npk = p.n / 8, groups = p.k / p.g;
-  if (!pf_encode(&tx, xdt, p.x, p.k, p.rows, p.k * 2, kPfBK, kPfBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+  if (!pf_encode(&tx, xdt, p.x, p.k, p.rows, p.k * 2, kPfBK, L::kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !pf_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kPfBN / 8, kPfBK,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !pf_encode(&ts, xdt, p.sc, p.n, groups, p.n * 2, kPfBN, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -492,53 +595,96 @@ static cudaError_t launch_prefill_t(const GemmProblem& p) {
                  CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = prefill_kernel<DT, ODT, ORDER>;
+  auto kern = prefill_kernel<DT, ODT, ORDER, HALVES>;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(PrefillLayout::kSmem));
+                                         static_cast<int>(L::kSmem));
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  dim3 grid(static_cast<uint32_t>((p.n + kPfBN - 1) / kPfBN),
-            static_cast<uint32_t>((p.rows + kPfBM - 1) / kPfBM));
-  kern<<<grid, kPfThreads, PrefillLayout::kSmem, p.stream>>>(
-      tx, tw, ts, tz, static_cast<const T*>(p.bias), static_cast<OT*>(p.out),
-      static_cast<uint32_t>(p.rows), static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n),
-      static_cast<uint32_t>(p.g), static_cast<uint32_t>(p.ld_out));
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<uint32_t>((p.n + kPfBN - 1) / kPfBN),
+                     static_cast<uint32_t>((p.rows + L::kBM - 1) / L::kBM),
+                     static_cast<uint32_t>(split));
+  cfg.blockDim = dim3(kPfThreads);
+  cfg.dynamicSmemBytes = L::kSmem;
+  cfg.stream = p.stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (split > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = static_cast<unsigned>(split);
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, tz, static_cast<const T*>(p.bias),
+                            static_cast<OT*>(p.out), static_cast<uint32_t>(p.rows),
+                            static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n),
+                            static_cast<uint32_t>(p.g), static_cast<uint32_t>(p.ld_out),
+                            static_cast<uint32_t>(split));
 }
 
 template <int DT, int ODT>
-static cudaError_t launch_prefill_o(const GemmProblem& p) {
-  return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural>(p)
-                                  : launch_prefill_t<DT, ODT, kOrderAwq>(p);
+static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split) {
+  if (halves == 1) {
+    return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 1>(p, split)
+                                    : launch_prefill_t<DT, ODT, kOrderAwq, 1>(p, split);
+  }
+  return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 2>(p, split)
+                                  : launch_prefill_t<DT, ODT, kOrderAwq, 2>(p, split);
 }
 
-cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan&, const DeviceInfo&) {
+cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo&) {
+  const int halves = pf_halves(plan);
+  const int split = plan.split < 1 ? 1 : plan.split;
   if (p.dtype == kF16) {
-    return p.out_dtype == kF32 ? launch_prefill_o<kF16, kF32>(p) : launch_prefill_o<kF16, kF16>(p);
+    return p.out_dtype == kF32 ? launch_prefill_o<kF16, kF32>(p, halves, split)
+                               : launch_prefill_o<kF16, kF16>(p, halves, split);
   }
   if (p.dtype == kBF16) {
-    return p.out_dtype == kF32 ? launch_prefill_o<kBF16, kF32>(p)
-                               : launch_prefill_o<kBF16, kBF16>(p);
+    return p.out_dtype == kF32 ? launch_prefill_o<kBF16, kF32>(p, halves, split)
+                               : launch_prefill_o<kBF16, kBF16>(p, halves, split);
   }
   return cudaErrorNotSupported;
 }
 
-cawq_plan prefill_default_plan(const GemmProblem&, const DeviceInfo&) {
+// One 128-row half up to 128 rows, else two; split K over a cluster while the
+// tiles alone would leave more than half of the SMs idle.
+cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   cawq_plan pl = {};
   pl.path = CAWQ_PATH_PREFILL;
   pl.tile_n = kPfBN;
   pl.stages = kPfBStages;
+  pl.warps = p.rows <= 128 ? 1 : 2;
+  const size_t bm = 128 * (size_t)pl.warps;
+  const size_t tiles = ((p.n + kPfBN - 1) / kPfBN) * ((p.rows + bm - 1) / bm);
+  const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
+  const size_t kt = p.k / kPfBK;
+  const int max_split = pl.warps == 1 ? kPfMaxSplit : 4;
+  int split = 1;
+  while (split < max_split && tiles * split * 2 <= sms && kt >= (size_t)split * 2 * 4) split *= 2;
+  pl.split = split;
   return pl;
 }
 
 void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
                         int max_count) {
   int c = 0;
-  cawq_plan pl = prefill_default_plan(p, dev);
-  if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
+  for (int halves : {1, 2}) {
+    for (int split : {1, 2, 4, 8}) {
+      cawq_plan pl = {};
+      pl.path = CAWQ_PATH_PREFILL;
+      pl.tile_n = kPfBN;
+      pl.stages = kPfBStages;
+      pl.warps = halves;
+      pl.split = split;
+      if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
+    }
+  }
   *count = c;
 }
 

@@ -285,3 +285,34 @@ def test_module_sees_replaced_weights(cuda_device):
                                   (y3, (qw2, qz2, s2, b))):
         ref = oracle.gemm_f64(x, w_, z_, s_, 128, bias=b_, dtype="f16", deq_round=False)
         assert max_rel_err(got.float().cpu().numpy(), ref) <= GEMM_TOL["f16"]
+
+
+@pytest.mark.parametrize("halves", [1, 2])
+@pytest.mark.parametrize("split", [1, 2, 4, 8])
+@pytest.mark.parametrize("rows", [20, 64, 128, 200])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_prefill_every_plan(cuda_device, halves, split, rows, dtype):
+    # 128- or 256-row tiles, K split over 1..8 CTAs of a cluster (the partial
+    # sums meet in the owner CTAs); N = 768 is three 256-column tiles
+    plan = {"path": PATH_PREFILL, "warps": halves, "split": split}
+    if halves == 2 and split > 4:
+        with pytest.raises(Exception):
+            _run(cuda_device, dtype, rows, 1024, 768, 128, plan=plan)
+        return
+    x, qw, qz, s, b = random_awq(1024, 768, 128, dtype, rows, seed=rows + split)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    y = cawq.gemm(t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), 128, bias=t(b, dtype),
+                  plan=plan)
+    y2 = cawq.gemm(t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), 128, bias=t(b, dtype),
+                   plan=plan)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)  # partial sums are added in rank order
+    ref = oracle.gemm_f64(x, qw, qz, s, 128, bias=b, dtype=dtype, deq_round=True)
+    assert max_rel_err(as_f64(to_numpy(y, dtype), dtype), ref) <= GEMM_TOL[dtype]
+
+
+def test_planner_splits_k_for_mid_m(cuda_device):
+    p = cawq.plan_get(64, 3584, 4608, 64, torch.float16)
+    assert p["path"] == PATH_PREFILL and p["warps"] == 1 and p["split"] == 8
+    p = cawq.plan_get(2048, 4096, 4096, 128, torch.float16)
+    assert p["path"] == PATH_PREFILL and p["warps"] == 2 and p["split"] == 1
