@@ -22,6 +22,7 @@ from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, a
                      validate_launch_params, version)
 from .modules import AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear, AWQLinearConfig
 from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
+from .loader import load_awq_linears
 
 import os as _os
 
@@ -35,7 +36,7 @@ if _os.path.exists(_lib.LIB_PATH):
 
 __all__ = [
     "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
-    "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm",
+    "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "load_awq_linears",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
     "dequantize_awq", "dequantize_native", "device_error", "gemm", "plan_cache_clear",
