@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   // Peers push into this CTA's receive buffer only after every CTA of the
   // cluster has passed this point (the matching wait precedes the pushes).
   if (split > 1) cluster_arrive_release();
+  // The next kernel in the stream may launch now: its CTAs take SMs as they
+  // free up and prefetch their weights; they read this kernel's output only
+  // after griddepcontrol.wait, which waits for this whole grid.
+  pdl_launch_dependents();
   __shared__ int s_issued;  // stages whose copies the producer issued
 
   bool ok = true;
@@ -231,8 +235,6 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       s_issued = issued;
     }
     __syncwarp();
-    // all loads issued: the next kernel in the stream may start its prologue
-    pdl_launch_dependents();
   }
 
   float tot[MT][4][4];
@@ -770,7 +772,7 @@ cudaError_t launch_decode(const GemmProblem& p, const cawq_plan& plan, const Dev
 cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   // Measured on B200 over chains of cold launches (Llama-2-7B shapes): two
   // strips per CTA, K split until there are about two CTAs per SM, and a
-  // 6-stage ring once a CTA has that many stages.
+  // 6-stage ring once a CTA has more than 8 stages (4 below).
   cawq_plan plan = {};
   plan.path = CAWQ_PATH_DECODE;
   plan.warps = 2;
@@ -781,7 +783,7 @@ cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   while (split < 16 && bands * split < 2 * sms && nst_total >= (size_t)split * 8) split *= 2;
   plan.split = split;
   const size_t per_cta = (nst_total + split - 1) / split;
-  plan.stages = per_cta >= 6 ? 6 : (per_cta >= 4 ? 4 : (per_cta >= 2 ? 2 : 1));
+  plan.stages = per_cta > 8 ? 6 : (per_cta >= 4 ? 4 : (per_cta >= 2 ? 2 : 1));
   while (plan.stages > 1 && !decode_supports(p, plan, dev)) --plan.stages;
   return plan;
 }
