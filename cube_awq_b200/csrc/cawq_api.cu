@@ -978,7 +978,8 @@ CAWQ_API cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const vo
                                               const void* scales, const void* bias, void* out,
                                               size_t rows, size_t k, size_t n, size_t group_size,
                                               cawq_dtype dtype, void* stream) {
-  if (rows * n > CAWQ_ROWPAR_SCRATCH_FLOATS) {
+  // Divide rather than multiply: rows * n can wrap around for absurd sizes.
+  if (n != 0 && rows > CAWQ_ROWPAR_SCRATCH_FLOATS / n) {
     return fail(CAWQ_ERR_INVALID_SHAPE,
                 fmt("rows * n = %zu exceeds the static scratch of %u floats "
                     "(CAWQ_ROWPAR_SCRATCH_FLOATS); use cawq_gemm_rowpar with a workspace",

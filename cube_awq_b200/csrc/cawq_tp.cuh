@@ -88,12 +88,15 @@ cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* o
 }
 
 // Fixed-size fp32 scratch of cawq_gemm_rowpar_noalloc: one per device,
-// part of the module image (no allocation at call time).
+// loaded with the module image, so the call allocates nothing. In host code
+// `g_rowpar_scratch` is only a handle for the runtime, not a device address:
+// the address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) float g_rowpar_scratch[CAWQ_ROWPAR_SCRATCH_FLOATS];
 
 cudaError_t rowpar_static_scratch(float** ptr) {
-  // cudaGetSymbolAddress once per device, with that device current (the
-  // caller's current device: the communicator's).
+  // Set-up on the first call per device: cudaGetSymbolAddress with that
+  // device current (the caller's current device, the communicator's), its
+  // status checked, the address kept for every later call on that device.
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
   static float* cached[kMaxDevices] = {};

@@ -349,15 +349,35 @@ cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint
                              size_t group_size, cawq_dtype dtype, void* stream);
 
 /*
- * cawq_gemm_rowpar without any caller workspace and without allocating: the
- * fp32 partial sums live in a fixed scratch array that is part of the
- * library's device image, CAWQ_ROWPAR_SCRATCH_FLOATS floats (4 MiB) per
- * device, so rows * n must not exceed it (else CAWQ_ERR_INVALID_SHAPE).
- * No counterpart in the reference (which is single-device).
- *   - Nothing in the scratch has to start at zero: the local GEMM writes
- *     every one of the rows * n partial sums before the all-reduce reads them.
- *   - One scratch per device: calls that overlap on a device (other streams,
- *     or graphs replayed concurrently) race on it; order them.
+ * cawq_gemm_rowpar for callers that have no fp32 workspace to pass and may
+ * not allocate one. No counterpart in the reference (which is single-device).
+ *
+ * Who needs it: a host that gives its whole device memory to its own pool at
+ * start-up (a serving engine sizing its KV cache, a framework's caching
+ * allocator) has nothing left for a cudaMalloc in the middle of a step, and a
+ * cudaMalloc / cudaFree there could also stall its other streams; a non-Python
+ * host binding this C ABI (the reference's Rust side) holds the layer's
+ * tensors and its output but no allocator for a rows * n fp32 buffer.
+ *
+ * The partial sums go to a scratch array compiled into the library's device
+ * image instead, CAWQ_ROWPAR_SCRATCH_FLOATS floats (4 MiB) on each device:
+ *   - rows * n above CAWQ_ROWPAR_SCRATCH_FLOATS is refused with
+ *     CAWQ_ERR_INVALID_SHAPE (use cawq_gemm_rowpar with a workspace instead);
+ *   - the first call on a device looks the array's device address up once
+ *     (cudaGetSymbolAddress, on the current device) and keeps it; make that
+ *     first call before any stream capture;
+ *   - this library allocates nothing in the call, on the device or through
+ *     any allocating library routine; NCCL's own connection buffers are
+ *     NCCL's, and with its default lazy connection a communicator may set
+ *     them up at its first collectives: a caller that must see none at all
+ *     makes one call of each size it will use beforehand, or runs with
+ *     NCCL_RUNTIME_CONNECT=0 so that cawq_tp_init connects everything;
+ *   - nothing in the array has to start at zero: the local GEMM writes all
+ *     rows * n partial sums before the all-reduce reads them, so the last
+ *     call's contents never leak into the next;
+ *   - every call on a device shares the one array: calls that overlap on the
+ *     GPU (on other streams, say) race on it and give wrong sums; the caller
+ *     orders them.
  * Other arguments and results are those of cawq_gemm_rowpar.
  */
 #define CAWQ_ROWPAR_SCRATCH_FLOATS (1u << 20)

@@ -1,9 +1,14 @@
-"""cawq_gemm_rowpar_noalloc: the row-parallel GEMM with its fp32 partial sums
-in the library's static device scratch instead of a caller workspace.
+"""cawq_gemm_rowpar_noalloc: the row-parallel GEMM for callers that cannot
+allocate a workspace -- hosts whose device memory already belongs to their own
+pool, or C-ABI hosts with no allocator for an fp32 buffer -- so its partial
+sums go to a 4 MiB scratch array compiled into the library instead.
 
-Collected last (file name). The GPU test compares it with cawq_gemm_rowpar
-(caller workspace) on two calls in a row, on a one-rank NCCL communicator;
-the CPU test checks that a request larger than the scratch is refused.
+The file name makes pytest collect it last. The GPU test runs the entry point
+twice in a row (the second call finds the first call's sums in the scratch)
+and compares both results with cawq_gemm_rowpar given a workspace of its own,
+on a one-rank NCCL communicator, then with the fp64 oracle. The CPU tests
+check that requests larger than the scratch are refused, including sizes
+whose rows * n would wrap around.
 """
 
 import ctypes
@@ -34,6 +39,15 @@ def test_oversize_request_is_refused_without_a_gpu():
     assert rows * n > _lib.CAWQ_ROWPAR_SCRATCH_FLOATS
 
 
+def test_wrapping_request_is_refused_without_a_gpu():
+    L = _lib.lib()
+    rows, n = 1 << 62, 8  # rows * n wraps to 0 in 64 bits
+    st = L.cawq_gemm_rowpar_noalloc(None, None, None, None, None, None, None, rows, 4096, n, 128,
+                                    _lib.CAWQ_F16, None)
+    assert st == _lib.CAWQ_ERR_INVALID_SHAPE
+    assert "CAWQ_ROWPAR_SCRATCH_FLOATS" in _lib.last_error()
+
+
 @pytest.mark.gpu
 def test_noalloc_matches_the_workspace_entry_point(cuda_device):
     L = _lib.lib()
@@ -49,7 +63,7 @@ def test_noalloc_matches_the_workspace_entry_point(cuda_device):
                    extra=(partial,))
         assert st == 0, _lib.last_error()
         outs = []
-        for _ in range(2):  # two calls in a row reuse the same scratch
+        for _ in range(2):  # the second call starts on the first call's sums
             y = torch.full((rows, n), float("nan"), dtype=torch.float16, device=cuda_device)
             st = _call(L.cawq_gemm_rowpar_noalloc, comm.handle, xt, qwt, qzt, st_, bt, y, rows, k,
                        n, g)
