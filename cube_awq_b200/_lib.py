@@ -78,7 +78,8 @@ class PlanC(ctypes.Structure):
 
     def as_dict(self) -> dict:
         return {"path": self.path, "split": self.split, "warps": self.warps,
-                "tile_n": self.tile_n, "stages": self.stages, "pdl": self.reserved[0] == 0}
+                "tile_n": self.tile_n, "stages": self.stages, "pdl": self.reserved[0] == 0,
+                "l2_prefetch": self.reserved[1], "mma": "i8" if self.reserved[2] else "f16"}
 
 
 _lib = None

@@ -6,12 +6,12 @@
 //
 // The work is bound by HBM bandwidth on the packed weights (0.5 byte per
 // weight). On B200 that leaves about three issue slots per weight, so the
-// kernel turns nibbles into tensor-core operands with two instructions per
-// pair of weights and lets mma.sync accumulate in fp32:
+// kernel turns nibbles into tensor-core operands with little more than one
+// instruction per pair of weights and lets mma.sync accumulate in fp32:
 //
 //   * Tiles. A CTA owns a band of `strips` x 128 output columns and a slice
 //     of K. Each strip is handled by two consumer warps, one per 64-column half
-//     (one packed word per lane). A cluster of `split` CTAs shares one band and
+//     (a lane holds 4 nibbles of 2 packed words). A cluster of `split` CTAs shares one band and
 //     splits K; partial sums are added across the cluster through distributed
 //     shared memory, so no global scratch is needed.
 //   * Loads. One producer warp streams 64-row stages through a TMA ring: one
@@ -23,11 +23,15 @@
 //     in the stream, so they are requested before griddepcontrol.wait; X
 //     after it (programmatic dependent launch).
 //   * Operands. The MMA is swapped: A = W^T (16 output columns x 16 k),
-//     B = X^T (16 k x 8 rows of X). Two packed words from k rows r, r' are
-//     byte-interleaved (prmt) so one lop3 yields the f16 pair
-//     (1024 + q[r], 1024 + q[r']) of one column; the high nibble is taken in
-//     place as 1024 + 16 q. bf16 (and f32 inputs, split into bf16 hi + lo)
-//     use 128 + q with a shift. No per-weight subtraction or scaling.
+//     B = X^T (16 k x 8 rows of X). One ldmatrix.x4.trans per 16-row step
+//     gives each lane, per register, one 16-bit element (4 nibbles = 4
+//     columns) of two consecutive k rows: exactly the k pair an A-fragment
+//     register holds. One lop3 per register and nibble then yields the f16
+//     pair (1024 + q[k], 1024 + q[k + 1]): nibbles 0 and 2 as 1024 + q,
+//     nibbles 1 and 3 in place as 1024 + 16 q, nibbles 2 and 3 after one
+//     8-bit shift of the register. bf16 (and f32 inputs,
+//     split into bf16 hi + lo) use 128 + q after a shift per nibble. No
+//     per-weight subtraction or scaling.
 //   * Group fold. Within a quantization group, sum_k x (c + q) is accumulated
 //     by the MMA, and sum_k x by one more MMA with an all-ones A. When the
 //     group ends each output adds
@@ -37,6 +41,15 @@
 // Arithmetic differs from the reference in rounding only: the reference
 // rounds (q - z) * s and every partial sum to F; here the weight is exact and
 // the sum is fp32 (see the tolerance of the parity tests).
+//
+// Integer path (plan.reserved[2] = 1; rows <= 4, 16-bit X, g % 64 == 0): an
+// extra warp turns each stage's X rows into exact 16-bit fixed point (a
+// power-of-two scale per row and stage, split into a signed high and an
+// unsigned low byte) laid out as int8 B fragments; the weights enter
+// mma.sync m16n8k32 as u8 nibbles (one AND per 4 weights: byte b of a
+// transposed ldmatrix register is nibble 2 (b & 1) (+1) of k row b >> 1, and
+// B spreads X over two column variants). Products accumulate exactly in
+// int32; the fold applies 1 / scale per stage and s (acc - z sum x) per group.
 #pragma once
 
 #include "cawq_common.cuh"
@@ -49,6 +62,10 @@ constexpr int kDecBoxWords = 32;   // packed words per k row in a weight box (2 
 constexpr int kDecStageRows = 64;  // k rows per TMA stage (4 MMA steps)
 constexpr int kDecMaxWarps = 8;
 constexpr int kDecMaxStages = 8;
+// integer path (rows <= 4): B-fragment table and X row info per stage
+constexpr int kDecI8MaxRows = 4;
+constexpr int kDecI8BTable = 4 * 32 * 16;
+constexpr int kDecI8RowInfo = kDecI8MaxRows * 8;
 
 // Shared-memory layout of one ring slot:
 //   [X tile: XB rows x 64 k, 128B swizzle][W: strips/2 x 64 rows x 128 B, 128B swizzle]
@@ -82,13 +99,23 @@ struct DecodeLayout {
     const size_t raw = z_off(strips, g) + gps(g) * z_row_bytes(strips);
     return (raw + 1023) / 1024 * 1024;
   }
+  // integer path: the stage's B fragments (4 steps x 32 lanes x 16 bytes) and
+  // per X row {1 / scale, scaled sum of X} follow the zero rows
+  static __host__ __device__ size_t b_off(int strips, uint32_t g) {
+    return z_off(strips, g) + gps(g) * z_row_bytes(strips);
+  }
+  static __host__ __device__ size_t slot_bytes_i8(int strips, uint32_t g) {
+    const size_t raw = b_off(strips, g) + kDecI8BTable + kDecI8RowInfo;
+    return (raw + 1023) / 1024 * 1024;
+  }
   // split-K receive buffer: [source rank][XB rows][band columns / split] fp32
   static __host__ __device__ size_t recv_bytes(int strips) {
     return (size_t)XB * strips * kDecTileCols * 4;
   }
-  static size_t smem_bytes(int strips, int stages, uint32_t g) {
-    return 1024 /* alignment slack */ + slot_bytes(strips, g) * stages + recv_bytes(strips) +
-           (size_t)(2 * stages + 1) * 8;
+  static size_t smem_bytes(int strips, int stages, uint32_t g, bool i8 = false) {
+    return 1024 /* alignment slack */ +
+           (i8 ? slot_bytes_i8(strips, g) : slot_bytes(strips, g)) * stages + recv_bytes(strips) +
+           (size_t)((i8 ? 4 : 2) * stages + 1) * 8;
   }
 };
 
@@ -96,27 +123,14 @@ struct DecodeLayout {
 // about 80 registers per thread for 8-row X tiles, 128 for 16.
 __host__ __device__ constexpr int dec_max_consumers(int mt) { return mt == 1 ? 16 : 8; }
 
-// Physical k row (0..15 within a 16-row step) that lane quad position t uses
-// for fragment slot i (0..3). The four rows one load instruction touches,
-// {2t + (i & 1) + 8 (i >> 1)}, differ in bits 1-2, so under the 128-byte
-// swizzle their 32-byte column pieces land in four different bank groups;
-// and the k pairs of one fragment register, (2t, 2t+1) and (2t+8, 2t+9), are
-// adjacent, so X^T fragments are single 32-bit loads.
-__device__ __forceinline__ int dec_row(int t, int i) { return 2 * t + (i & 1) + 8 * (i >> 1); }
-
-// prmt selectors: bytes (b of word a, b of word b) -> result bytes 0 and 2.
-__device__ __forceinline__ uint32_t dec_sel(int b) {
-  return static_cast<uint32_t>(b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12));
-}
-
-template <int DT, int ODT, int ORDER, int MT, bool GA>
-__global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8>
+__global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                   const uint32_t* __restrict__ qz, const typename DType<DT>::T* __restrict__ sc,
                   const typename DType<DT>::T* __restrict__ bias,
                   typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
                   uint32_t g, uint32_t ld_out, uint32_t split, uint32_t nstage_ring,
-                  uint32_t strips_u) {
+                  uint32_t strips_u, uint32_t pf_stages) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
   constexpr bool kF16Mma = (DT == kF16);
@@ -129,7 +143,9 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
   const int strips = static_cast<int>(strips_u);
-  const int consumers = 2 * strips;  // warps 0..consumers-1; the producer follows
+  // warps 0..consumers-1; then the producer; on the integer path the X
+  // preparation warp last
+  const int consumers = 2 * strips;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;
@@ -146,14 +162,16 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   const int nst = static_cast<int>(c_end - c_beg);
   const uint32_t end_step = c_end * 4 < steps ? c_end * 4 : steps;
   const int NS = static_cast<int>(nstage_ring);
-  const size_t slot = L::slot_bytes(strips, g);
+  const size_t slot = I8 ? L::slot_bytes_i8(strips, g) : L::slot_bytes(strips, g);
   const int gps = L::gps(g);
 
   const size_t ring_bytes = slot * NS;
   float* recv = reinterpret_cast<float*>(smem + ring_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes + L::recv_bytes(strips));
   uint64_t* empty = full + NS;
-  uint64_t* recv_bar = empty + NS;  // the peers' partial sums have landed
+  uint64_t* bfull = empty + NS;     // integer path: the stage's B fragments are ready
+  uint64_t* xfull = bfull + NS;     // integer path: the stage's X tile has landed
+  uint64_t* recv_bar = empty + (I8 ? 3 : 1) * NS;  // the peers' partial sums have landed
   const uint32_t rows_eff = rows < (uint32_t)XB ? rows : (uint32_t)XB;
   const uint32_t bcols = static_cast<uint32_t>(strips * kDecTileCols);
   const uint32_t ncols = bcols / split;  // columns of the band this CTA sums (multiple of 8)
@@ -161,7 +179,11 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], static_cast<uint32_t>(consumers));
+      mbar_init(&empty[s], static_cast<uint32_t>(consumers + (I8 ? 1 : 0)));
+      if constexpr (I8) {
+        mbar_init(&bfull[s], 1);
+        mbar_init(&xfull[s], 1);
+      }
     }
     mbar_init(recv_bar, 1);
     if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rows_eff * ncols * 4);
@@ -185,7 +207,9 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       const uint32_t bcol0 = pband * 8;
       const uint32_t vcols = min((uint32_t)(strips * kDecTileCols), n - min(n, bcol0));
       const uint32_t ngroups = k / g;
-      const uint32_t tx = static_cast<uint32_t>(L::kXBytes + strips * L::kWBytes) +
+      // integer path: X has its own barrier, so that its preparation does not
+      // wait for the stage's weights
+      const uint32_t tx = static_cast<uint32_t>((I8 ? 0 : L::kXBytes) + strips * L::kWBytes) +
                           (uint32_t)gps * (vcols * (uint32_t)sizeof(T) + vcols / 2);
       auto issue_weights = [&](int j) {
         const int sl = j % NS;
@@ -215,12 +239,29 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         if constexpr (DT == kF32) {
           tma_load_2d(dst, &tm_x, kr, 0, &full[sl]);
           tma_load_2d(dst + XB * 128, &tm_x, kr + 32, 0, &full[sl]);
+        } else if constexpr (I8) {
+          mbar_arrive_expect_tx(&xfull[sl], static_cast<uint32_t>(L::kXBytes));
+          tma_load_2d(dst, &tm_x, kr, 0, &xfull[sl]);
         } else {
           tma_load_2d(dst, &tm_x, kr, 0, &full[sl]);
         }
       };
+      // stages past the ring: weights, scales and zeros prefetched into L2 only
+      auto prefetch_weights = [&](int j) {
+        const int kr = static_cast<int>((c_beg + j) * kDecStageRows);
+        for (int b = 0; b < strips / 2; ++b)
+          tma_prefetch_l2_2d(&tm_w, static_cast<int>(pband + b * kDecBoxWords), kr);
+        const uint32_t g0 = (uint32_t)kr / g;
+        for (int r = 0; r < gps && vcols; ++r) {
+          const uint32_t grp = min(g0 + r, ngroups - 1);
+          bulk_prefetch_l2(sc + (size_t)grp * n + bcol0, vcols * sizeof(T));
+          bulk_prefetch_l2(qz + (size_t)grp * npk + pband, vcols / 2);
+        }
+      };
       const int pro = NS < nst ? NS : nst;
       for (int j = 0; j < pro; ++j) issue_weights(j);  // independent of earlier kernels
+      const int pf_end = (int)min((uint32_t)nst, (uint32_t)pro + pf_stages);
+      for (int j = pro; j < pf_end; ++j) prefetch_weights(j);
       pdl_wait();                                       // X may be the previous kernel's output
       for (int j = 0; j < pro; ++j) issue_x(j);
       int issued = pro;
@@ -237,6 +278,90 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     __syncwarp();
   }
 
+  if constexpr (I8) {
+    if (warp == consumers + 1) {
+      // --------------------------------------------------- X preparation
+      // Per stage, each X row (rows <= 4) becomes 16-bit fixed point with a
+      // power-of-two scale: |x| < 2^(e+1) over the row's 64 values, so
+      // x * 2^(14 - e) rounds into [-2^15, 2^15). The integer splits into a
+      // signed high byte and an unsigned low byte (x_int = 256 hi + lo), each
+      // the B operand of one integer MMA. Lane L writes the B fragments of
+      // consumer lane L = (gq, t): column gq is X row gq >> 1, column variant
+      // gq & 1; its k rows are 2t, 2t + 1 (+ 8) of each 16-row step, one byte
+      // each at byte position variant (+ 2); the other bytes are zero. Row r
+      // also gets {1 / scale, sum(x_int) / scale}.
+      const int rr = gq >> 1;
+      const int vv = gq & 1;
+      const bool live = rr < (int)rows_eff;
+      const uint32_t sel_hi = vv ? 0x5010u : 0x0501u;  // byte 1 of each k's integer
+      const uint32_t sel_lo = vv ? 0x4000u : 0x0400u;  // byte 0
+      const uint32_t vmask = vv ? 0xFF00FF00u : 0x00FF00FFu;
+      for (int j = 0; j < nst && ok; ++j) {
+        const int sl = j % NS;
+        ok = mbar_wait_bounded(&xfull[sl], static_cast<uint32_t>((j / NS) & 1));
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        uint8_t* sbase = smem + sl * slot;
+        float xv[16];  // [4 st + 2 p + i]: k row 16 st + 8 p + 2 t + i of row rr
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            uint32_t w = 0u;
+            if (live) {
+              const int kk = 16 * st + 8 * pp + 2 * t;  // 16-byte chunk kk >> 3 of the row
+              w = *reinterpret_cast<const uint32_t*>(sbase + rr * 128 +
+                                                     (((kk >> 3) ^ (rr & 7)) << 4) + ((kk & 7) << 1));
+            }
+            const T* h = reinterpret_cast<const T*>(&w);
+            xv[4 * st + 2 * pp] = DType<DT>::to_f32(h[0]);
+            xv[4 * st + 2 * pp + 1] = DType<DT>::to_f32(h[1]);
+          }
+        }
+        float mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(xv[i]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        // e = floor(log2 mx) from the exponent field (0 and subnormals give a
+        // tiny e, clamped so that both scales stay normal floats)
+        const int e = max(static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu) - 127, -100);
+        const float scale = __uint_as_float(static_cast<uint32_t>(127 + 14 - e) << 23);
+        const float inv = __uint_as_float(static_cast<uint32_t>(127 - 14 + e) << 23);
+        int xi[16];
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          xi[i] = min(__float2int_rn(xv[i] * scale), 32767);
+          sum += xi[i];
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        uint4* btab = reinterpret_cast<uint4*>(sbase + L::b_off(strips, g));
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          const uint32_t p0 = static_cast<uint32_t>(xi[4 * st]), p1 = static_cast<uint32_t>(xi[4 * st + 1]);
+          const uint32_t q0 = static_cast<uint32_t>(xi[4 * st + 2]), q1 = static_cast<uint32_t>(xi[4 * st + 3]);
+          uint4 w;
+          w.x = prmt(p0, p1, sel_hi) & vmask;  // b0, high bytes
+          w.y = prmt(q0, q1, sel_hi) & vmask;  // b1, high bytes
+          w.z = prmt(p0, p1, sel_lo) & vmask;  // b0, low bytes
+          w.w = prmt(q0, q1, sel_lo) & vmask;  // b1, low bytes
+          btab[st * 32 + lane] = w;
+        }
+        if (t == 0 && vv == 0 && rr < kDecI8MaxRows) {
+          float2* info = reinterpret_cast<float2*>(sbase + L::b_off(strips, g) + kDecI8BTable);
+          info[rr] = make_float2(inv, static_cast<float>(sum) * inv);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bfull[sl]);
+          mbar_arrive(&empty[sl]);
+        }
+      }
+    }
+  }
+
   float tot[MT][4][4];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
@@ -245,21 +370,197 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) tot[m][j][e] = 0.f;
 
-  // this warp's strip and 64-column half
+  // this warp's strip and 64-column half; the lane's two packed words inside
+  // the strip (element gq of the warp's 16-byte chunks A and B) and which four
+  // nibbles of them it holds (npar 0: nibbles 0-3, npar 1: nibbles 4-7)
   const int strip = warp % strips;
   const int half = (warp / strips) & 1;
-  const int word = 8 * half + gq;  // packed word of this lane inside the strip
+  const int wA = 8 * half + (gq >> 1);
+  const int wB = wA + 4;
+  const int npar = gq & 1;
+  int oword = 0;               // the word whose 8 columns this lane writes
+  float outv[MT][2][8] = {};   // its sums, rows 8m + 2t + e, column order
 
   if (warp < consumers) {
     // -------------------------------------------------------- consumers
-    uint32_t woff[4];  // weight rows dec_row(t, i) of a step, this lane's word
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = dec_row(t, i);
-      const int bw = 16 * (strip & 1) + word;  // word inside the 128-byte box row
-      woff[i] = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + r * 128 +
-                ((((bw >> 2) ^ (r & 7))) << 4) + ((bw & 3) << 2);
+    // Weights: one ldmatrix.x4.trans per 16-row step. Lane L supplies row
+    // L & 7 of matrix L >> 3 (matrices 0 / 1: k rows 0-7 of chunks A / B,
+    // 2 / 3: rows 8-15); the 128-byte swizzle moves chunk c of box row r to
+    // c ^ (r & 7), which spreads each matrix over all banks.
+    uint32_t wld;
+    {
+      const int mi = lane >> 3, r8 = lane & 7;
+      const int chunk = 4 * (strip & 1) + 2 * half + (mi & 1);  // 16-byte chunk in the box row
+      wld = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + (8 * (mi >> 1) + r8) * 128 +
+            ((chunk ^ r8) << 4);
     }
+    // scales of words wA / wB and their zero words inside the stage rows
+    const uint32_t s_off[2] = {(uint32_t)(strip * kDecTileCols + 8 * wA) * (uint32_t)sizeof(T),
+                               (uint32_t)(strip * kDecTileCols + 8 * wB) * (uint32_t)sizeof(T)};
+    const uint32_t z_off[2] = {(uint32_t)(strip * kDecTileWords + wA) * 4,
+                               (uint32_t)(strip * kDecTileWords + wB) * 4};
+
+    // this group's 8 scales (s') and zero terms (c') of the lane's columns:
+    // nibble 4 npar + n of words wA (slot 0) and wB (slot 1); `zmul` scales
+    // the zero of odd nibbles n (their weights entered the MMA as 16 q)
+    auto group_scales = [&](const uint8_t* srow, float (&sc)[2][4], float div_odd) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float s8[8];  // the word's 8 scales, column order
+        if constexpr (DT == kF32) {
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const float4 f = *reinterpret_cast<const float4*>(srow + s_off[q] + 16 * v);
+            s8[4 * v + 0] = f.x; s8[4 * v + 1] = f.y;
+            s8[4 * v + 2] = f.z; s8[4 * v + 3] = f.w;
+          }
+        } else {
+          const uint4 raw = *reinterpret_cast<const uint4*>(srow + s_off[q]);
+          const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) s8[c] = DType<DT>::to_f32(h[c]);
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const float s0 = s8[col_of_nibble(n, ORDER)], s1 = s8[col_of_nibble(4 + n, ORDER)];
+          sc[q][n] = (npar ? s1 : s0) * ((n & 1) ? div_odd : 1.f);
+        }
+      }
+    };
+    // the two zero words, each shifted to the lane's 4 nibbles, packed as
+    // (slot 0 | slot 1 << 16)
+    auto group_zeros = [&](const uint8_t* zrow) {
+      const uint32_t za = *reinterpret_cast<const uint32_t*>(zrow + z_off[0]) >> (16 * npar);
+      const uint32_t zb = *reinterpret_cast<const uint32_t*>(zrow + z_off[1]) >> (16 * npar);
+      return prmt(za, zb, 0x5410u);
+    };
+
+    if constexpr (I8) {
+      // ------------------------------------------- consumers, integer path
+      // Per 16-row step, nibble masks 0x0F / 0xF0 turn the same ldmatrix.trans
+      // registers into u8 A fragments: byte b of a register is nibble 2 (b & 1)
+      // (mask 0x0F; nibble 2 (b & 1) + 1 as 16 q with 0xF0) of element gq at k
+      // row 2t + (b >> 1), which matches the B fragment's (k row, variant)
+      // bytes. D column 2t + v is X row t, column variant v: nibble 2 v + mask
+      // of the slot's element. Per stage: D (exact int32, high and low byte
+      // MMAs) / scale accumulates per column; per group: tot += s' (acc - z'
+      // * sum_k x).
+      using Zero = std::integral_constant<bool, true>;
+      using NoZero = std::integral_constant<bool, false>;
+      const uint32_t brow = static_cast<uint32_t>(L::b_off(strips, g));
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [slot][n]
+      float xs = 0.f;  // sum over the group's stages of sum(x_int) / scale, X row t
+      float ti[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // [slot][n]
+      auto imma = [&](int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                      uint32_t b0, uint32_t b1, auto zero_tag, auto signed_tag) {
+        constexpr bool kZero = decltype(zero_tag)::value;
+        constexpr bool kSigned = decltype(signed_tag)::value;
+        if constexpr (kZero && kSigned) {
+          asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+              "{%8,%9}, {%10,%10,%10,%10};"
+              : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+        } else if constexpr (kZero) {
+          asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+              "{%8,%9}, {%10,%10,%10,%10};"
+              : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+        } else if constexpr (kSigned) {
+          asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+              "{%8,%9}, {%0,%1,%2,%3};"
+              : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        } else {
+          asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+              "{%8,%9}, {%0,%1,%2,%3};"
+              : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        }
+      };
+      auto fold_i8 = [&](const uint8_t* sbase) {
+        float sc[2][4];
+        group_scales(sbase + L::s_off(strips), sc, 0.0625f);
+        const uint32_t zz = group_zeros(sbase + L::z_off(strips, g));
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            const float z = static_cast<float>((zz >> (16 * q + 4 * n)) & 15u) * ((n & 1) ? 16.f : 1.f);
+            ti[q][n] = fmaf(sc[q][n], fmaf(-z, xs, acc[q][n]), ti[q][n]);
+            acc[q][n] = 0.f;
+          }
+        }
+        xs = 0.f;
+      };
+      int sl = 0;
+      uint32_t par = 0;
+      const uint32_t spgs = g / kDecStageRows;  // stages per group (g % 64 == 0 here)
+      uint32_t in_grp = c_beg % spgs;
+      for (int j = 0; j < nst; ++j) {
+        if (ok) ok = mbar_wait_bounded(&full[sl], par);
+        if (ok) ok = mbar_wait_bounded(&bfull[sl], par);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const uint8_t* sbase = smem + sl * slot;
+        int Dh[2][4], Dl[2][4];  // [mask][fragment]: high / low byte products
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          uint32_t R[4];
+          ldmatrix_x4_trans(smem_u32(sbase) + wld + st * 2048, R[0], R[1], R[2], R[3]);
+          const uint4 bt = *reinterpret_cast<const uint4*>(sbase + brow + st * 512 + lane * 16);
+#pragma unroll
+          for (int mk = 0; mk < 2; ++mk) {
+            const uint32_t msk = mk ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+            const uint32_t a0 = R[0] & msk, a1 = R[1] & msk, a2 = R[2] & msk, a3 = R[3] & msk;
+            if (st == 0) {
+              imma(Dh[mk], a0, a1, a2, a3, bt.x, bt.y, Zero{}, Zero{});
+              imma(Dl[mk], a0, a1, a2, a3, bt.z, bt.w, Zero{}, NoZero{});
+            } else {
+              imma(Dh[mk], a0, a1, a2, a3, bt.x, bt.y, NoZero{}, Zero{});
+              imma(Dl[mk], a0, a1, a2, a3, bt.z, bt.w, NoZero{}, NoZero{});
+            }
+          }
+        }
+        const float2 ri = *reinterpret_cast<const float2*>(sbase + brow + kDecI8BTable + t * 8);
+        xs += ri.y;
+#pragma unroll
+        for (int mk = 0; mk < 2; ++mk) {
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            // fragment f: slot f >> 1, variant f & 1 -> element nibble 2 (f & 1) + mk
+            const float val = static_cast<float>(Dh[mk][f] * 256 + Dl[mk][f]);
+            acc[f >> 1][2 * (f & 1) + mk] = fmaf(val, ri.x, acc[f >> 1][2 * (f & 1) + mk]);
+          }
+        }
+        if (++in_grp == spgs || j + 1 == nst) {
+          fold_i8(sbase);
+          in_grp = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);
+        if (++sl == NS) {
+          sl = 0;
+          par ^= 1u;
+        }
+      }
+      // exchange with lane gq ^ 1 so that each lane has all 8 columns of one
+      // word (X row t)
+      oword = npar ? wB : wA;
+      float lo[4], hi[4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const float keep = npar ? ti[1][n] : ti[0][n];
+        const float send = npar ? ti[0][n] : ti[1][n];
+        const float recv = __shfl_xor_sync(0xffffffffu, send, 4);
+        lo[n] = npar ? recv : keep;
+        hi[n] = npar ? keep : recv;
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        outv[0][0][col_of_nibble(n, ORDER)] = lo[n];
+        outv[0][0][col_of_nibble(4 + n, ORDER)] = hi[n];
+      }
+    } else {
     // X^T fragments. 16-bit X: one ldmatrix.x4 per 8-row block of X loads the
     // fragments of two steps; lane L gives the address of row 8m + (L & 7),
     // 16-byte k chunk 4p + (L >> 3) of step pair p, under the tile's 128-byte
@@ -277,9 +578,6 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
       for (int p = 0; p < 2; ++p)
         xld[m][p] = static_cast<uint32_t>((8 * m + lr) * 128 + (((4 * p + li) ^ lr) << 4));
     }
-    // scales of this lane's 8 columns and its zero word inside the stage rows
-    const uint32_t s_lane = (uint32_t)(strip * kDecTileCols + 8 * word) * (uint32_t)sizeof(T);
-    const uint32_t z_lane = (uint32_t)(strip * kDecTileWords + word) * 4;
 
     float D[MT][4][4];
     float Dx[MT][4];  // sum_k x over the current group (ones MMA)
@@ -294,62 +592,70 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     }
 
     // tot += s' * (D - c' * sum_k x) with this group's scales / zeros from the
-    // stage's shared-memory rows (see the file comment). c' = offset + zero is
-    // built by the same magic-number lop3 as the weights: for f16 the lo
-    // nibble gives 1024 + z and the hi nibble, in place, 1024 + 16 z; for
-    // bf16 both give 128 + z. With `clear` the accumulators restart at 0;
-    // else the next group's first MMA overwrites them.
+    // stage's shared-memory rows (see the file comment), for the lane's 8
+    // columns: nibble 4 npar + n of words wA (slot 0) and wB (slot 1). c' =
+    // offset + zero is built by the same magic-number lop3 as the weights: for
+    // f16 nibbles n = 0, 2 give 1024 + z and n = 1, 3, in place, 1024 + 16 z
+    // (their weights entered the MMA as 16 q); for bf16 every nibble gives
+    // 128 + z. With `clear` the accumulators restart at 0; else the next
+    // group's first MMA overwrites them.
     auto fold = [&](const uint8_t* srow, const uint8_t* zrow, auto clear_tag) {
       constexpr bool kClear = decltype(clear_tag)::value;
-      float s_reg[8];
-      if constexpr (DT == kF32) {
+      float sc[2][4];  // [slot][n] scale of nibble 4 npar + n
 #pragma unroll
-        for (int v = 0; v < 2; ++v) {
-          const float4 f = *reinterpret_cast<const float4*>(srow + s_lane + 16 * v);
-          s_reg[4 * v + 0] = f.x; s_reg[4 * v + 1] = f.y;
-          s_reg[4 * v + 2] = f.z; s_reg[4 * v + 3] = f.w;
+      for (int q = 0; q < 2; ++q) {
+        float s8[8];  // the word's 8 scales, column order
+        if constexpr (DT == kF32) {
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const float4 f = *reinterpret_cast<const float4*>(srow + s_off[q] + 16 * v);
+            s8[4 * v + 0] = f.x; s8[4 * v + 1] = f.y;
+            s8[4 * v + 2] = f.z; s8[4 * v + 3] = f.w;
+          }
+        } else {
+          const uint4 raw = *reinterpret_cast<const uint4*>(srow + s_off[q]);
+          const T* h = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) s8[c] = DType<DT>::to_f32(h[c]);
         }
-      } else {
-        const uint4 raw = *reinterpret_cast<const uint4*>(srow + s_lane);
-        const T* h = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) s_reg[c] = DType<DT>::to_f32(h[c]);
-      }
-      const uint32_t zw = *reinterpret_cast<const uint32_t*>(zrow + z_lane);
-      float cz[8];  // c' of nibble p of zw
-      if constexpr (kF16Mma) {
-        const uint32_t z8 = zw >> 8;
-        const uint32_t q[4] = {lop3_and_or(zw, 0x000F000Fu, 0x64006400u),   // nibbles 0, 4
-                               lop3_and_or(zw, 0x00F000F0u, 0x64006400u),   // 1, 5 (x16)
-                               lop3_and_or(z8, 0x000F000Fu, 0x64006400u),   // 2, 6
-                               lop3_and_or(z8, 0x00F000F0u, 0x64006400u)};  // 3, 7 (x16)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q[i]));
-          cz[i] = f.x;
-          cz[i + 4] = f.y;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t q = lop3_and_or(zw >> (4 * i), 0x000F000Fu, 0x43004300u);
-          cz[i] = __uint_as_float(q << 16);             // nibble i
-          cz[i + 4] = __uint_as_float(q & 0xFFFF0000u);  // nibble i + 4
+        for (int n = 0; n < 4; ++n) {
+          const float s0 = s8[col_of_nibble(n, ORDER)], s1 = s8[col_of_nibble(4 + n, ORDER)];
+          sc[q][n] = npar ? s1 : s0;
+          if constexpr (kF16Mma) {
+            if (n & 1) sc[q][n] *= 0.0625f;  // the nibble entered the MMA as 16 q
+          }
         }
       }
+      // the two zero words, each shifted to the lane's 4 nibbles, packed as
+      // (slot 0 | slot 1 << 16): one lop3 gives c' of both slots
+      const uint32_t za = *reinterpret_cast<const uint32_t*>(zrow + z_off[0]) >> (16 * npar);
+      const uint32_t zb = *reinterpret_cast<const uint32_t*>(zrow + z_off[1]) >> (16 * npar);
+      const uint32_t zz = prmt(za, zb, 0x5410u);
+      float cz[2][4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const float sl = s_reg[col_of_nibble(2 * b, ORDER)];
-        float sh = s_reg[col_of_nibble(2 * b + 1, ORDER)];
-        if constexpr (kF16Mma) sh *= 0.0625f;  // the hi nibble entered the MMA as 16 q
-        const float cl = cz[2 * b], ch = cz[2 * b + 1];
+      for (int n = 0; n < 4; ++n) {
+        if constexpr (kF16Mma) {
+          const uint32_t src = n < 2 ? zz : (zz >> 8);
+          const uint32_t q = lop3_and_or(src, (n & 1) ? 0x00F000F0u : 0x000F000Fu, 0x64006400u);
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&q));
+          cz[0][n] = f.x;
+          cz[1][n] = f.y;
+        } else {
+          const uint32_t q = lop3_and_or(zz >> (4 * n), 0x000F000Fu, 0x43004300u);
+          cz[0][n] = __uint_as_float(q << 16);
+          cz[1][n] = __uint_as_float(q & 0xFFFF0000u);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          tot[m][b][0] = fmaf(sl, fmaf(-cl, Dx[m][0], D[m][b][0]), tot[m][b][0]);
-          tot[m][b][1] = fmaf(sl, fmaf(-cl, Dx[m][1], D[m][b][1]), tot[m][b][1]);
-          tot[m][b][2] = fmaf(sh, fmaf(-ch, Dx[m][0], D[m][b][2]), tot[m][b][2]);
-          tot[m][b][3] = fmaf(sh, fmaf(-ch, Dx[m][1], D[m][b][3]), tot[m][b][3]);
-          if constexpr (kClear) D[m][b][0] = D[m][b][1] = D[m][b][2] = D[m][b][3] = 0.f;
+          tot[m][n][0] = fmaf(sc[0][n], fmaf(-cz[0][n], Dx[m][0], D[m][n][0]), tot[m][n][0]);
+          tot[m][n][1] = fmaf(sc[0][n], fmaf(-cz[0][n], Dx[m][1], D[m][n][1]), tot[m][n][1]);
+          tot[m][n][2] = fmaf(sc[1][n], fmaf(-cz[1][n], Dx[m][0], D[m][n][2]), tot[m][n][2]);
+          tot[m][n][3] = fmaf(sc[1][n], fmaf(-cz[1][n], Dx[m][1], D[m][n][3]), tot[m][n][3]);
+          if constexpr (kClear) D[m][n][0] = D[m][n][1] = D[m][n][2] = D[m][n][3] = 0.f;
         }
       }
       if constexpr (kClear) {
@@ -391,39 +697,43 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     };
 
     // one 16-row step with X^T fragments bh (and the bf16 lo parts bl of f32 X):
-    // the ones MMA, dequantize and multiply
+    // the ones MMA, dequantize and multiply. R[0..3] hold, per lane, element
+    // gq of chunks A / B at k rows (2t, 2t + 1) and (2t + 8, 2t + 9): nibble n
+    // of each half is column n of the lane's slot, so one lop3 per register
+    // and nibble gives the f16 pair (magic + q[k], magic + q[k + 1]), the A
+    // fragment of MMA n.
     auto step_mma = [&](const uint8_t* sbase, int s, const uint32_t (&bh)[MT][2],
                         const uint32_t (&bl)[MT][2], auto zero_tag) {
-      uint32_t wv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        wv[i] = *reinterpret_cast<const uint32_t*>(sbase + woff[i] + s * 2048);
+      uint32_t R[4];
+      ldmatrix_x4_trans(smem_u32(sbase) + wld + s * 2048, R[0], R[1], R[2], R[3]);
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         mma(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1], zero_tag);
         if constexpr (DT == kF32)
           mma_16816<true>(Dx[m], kOnes, kOnes, kOnes, kOnes, bl[m][0], bl[m][1]);
       }
+      [[maybe_unused]] uint32_t Rh[4];
+      if constexpr (kF16Mma) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t p01 = prmt(wv[0], wv[1], dec_sel(b));
-        const uint32_t p23 = prmt(wv[2], wv[3], dec_sel(b));
-        uint32_t a0, a1, a2, a3;
-        if constexpr (kF16Mma) {
-          a0 = lop3_and_or(p01, 0x000F000Fu, 0x64006400u);
-          a1 = lop3_and_or(p01, 0x00F000F0u, 0x64006400u);
-          a2 = lop3_and_or(p23, 0x000F000Fu, 0x64006400u);
-          a3 = lop3_and_or(p23, 0x00F000F0u, 0x64006400u);
-        } else {
-          a0 = lop3_and_or(p01, 0x000F000Fu, 0x43004300u);
-          a1 = lop3_and_or(p01 >> 4, 0x000F000Fu, 0x43004300u);
-          a2 = lop3_and_or(p23, 0x000F000Fu, 0x43004300u);
-          a3 = lop3_and_or(p23 >> 4, 0x000F000Fu, 0x43004300u);
+        for (int i = 0; i < 4; ++i) Rh[i] = R[i] >> 8;
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        uint32_t a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if constexpr (kF16Mma) {
+            // nibbles 0, 1 in place (1024 + q, 1024 + 16 q); 2, 3 after >> 8
+            a[i] = lop3_and_or(n < 2 ? R[i] : Rh[i], (n & 1) ? 0x00F000F0u : 0x000F000Fu,
+                               0x64006400u);
+          } else {
+            a[i] = lop3_and_or(n ? (R[i] >> (4 * n)) : R[i], 0x000F000Fu, 0x43004300u);
+          }
         }
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          mma(D[m][b], a0, a1, a2, a3, bh[m][0], bh[m][1], zero_tag);
-          if constexpr (DT == kF32) mma_16816<true>(D[m][b], a0, a1, a2, a3, bl[m][0], bl[m][1]);
+          mma(D[m][n], a[0], a[1], a[2], a[3], bh[m][0], bh[m][1], zero_tag);
+          if constexpr (DT == kF32) mma_16816<true>(D[m][n], a[0], a[1], a[2], a[3], bl[m][0], bl[m][1]);
         }
       }
     };
@@ -538,6 +848,31 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
         }
       }
     }
+
+    // Lanes gq and gq ^ 1 hold the two nibble halves of words wA and wB: swap
+    // one slot so that each lane has all 8 columns of one word.
+    oword = npar ? wB : wA;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float lo[4], hi[4];  // nibbles 0-3 and 4-7 of oword
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const float keep = npar ? tot[m][n][2 + e] : tot[m][n][e];
+          const float send = npar ? tot[m][n][e] : tot[m][n][2 + e];
+          const float recv = __shfl_xor_sync(0xffffffffu, send, 4);
+          lo[n] = npar ? recv : keep;
+          hi[n] = npar ? keep : recv;
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          outv[m][e][col_of_nibble(n, ORDER)] = lo[n];
+          outv[m][e][col_of_nibble(4 + n, ORDER)] = hi[n];
+        }
+      }
+    }
+    }  // f16 / bf16 tensor path
   }
 
   // Before exiting, no copy this CTA issued may still be writing its shared
@@ -547,8 +882,10 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
     if (!__syncthreads_or(ok ? 0 : 1)) return;
     if (threadIdx.x == 0) {
       const int issued = s_issued;
-      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j) {
         mbar_wait_bounded(&full[j % NS], static_cast<uint32_t>((j / NS) & 1));
+        if constexpr (I8) mbar_wait_bounded(&xfull[j % NS], static_cast<uint32_t>((j / NS) & 1));
+      }
     }
     __syncthreads();
   };
@@ -563,20 +900,17 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const uint32_t row = static_cast<uint32_t>(8 * m + 2 * t + e);
+        for (int e = 0; e < (I8 ? 1 : 2); ++e) {
+          // integer path: lane row t; else rows 8m + 2t + e
+          const uint32_t row = static_cast<uint32_t>(I8 ? t : 8 * m + 2 * t + e);
           if (row >= rows_eff) continue;
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-#pragma unroll
-            for (int hi = 0; hi < 2; ++hi) {
-              const uint32_t col = pband * 8 + strip * kDecTileCols + 8 * word +
-                                   col_of_nibble(2 * b + hi, ORDER);
-              if (col < n) {
-                float v = tot[m][b][2 * hi + e];
-                if (bias) v += DType<DT>::to_f32(bias[col]);
-                out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
-              }
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t col = pband * 8 + strip * kDecTileCols + 8 * oword + c;
+            if (col < n) {
+              float v = outv[m][e][c];
+              if (bias) v += DType<DT>::to_f32(bias[col]);
+              out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
             }
           }
         }
@@ -591,16 +925,11 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 32, 1)
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const uint32_t row = static_cast<uint32_t>(8 * m + 2 * t + e);
+      for (int e = 0; e < (I8 ? 1 : 2); ++e) {
+        const uint32_t row = static_cast<uint32_t>(I8 ? t : 8 * m + 2 * t + e);
         if (row >= rows_eff) continue;
-        float v[8];  // this lane's 8 consecutive columns, natural order
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          v[col_of_nibble(2 * b, ORDER)] = tot[m][b][e];
-          v[col_of_nibble(2 * b + 1, ORDER)] = tot[m][b][2 + e];
-        }
-        const uint32_t col8 = static_cast<uint32_t>(strip * kDecTileCols + 8 * word);
+        const float* v = outv[m][e];  // this lane's 8 consecutive columns
+        const uint32_t col8 = static_cast<uint32_t>(strip * kDecTileCols + 8 * oword);
         const uint32_t q = col8 / ncols;
         float* dst = recv + ((size_t)rank * XB + row) * ncols + (col8 - q * ncols);
         if (q == rank) {
@@ -641,14 +970,25 @@ static bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base
 
 static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 
+// plan.reserved[2] = 1 selects the integer tensor path (int8 MMA on exact
+// 16-bit fixed-point X) where it applies: rows <= 4, 16-bit X, groups that
+// are whole 64-row stages. Off by default: its larger stage slots and extra
+// warp hold fewer CTAs per SM, which costs more than its faster inner loop
+// gains in chains of dependent launches.
+static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
+  return plan.reserved[2] == 1 && p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
+         p.g % kDecStageRows == 0;
+}
+
 static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
   const uint32_t g = static_cast<uint32_t>(p.g);
   const bool mt1 = decode_mt(p.rows) == 1;
+  const bool i8 = decode_use_i8(p, plan);
   if (p.dtype == kF32) {
     return mt1 ? DecodeLayout<kF32, 1>::smem_bytes(plan.warps, plan.stages, g)
                : DecodeLayout<kF32, 2>::smem_bytes(plan.warps, plan.stages, g);
   }
-  return mt1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages, g)
+  return mt1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages, g, i8)
              : DecodeLayout<kF16, 2>::smem_bytes(plan.warps, plan.stages, g);
 }
 
@@ -664,13 +1004,14 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   if (plan.warps < 2 || (plan.warps & 1) || 2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
     return false;
   if (plan.stages < 1 || plan.stages > kDecMaxStages) return false;
+  if (plan.reserved[2] < 0 || plan.reserved[2] > 1) return false;
   const size_t bands =
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps);
   if (bands * plan.split >= (1ull << 31)) return false;
   return decode_smem(p, plan) <= dev.smem_optin && dev.cc_major == 10;
 }
 
-template <int DT, int ODT, int ORDER, int MT, bool GA>
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8>
 static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
@@ -689,7 +1030,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                  CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA>;
+  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA, I8>;
   const size_t smem = decode_smem(p, plan);
   // function attributes are per process; set each once (a repeat is harmless)
   static size_t smem_set = 0;
@@ -710,7 +1051,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(bands * plan.split);
-  cfg.blockDim = dim3((2 * plan.warps + 1) * 32);
+  cfg.blockDim = dim3((2 * plan.warps + (I8 ? 2 : 1)) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = p.stream;
   cudaLaunchAttribute attr[2];
@@ -737,18 +1078,22 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                             static_cast<uint32_t>(p.rows), static_cast<uint32_t>(p.k),
                             static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g),
                             static_cast<uint32_t>(p.ld_out), static_cast<uint32_t>(plan.split),
-                            static_cast<uint32_t>(plan.stages), static_cast<uint32_t>(plan.warps));
+                            static_cast<uint32_t>(plan.stages), static_cast<uint32_t>(plan.warps),
+                            static_cast<uint32_t>(plan.reserved[1] > 0 ? plan.reserved[1] : 0));
 }
 
 template <int DT, int ODT, int ORDER>
 static cudaError_t launch_decode_m(const GemmProblem& p, const cawq_plan& plan) {
   const bool ga = p.g % kDecStageRows == 0;  // groups end on stage boundaries
-  if (decode_mt(p.rows) == 1) {
-    return ga ? launch_decode_t<DT, ODT, ORDER, 1, true>(p, plan)
-              : launch_decode_t<DT, ODT, ORDER, 1, false>(p, plan);
+  if constexpr (DT != kF32) {
+    if (decode_use_i8(p, plan)) return launch_decode_t<DT, ODT, ORDER, 1, true, true>(p, plan);
   }
-  return ga ? launch_decode_t<DT, ODT, ORDER, 2, true>(p, plan)
-            : launch_decode_t<DT, ODT, ORDER, 2, false>(p, plan);
+  if (decode_mt(p.rows) == 1) {
+    return ga ? launch_decode_t<DT, ODT, ORDER, 1, true, false>(p, plan)
+              : launch_decode_t<DT, ODT, ORDER, 1, false, false>(p, plan);
+  }
+  return ga ? launch_decode_t<DT, ODT, ORDER, 2, true, false>(p, plan)
+            : launch_decode_t<DT, ODT, ORDER, 2, false, false>(p, plan);
 }
 
 template <int DT, int ODT>

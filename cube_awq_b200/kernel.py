@@ -315,6 +315,11 @@ def _plan_c(plan: dict) -> _lib.PlanC:
     p.tile_n = int(plan.get("tile_n", 0))
     p.stages = int(plan.get("stages", 0))
     p.reserved[0] = 0 if plan.get("pdl", True) else 1
+    p.reserved[1] = int(plan.get("l2_prefetch", 0))
+    mma = plan.get("mma", "f16")
+    if mma not in ("f16", "i8"):
+        raise ValueError("plan['mma'] must be 'f16' or 'i8'")
+    p.reserved[2] = 1 if mma == "i8" else 0
     return p
 
 

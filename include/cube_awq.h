@@ -108,7 +108,14 @@ typedef struct cawq_plan {
   int stages;    /* pipeline stages                                      */
   int reserved[3]; /* reserved[0] = 1: launch without programmatic
                       dependent launch (no overlap with the previous
-                      kernel of the stream); others must be 0          */
+                      kernel of the stream).
+                      reserved[1] (decode): weight stages past the ring
+                      to prefetch into L2 before waiting for the
+                      previous kernel (0 = none).
+                      reserved[2] (decode): 0 = f16 / bf16 tensor
+                      path; 1 = integer tensor path where it applies
+                      (rows <= 4, f16 / bf16 X, group_size % 64 == 0:
+                      X as exact 16-bit fixed point, int8 MMA)      */
 } cawq_plan;
 
 /* ----------------------------------------------------------------------- */

@@ -107,16 +107,43 @@ def test_decode_default_plan_parity(cuda_device, dtype, rows, k, n, g):
 @pytest.mark.parametrize("split", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("warps", [2, 4, 6, 8])
 @pytest.mark.parametrize("stages", [1, 2, 3, 4])
-@pytest.mark.parametrize("rows,dtype", [(3, "f32"), (3, "f16"), (11, "f16")])
-def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype):
+@pytest.mark.parametrize("rows,dtype,mma", [(3, "f32", "f16"), (3, "f16", "f16"),
+                                            (3, "f16", "i8"), (4, "bf16", "i8"),
+                                            (11, "f16", "f16")])
+def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype, mma):
     # warps = 128-column strips per CTA (two consumer warps each), split = CTAs
     # of a cluster along K; N = 1184 leaves the last band of every strip count
-    # partly out of range
+    # partly out of range. mma "i8" selects the integer tensor path (rows <= 4
+    # with 16-bit X, here g = 128); "f16" is the f16 / bf16 MMA path.
     if rows > 8 and 2 * warps > 8:
         pytest.skip("more warps than a 16-row tile allows")
-    plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages}
+    plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages, "mma": mma}
     got, ref, _ = _run(cuda_device, dtype, rows, 2048, 1184, 128, plan=plan)
     assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("rows", [1, 2, 4])
+@pytest.mark.parametrize("g", [64, 128, 256])
+def test_decode_integer_path_with_activation_outliers(cuda_device, dtype, rows, g):
+    # The integer path scales each 64-k slice of an X row by a power of two of
+    # its own maximum: a few activations 300x larger than the rest cost the
+    # other values of their slice some bits, which the tolerance still covers;
+    # the result also stays close to the f16 / bf16 MMA path's.
+    k, n = 4096, 1024
+    _, qw, qz, s, _ = random_awq(k, n, g, dtype, rows, seed=77)
+    rng = np.random.default_rng(78)
+    x32 = rng.standard_normal((rows, k)).astype(np.float32)
+    x32[:, rng.choice(k, size=12, replace=False)] *= 300.0
+    x = x32.astype(np.float16) if dtype == "f16" else oracle.bf16_bits(x32)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    args = (t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), g)
+    plan = {"path": PATH_DECODE, "split": 4, "warps": 2, "stages": 4}
+    y_i8 = as_f64(to_numpy(cawq.gemm(*args, plan=dict(plan, mma="i8")), dtype), dtype)
+    y_f16 = as_f64(to_numpy(cawq.gemm(*args, plan=plan), dtype), dtype)
+    ref = oracle.gemm_f64(x, qw, qz, s, g, dtype=dtype, deq_round=False)
+    assert max_rel_err(y_i8, ref) <= GEMM_TOL[dtype]
+    assert max_rel_err(y_i8, y_f16) <= GEMM_TOL[dtype]
 
 
 @pytest.mark.parametrize("pdl", [True, False])
