@@ -66,6 +66,9 @@ constexpr int kDecMaxStages = 8;
 constexpr int kDecI8MaxRows = 4;
 constexpr int kDecI8BTable = 4 * 32 * 16;
 constexpr int kDecI8RowInfo = kDecI8MaxRows * 8;
+constexpr int kDecI8BSlots = 2;  // B-fragment tables in flight (their own small ring)
+constexpr int kDecI8BSlot = kDecI8BTable + kDecI8RowInfo;
+constexpr int kDecI8MaxStrips = 4;
 
 // Shared-memory layout of one ring slot:
 //   [X tile: XB rows x 64 k, 128B swizzle][W: strips/2 x 64 rows x 128 B, 128B swizzle]
@@ -99,23 +102,17 @@ struct DecodeLayout {
     const size_t raw = z_off(strips, g) + gps(g) * z_row_bytes(strips);
     return (raw + 1023) / 1024 * 1024;
   }
-  // integer path: the stage's B fragments (4 steps x 32 lanes x 16 bytes) and
-  // per X row {1 / scale, scaled sum of X} follow the zero rows
-  static __host__ __device__ size_t b_off(int strips, uint32_t g) {
-    return z_off(strips, g) + gps(g) * z_row_bytes(strips);
-  }
-  static __host__ __device__ size_t slot_bytes_i8(int strips, uint32_t g) {
-    const size_t raw = b_off(strips, g) + kDecI8BTable + kDecI8RowInfo;
-    return (raw + 1023) / 1024 * 1024;
-  }
   // split-K receive buffer: [source rank][XB rows][band columns / split] fp32
   static __host__ __device__ size_t recv_bytes(int strips) {
     return (size_t)XB * strips * kDecTileCols * 4;
   }
+  // integer path: after the receive buffer, kDecI8BSlots tables of the
+  // stage's B fragments (4 steps x 32 lanes x 16 bytes) and, per X row,
+  // {1 / scale, sum(x_int) / scale}
   static size_t smem_bytes(int strips, int stages, uint32_t g, bool i8 = false) {
-    return 1024 /* alignment slack */ +
-           (i8 ? slot_bytes_i8(strips, g) : slot_bytes(strips, g)) * stages + recv_bytes(strips) +
-           (size_t)((i8 ? 4 : 2) * stages + 1) * 8;
+    return 1024 /* alignment slack */ + slot_bytes(strips, g) * stages + recv_bytes(strips) +
+           (i8 ? (size_t)kDecI8BSlots * kDecI8BSlot : 0) +
+           (size_t)((i8 ? 3 : 2) * stages + (i8 ? 2 * kDecI8BSlots : 0) + 1) * 8;
   }
 };
 
@@ -123,8 +120,12 @@ struct DecodeLayout {
 // about 80 registers per thread for 8-row X tiles, 128 for 16.
 __host__ __device__ constexpr int dec_max_consumers(int mt) { return mt == 1 ? 16 : 8; }
 
+// The integer path runs at most kDecI8MaxStrips strips and keeps 3 CTAs per
+// SM within the register file.
 template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8>
-__global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
+__global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
+                                     : dec_max_consumers(MT) * 32 + 32,
+                                  I8 ? 3 : 1)
     decode_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                   const uint32_t* __restrict__ qz, const typename DType<DT>::T* __restrict__ sc,
                   const typename DType<DT>::T* __restrict__ bias,
@@ -162,16 +163,19 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
   const int nst = static_cast<int>(c_end - c_beg);
   const uint32_t end_step = c_end * 4 < steps ? c_end * 4 : steps;
   const int NS = static_cast<int>(nstage_ring);
-  const size_t slot = I8 ? L::slot_bytes_i8(strips, g) : L::slot_bytes(strips, g);
+  const size_t slot = L::slot_bytes(strips, g);
   const int gps = L::gps(g);
 
   const size_t ring_bytes = slot * NS;
   float* recv = reinterpret_cast<float*>(smem + ring_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes + L::recv_bytes(strips));
+  uint8_t* btabs = smem + ring_bytes + L::recv_bytes(strips);  // integer path: B tables
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      btabs + (I8 ? (size_t)kDecI8BSlots * kDecI8BSlot : 0));
   uint64_t* empty = full + NS;
-  uint64_t* bfull = empty + NS;     // integer path: the stage's B fragments are ready
-  uint64_t* xfull = bfull + NS;     // integer path: the stage's X tile has landed
-  uint64_t* recv_bar = empty + (I8 ? 3 : 1) * NS;  // the peers' partial sums have landed
+  uint64_t* xfull = empty + NS;              // integer path: the stage's X tile has landed
+  uint64_t* bfull = xfull + NS;              // integer path: B table ready / free
+  uint64_t* bempty = bfull + kDecI8BSlots;
+  uint64_t* recv_bar = I8 ? bempty + kDecI8BSlots : empty + NS;  // peers' partial sums landed
   const uint32_t rows_eff = rows < (uint32_t)XB ? rows : (uint32_t)XB;
   const uint32_t bcols = static_cast<uint32_t>(strips * kDecTileCols);
   const uint32_t ncols = bcols / split;  // columns of the band this CTA sums (multiple of 8)
@@ -180,9 +184,12 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], static_cast<uint32_t>(consumers + (I8 ? 1 : 0)));
-      if constexpr (I8) {
-        mbar_init(&bfull[s], 1);
-        mbar_init(&xfull[s], 1);
+      if constexpr (I8) mbar_init(&xfull[s], 1);
+    }
+    if constexpr (I8) {
+      for (int b = 0; b < kDecI8BSlots; ++b) {
+        mbar_init(&bfull[b], 1);
+        mbar_init(&bempty[b], static_cast<uint32_t>(consumers));
       }
     }
     mbar_init(recv_bar, 1);
@@ -298,10 +305,15 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
       const uint32_t vmask = vv ? 0xFF00FF00u : 0x00FF00FFu;
       for (int j = 0; j < nst && ok; ++j) {
         const int sl = j % NS;
+        const int bs = j % kDecI8BSlots;
         ok = mbar_wait_bounded(&xfull[sl], static_cast<uint32_t>((j / NS) & 1));
+        // the consumers are done with the table this slot held two stages ago
+        if (ok && j >= kDecI8BSlots)
+          ok = mbar_wait_bounded(&bempty[bs], static_cast<uint32_t>(((j / kDecI8BSlots) - 1) & 1));
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         uint8_t* sbase = smem + sl * slot;
+        uint8_t* tbase = btabs + (size_t)bs * kDecI8BSlot;
         float xv[16];  // [4 st + 2 p + i]: k row 16 st + 8 p + 2 t + i of row rr
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
@@ -337,7 +349,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
         }
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        uint4* btab = reinterpret_cast<uint4*>(sbase + L::b_off(strips, g));
+        uint4* btab = reinterpret_cast<uint4*>(tbase);
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           const uint32_t p0 = static_cast<uint32_t>(xi[4 * st]), p1 = static_cast<uint32_t>(xi[4 * st + 1]);
@@ -350,12 +362,12 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
           btab[st * 32 + lane] = w;
         }
         if (t == 0 && vv == 0 && rr < kDecI8MaxRows) {
-          float2* info = reinterpret_cast<float2*>(sbase + L::b_off(strips, g) + kDecI8BTable);
+          float2* info = reinterpret_cast<float2*>(tbase + kDecI8BTable);
           info[rr] = make_float2(inv, static_cast<float>(sum) * inv);
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&bfull[sl]);
+          mbar_arrive(&bfull[bs]);
           mbar_arrive(&empty[sl]);
         }
       }
@@ -447,7 +459,6 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
       // * sum_k x).
       using Zero = std::integral_constant<bool, true>;
       using NoZero = std::integral_constant<bool, false>;
-      const uint32_t brow = static_cast<uint32_t>(L::b_off(strips, g));
       float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // [slot][n]
       float xs = 0.f;  // sum over the group's stages of sum(x_int) / scale, X row t
       float ti[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // [slot][n]
@@ -497,17 +508,19 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
       const uint32_t spgs = g / kDecStageRows;  // stages per group (g % 64 == 0 here)
       uint32_t in_grp = c_beg % spgs;
       for (int j = 0; j < nst; ++j) {
+        const int bs = j % kDecI8BSlots;
         if (ok) ok = mbar_wait_bounded(&full[sl], par);
-        if (ok) ok = mbar_wait_bounded(&bfull[sl], par);
+        if (ok) ok = mbar_wait_bounded(&bfull[bs], static_cast<uint32_t>((j / kDecI8BSlots) & 1));
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         const uint8_t* sbase = smem + sl * slot;
+        const uint8_t* tbase = btabs + (size_t)bs * kDecI8BSlot;
         int Dh[2][4], Dl[2][4];  // [mask][fragment]: high / low byte products
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           uint32_t R[4];
           ldmatrix_x4_trans(smem_u32(sbase) + wld + st * 2048, R[0], R[1], R[2], R[3]);
-          const uint4 bt = *reinterpret_cast<const uint4*>(sbase + brow + st * 512 + lane * 16);
+          const uint4 bt = *reinterpret_cast<const uint4*>(tbase + st * 512 + lane * 16);
 #pragma unroll
           for (int mk = 0; mk < 2; ++mk) {
             const uint32_t msk = mk ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
@@ -521,7 +534,7 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
             }
           }
         }
-        const float2 ri = *reinterpret_cast<const float2*>(sbase + brow + kDecI8BTable + t * 8);
+        const float2 ri = *reinterpret_cast<const float2*>(tbase + kDecI8BTable + t * 8);
         xs += ri.y;
 #pragma unroll
         for (int mk = 0; mk < 2; ++mk) {
@@ -537,7 +550,10 @@ __global__ void __launch_bounds__(dec_max_consumers(MT) * 32 + 64, 1)
           in_grp = 0;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[sl]);
+        if (lane == 0) {
+          mbar_arrive(&empty[sl]);
+          mbar_arrive(&bempty[bs]);
+        }
         if (++sl == NS) {
           sl = 0;
           par ^= 1u;
@@ -977,7 +993,7 @@ static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 // gains in chains of dependent launches.
 static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
   return plan.reserved[2] == 1 && p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
-         p.g % kDecStageRows == 0;
+         p.g % kDecStageRows == 0 && plan.warps <= kDecI8MaxStrips;
 }
 
 static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
