@@ -166,6 +166,12 @@ __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, ui
       : "memory");
 }
 
+// Barrier among `count` threads (a multiple of 32) of the CTA on named
+// barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Prefetches into L2 (no shared memory, no completion): one 2-D tensor box,
 // or a 1-D byte range (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {

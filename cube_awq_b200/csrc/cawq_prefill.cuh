@@ -33,6 +33,8 @@
 // dequantized values; the products are exact and the sum is fp32.
 #pragma once
 
+#include <mutex>
+
 #include "cawq_common.cuh"
 
 namespace cawq {
@@ -42,23 +44,33 @@ constexpr int kPfBK = 64;
 constexpr int kPfXStages = 3;
 constexpr int kPfWStages = 4;
 constexpr int kPfBStages = 2;
-constexpr int kPfDqWarps = 8;                       // dequant / epilogue warps
-constexpr int kPfThreads = 96 + 32 * kPfDqWarps;    // + X producer, MMA, W producer
+// dequant / epilogue warps: 16 for 128-row tiles (their stage has a quarter
+// of the MMA work, so dequantization paces the loop), 8 for 256-row tiles
+// (their registers would not fit 16)
+__host__ __device__ constexpr int pf_dq_warps(int halves) { return halves == 1 ? 16 : 8; }
+__host__ __device__ constexpr int pf_threads(int halves) {
+  return 96 + 32 * pf_dq_warps(halves);  // + X producer, MMA, W producer
+}
 constexpr int kPfMaxSplit = 8;                      // CTAs of a cluster splitting K
 
 // HALVES = 128-row MMA halves per CTA tile (1 or 2)
 template <int HALVES>
 struct PrefillLayout {
   static constexpr int kBM = 128 * HALVES;
+  // ring depths: 128-row tiles stream more weight bytes per unit of MMA work,
+  // so they keep more packed stages in flight and one more dequantized stage
+  static constexpr int kXSt = kPfXStages;
+  static constexpr int kWSt = HALVES == 1 ? 8 : kPfWStages;
+  static constexpr int kBSt = HALVES == 1 ? 3 : kPfBStages;
   static constexpr int kX = kBM * kPfBK * 2;        // 16 KB per half
   static constexpr int kB = kPfBK * kPfBN * 2;      // 32768
   static constexpr int kW = kPfBK * kPfBN / 8 * 4;  // 8192
   static constexpr int kS = kPfBN * 2;              // 512
   static constexpr int kZ = kPfBN / 8 * 4;          // 128
   static constexpr int kWSlot = ((kW + kS + kZ) + 1023) / 1024 * 1024;
-  static constexpr size_t kOffB = (size_t)kX * kPfXStages;
-  static constexpr size_t kOffW = kOffB + (size_t)kB * kPfBStages;
-  static constexpr size_t kOffBars = kOffW + (size_t)kWSlot * kPfWStages;
+  static constexpr size_t kOffB = (size_t)kX * kXSt;
+  static constexpr size_t kOffW = kOffB + (size_t)kB * kBSt;
+  static constexpr size_t kOffBars = kOffW + (size_t)kWSlot * kWSt;
   static constexpr int kBars = 1024;  // barriers + TMEM slot
   static constexpr size_t kSmem = 1024 + kOffBars + kBars;
 };
@@ -185,7 +197,7 @@ __device__ __forceinline__ void pf_pairs(uint32_t q, uint32_t (&t)[4]) {
 }
 
 template <int DT, int ODT, int ORDER, int HALVES>
-__global__ void __launch_bounds__(kPfThreads, 1)
+__global__ void __launch_bounds__(pf_threads(HALVES), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                    const typename DType<DT>::T* __restrict__ bias,
@@ -193,17 +205,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                    uint32_t g, uint32_t ld_out, uint32_t split) {
   using L = PrefillLayout<HALVES>;
   constexpr int BM = L::kBM;
+  constexpr int kPfDqWarps = pf_dq_warps(HALVES);
   constexpr uint32_t kTmemCols = HALVES * kPfBN;
   using H = PfHalf2<DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* full_x = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
-  uint64_t* empty_x = full_x + kPfXStages;
-  uint64_t* full_w = empty_x + kPfXStages;
-  uint64_t* empty_w = full_w + kPfWStages;
-  uint64_t* bready = empty_w + kPfWStages;
-  uint64_t* bempty = bready + kPfBStages;
-  uint64_t* acc_full = bempty + kPfBStages;
+  uint64_t* empty_x = full_x + L::kXSt;
+  uint64_t* full_w = empty_x + L::kXSt;
+  uint64_t* empty_w = full_w + L::kWSt;
+  uint64_t* bready = empty_w + L::kWSt;
+  uint64_t* bempty = bready + L::kBSt;
+  uint64_t* acc_full = bempty + L::kBSt;
   uint64_t* drain_bar = acc_full + 1;  // the MMA thread's own MMAs, on a failed run
   uint64_t* recv_bar = drain_bar + 1;  // split K: the peers' partial sums have landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
@@ -220,29 +233,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int KT = static_cast<int>(k / kPfBK);
   const int kt0 = static_cast<int>((uint64_t)KT * rank / split);
   const int KTL = static_cast<int>((uint64_t)KT * (rank + 1) / split) - kt0;
-  const int rpo = BM / static_cast<int>(split);  // rows of the tile each CTA sums
+  // Split K: the tile's valid rows are dealt out to the CTAs of the cluster,
+  // rpo each (the last ones may get fewer or none); CTA q sums rows
+  // [q rpo, q rpo + own_rows).
+  // (128-row tiles). 256-row tiles: BM / split rows each, the CTA's own part
+  // summed straight from TMEM (their receive buffer would not fit).
+  const int vrows = min(BM, static_cast<int>(rows) - static_cast<int>(m0));
+  const int rpo = HALVES == 1 ? (vrows + static_cast<int>(split) - 1) / static_cast<int>(split)
+                              : BM / static_cast<int>(split);
+  const int own_rows =
+      HALVES == 1 ? max(0, min(rpo, vrows - static_cast<int>(rank) * rpo)) : rpo;
 
   auto x_slot = [&](int s) { return smem + (size_t)s * L::kX; };
   auto b_slot = [&](int s) { return smem + L::kOffB + (size_t)s * L::kB; };
   auto w_slot = [&](int s) { return smem + L::kOffW + (size_t)s * L::kWSlot; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPfXStages; ++s) {
+    for (int s = 0; s < L::kXSt; ++s) {
       mbar_init(&full_x[s], 1);
       mbar_init(&empty_x[s], 1);
     }
-    for (int s = 0; s < kPfWStages; ++s) {
+    for (int s = 0; s < L::kWSt; ++s) {
       mbar_init(&full_w[s], 1);
       mbar_init(&empty_w[s], 32 * kPfDqWarps);
     }
-    for (int s = 0; s < kPfBStages; ++s) {
+    for (int s = 0; s < L::kBSt; ++s) {
       mbar_init(&bready[s], 32 * kPfDqWarps);
       mbar_init(&bempty[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(drain_bar, 1);
     mbar_init(recv_bar, 1);
-    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rpo * kPfBN * 4);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * own_rows * kPfBN * 4);
     fence_mbarrier_init();
     fence_proxy_async_smem();
     tma_prefetch_desc(&tm_x);
@@ -260,7 +282,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       bool ok = true;
       int issued = 0;
       for (int i = 0; i < KTL && ok; ++i) {
-        const int s = i % kPfXStages, u = i / kPfXStages;
+        const int s = i % L::kXSt, u = i / L::kXSt;
         if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         mbar_arrive_expect_tx(&full_x[s], L::kX);
@@ -278,7 +300,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       int issued = 0;
       for (int i = 0; i < KTL && ok; ++i) {
         const int kt = kt0 + i;
-        const int s = i % kPfWStages, u = i / kPfWStages;
+        const int s = i % L::kWSt, u = i / L::kWSt;
         if (u > 0) ok = mbar_wait_bounded(&empty_w[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         uint8_t* b = w_slot(s);
@@ -299,8 +321,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       constexpr uint32_t idesc = umma_idesc_f16(DT == kBF16, 128, kPfBN);
       bool ok = true;
       for (int kt = 0; kt < KTL && ok; ++kt) {
-        const int sx = kt % kPfXStages, ux = kt / kPfXStages;
-        const int sb = kt % kPfBStages, ub = kt / kPfBStages;
+        const int sx = kt % L::kXSt, ux = kt / L::kXSt;
+        const int sb = kt % L::kBSt, ub = kt / L::kBSt;
         ok = mbar_wait_bounded(&full_x[sx], (uint32_t)(ux & 1)) &&
              mbar_wait_bounded(&bready[sb], (uint32_t)(ub & 1));
         if (!ok) break;
@@ -336,8 +358,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int l = lane & 7;    // packed word l + 8a, a = 0..3
     bool ok = true;
     for (int kt = 0; kt < KTL; ++kt) {
-      const int sw = kt % kPfWStages, uw = kt / kPfWStages;
-      const int sb = kt % kPfBStages, ub = kt / kPfBStages;
+      const int sw = kt % L::kWSt, uw = kt / L::kWSt;
+      const int sb = kt % L::kBSt, ub = kt / L::kBSt;
       if (ok) ok = mbar_wait_bounded(&full_w[sw], (uint32_t)(uw & 1));
       if (ok && ub > 0) ok = mbar_wait_bounded(&bempty[sb], (uint32_t)((ub - 1) & 1));
       if (ok) {
@@ -463,6 +485,70 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
     } else {
+      if constexpr (HALVES == 1) {
+      // Every CTA writes each valid row of its partial sums into slot [its
+      // rank] of the receive buffer [source][rpo rows][256 columns] of the
+      // row's owner (st.async to distributed shared memory for the peers,
+      // counted on their recv_bar; plain stores for its own rows), which
+      // reuses the rings. After the peers' bytes have landed and the
+      // epilogue warps have met, all of them sum the owned rows over the
+      // slots in rank order (deterministic) and store them.
+      float* recv = reinterpret_cast<float*>(smem);
+      const uint32_t bar_local = smem_u32(recv_bar);
+      if (ok) {
+#pragma unroll 1
+        for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
+          const int h = cc >> 3, c = cc & 7;
+          const int r = 128 * h + 32 * lq + lane;  // tile row
+          if (128 * h + 32 * lq >= vrows) continue;  // no valid row in this warp's quarter
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
+          if (r >= vrows) continue;
+          const uint32_t q = static_cast<uint32_t>(r / rpo);
+          float* dst = recv + ((size_t)rank * rpo + (r - (int)q * rpo)) * kPfBN + 32 * c;
+          if (q == rank) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            const uint32_t ra = map_shared_rank(smem_u32(dst), q);
+            const uint32_t rb = map_shared_rank(bar_local, q);
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_async_v4(ra + 4 * i, v[i], v[i + 1], v[i + 2], v[i + 3], rb);
+          }
+        }
+      }
+      const bool got = mbar_wait_bounded(recv_bar, 0u);
+      named_bar_sync(1, 32 * kPfDqWarps);  // this CTA's own rows are in place
+      if (ok && got) {
+        // owned rows x 64 column quads, spread over the epilogue threads
+        const int tid = threadIdx.x - 96;
+        for (int idx = tid; idx < own_rows * (kPfBN / 4); idx += 32 * kPfDqWarps) {
+          const int i = idx / (kPfBN / 4), c4 = idx - i * (kPfBN / 4);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (uint32_t src = 0; src < split; ++src) {
+            const float4 f = *reinterpret_cast<const float4*>(
+                recv + ((size_t)src * rpo + i) * kPfBN + 4 * c4);
+            acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
+          }
+          const uint32_t row = m0 + rank * rpo + i;
+          const uint32_t col = n0 + 4 * c4;
+          if (row < rows && col < n) {
+            float v4[4] = {acc.x, acc.y, acc.z, acc.w};
+            typename DType<ODT>::T* o = out + (size_t)row * ld_out + col;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (col + e < n) {
+                float vv = v4[e];
+                if (bias) vv += DType<DT>::to_f32(bias[col + e]);
+                o[e] = DType<ODT>::from_f32(vv);
+              }
+            }
+          }
+        }
+      }
+      } else {
       // CTA q owns tile rows [q rpo, (q+1) rpo). Each CTA sends the rows it
       // does not own to their owner (st.async into the owner's receive
       // buffer [source slot][row][256 columns], which reuses its rings;
@@ -522,6 +608,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           store(m0 + r, n0 + 32 * c, acc);
         }
       }
+      }
     }
   }
   // No copy this CTA issued may still be writing its shared memory when it
@@ -529,10 +616,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // stage issued into each ring slot.
   if (__syncthreads_or(role_ok ? 0 : 1) && threadIdx.x == 0) {
     const int xi = s_x_issued, wi = s_w_issued;
-    for (int j = xi > kPfXStages ? xi - kPfXStages : 0; j < xi; ++j)
-      mbar_wait_bounded(&full_x[j % kPfXStages], (uint32_t)((j / kPfXStages) & 1));
-    for (int j = wi > kPfWStages ? wi - kPfWStages : 0; j < wi; ++j)
-      mbar_wait_bounded(&full_w[j % kPfWStages], (uint32_t)((j / kPfWStages) & 1));
+    for (int j = xi > L::kXSt ? xi - L::kXSt : 0; j < xi; ++j)
+      mbar_wait_bounded(&full_x[j % L::kXSt], (uint32_t)((j / L::kXSt) & 1));
+    for (int j = wi > L::kWSt ? wi - L::kWSt : 0; j < wi; ++j)
+      mbar_wait_bounded(&full_w[j % L::kWSt], (uint32_t)((j / L::kWSt) & 1));
   }
   tc_fence_before();
   __syncthreads();
@@ -607,7 +694,7 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
   cfg.gridDim = dim3(static_cast<uint32_t>((p.n + kPfBN - 1) / kPfBN),
                      static_cast<uint32_t>((p.rows + L::kBM - 1) / L::kBM),
                      static_cast<uint32_t>(split));
-  cfg.blockDim = dim3(kPfThreads);
+  cfg.blockDim = dim3(pf_threads(L::kBM / 128));
   cfg.dynamicSmemBytes = L::kSmem;
   cfg.stream = p.stream;
   cudaLaunchAttribute attr[1];
@@ -654,6 +741,45 @@ cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const De
 
 // One 128-row half up to 128 rows, else two; split K over a cluster while the
 // tiles alone would leave more than half of the SMs idle.
+// Clusters of `split` CTAs (one per SM: the tile's shared memory) that can be
+// resident at once on the current device, from the occupancy calculator;
+// cached per (device, tile height, split). 0 if the query fails.
+template <int HALVES>
+static int pf_max_active_clusters(int device, int split) {
+  static std::mutex mu;
+  static int cache[64][4] = {};  // [device][log2 split - 1], 0 = not yet asked
+  int lg = 0;
+  while ((2 << lg) < split) ++lg;
+  if (device < 0 || device >= 64 || lg > 3) return 0;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[device][lg] != 0) return cache[device][lg] > 0 ? cache[device][lg] : 0;
+  using L = PrefillLayout<HALVES>;
+  auto kern = prefill_kernel<kF16, kF16, kOrderAwq, HALVES>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(L::kSmem)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, static_cast<unsigned>(split));
+    cfg.blockDim = dim3(pf_threads(HALVES));
+    cfg.dynamicSmemBytes = L::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = static_cast<unsigned>(split);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+  } else {
+    (void)cudaGetLastError();
+  }
+  cache[device][lg] = n > 0 ? n : -1;
+  return n;
+}
+
 cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   cawq_plan pl = {};
   pl.path = CAWQ_PATH_PREFILL;
@@ -667,6 +793,15 @@ cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   const int max_split = pl.warps == 1 ? kPfMaxSplit : 4;
   int split = 1;
   while (split < max_split && tiles * split * 2 <= sms && kt >= (size_t)split * 2 * 4) split *= 2;
+  // all clusters in one wave: a cluster needs `split` SMs of one GPC at once,
+  // and a tile count above what fits leaves the last clusters for a second
+  // wave (measured: Qwen2 qkv at M = 64, 18 clusters of 8 -> 24 us, of 4 -> 17 us)
+  while (split > 1) {
+    const int act = pl.warps == 1 ? pf_max_active_clusters<1>(dev.device, split)
+                                  : pf_max_active_clusters<2>(dev.device, split);
+    if (act <= 0 || tiles <= (size_t)act) break;
+    split /= 2;
+  }
   pl.split = split;
   return pl;
 }

@@ -339,7 +339,13 @@ def test_prefill_every_plan(cuda_device, halves, split, rows, dtype):
 
 
 def test_planner_splits_k_for_mid_m(cuda_device):
-    p = cawq.plan_get(64, 3584, 4608, 64, torch.float16)
+    # Qwen2 o_proj at M = 64: 14 output tiles -> clusters of 8 CTAs along K;
+    # qkv: 18 tiles, of which only 16 clusters of 8 (one CTA per SM) are
+    # resident at once on a B200, so the planner halves the split instead of
+    # leaving two clusters for a second wave
+    p = cawq.plan_get(64, 3584, 3584, 64, torch.float16)
     assert p["path"] == PATH_PREFILL and p["warps"] == 1 and p["split"] == 8
+    p = cawq.plan_get(64, 3584, 4608, 64, torch.float16)
+    assert p["path"] == PATH_PREFILL and p["warps"] == 1 and p["split"] == 4
     p = cawq.plan_get(2048, 4096, 4096, 128, torch.float16)
     assert p["path"] == PATH_PREFILL and p["warps"] == 2 and p["split"] == 1
