@@ -490,9 +490,11 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
       // rank] of the receive buffer [source][rpo rows][256 columns] of the
       // row's owner (st.async to distributed shared memory for the peers,
       // counted on their recv_bar; plain stores for its own rows), which
-      // reuses the rings. After the peers' bytes have landed and the
-      // epilogue warps have met, all of them sum the owned rows over the
-      // slots in rank order (deterministic) and store them.
+      // reuses the rings. A lane writes one row, so the 16-byte chunk c of
+      // row r sits at c ^ (r & 7): the 8 rows of a store land in 8 different
+      // bank groups. After the peers' bytes have landed and the epilogue
+      // warps have met, all of them sum the owned rows over the slots in rank
+      // order (deterministic) and store them.
       float* recv = reinterpret_cast<float*>(smem);
       const uint32_t bar_local = smem_u32(recv_bar);
       if (ok) {
@@ -505,17 +507,20 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
           if (r >= vrows) continue;
           const uint32_t q = static_cast<uint32_t>(r / rpo);
-          float* dst = recv + ((size_t)rank * rpo + (r - (int)q * rpo)) * kPfBN + 32 * c;
+          const int lr = r - (int)q * rpo;  // row inside the owner's slot
+          float* dst = recv + ((size_t)rank * rpo + lr) * kPfBN + 32 * c;
+          const int sw = lr & 7;
           if (q == rank) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<float4*>(dst + 4 * (i ^ sw)) =
+                  make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           } else {
             const uint32_t ra = map_shared_rank(smem_u32(dst), q);
             const uint32_t rb = map_shared_rank(bar_local, q);
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              st_async_v4(ra + 4 * i, v[i], v[i + 1], v[i + 2], v[i + 3], rb);
+            for (int i = 0; i < 8; ++i)
+              st_async_v4(ra + 16 * (i ^ sw), v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3], rb);
           }
         }
       }
@@ -527,9 +532,10 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
         for (int idx = tid; idx < own_rows * (kPfBN / 4); idx += 32 * kPfDqWarps) {
           const int i = idx / (kPfBN / 4), c4 = idx - i * (kPfBN / 4);
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          const int pc4 = c4 ^ (i & 7);  // swizzled chunk of row i
           for (uint32_t src = 0; src < split; ++src) {
             const float4 f = *reinterpret_cast<const float4*>(
-                recv + ((size_t)src * rpo + i) * kPfBN + 4 * c4);
+                recv + ((size_t)src * rpo + i) * kPfBN + 4 * pc4);
             acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
           }
           const uint32_t row = m0 + rank * rpo + i;
