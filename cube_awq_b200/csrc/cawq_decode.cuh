@@ -292,17 +292,23 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       // power-of-two scale: |x| < 2^(e+1) over the row's 64 values, so
       // x * 2^(14 - e) rounds into [-2^15, 2^15). The integer splits into a
       // signed high byte and an unsigned low byte (x_int = 256 hi + lo), each
-      // the B operand of one integer MMA. Lane L writes the B fragments of
-      // consumer lane L = (gq, t): column gq is X row gq >> 1, column variant
-      // gq & 1; its k rows are 2t, 2t + 1 (+ 8) of each 16-row step, one byte
-      // each at byte position variant (+ 2); the other bytes are zero. Row r
+      // the B operand of one integer MMA. Consumer lane (gq, t) reads B column
+      // gq = (X row gq >> 1, variant gq & 1): per 16-row step st, word b0 holds
+      // the digits of k rows 16 st + 2t, +1 at bytes (variant, variant + 2),
+      // b1 those of 16 st + 8 + 2t, +1. Lane L here converts exactly the k
+      // pair (2L, 2L + 1) of every live row, i.e. step L >> 3, word
+      // (L >> 2) & 1, t = L & 3, and writes it for both variants. The words of
+      // the other B columns stay zero (the tables are cleared once). Row r
       // also gets {1 / scale, sum(x_int) / scale}.
-      const int rr = gq >> 1;
-      const int vv = gq & 1;
-      const bool live = rr < (int)rows_eff;
-      const uint32_t sel_hi = vv ? 0x5010u : 0x0501u;  // byte 1 of each k's integer
-      const uint32_t sel_lo = vv ? 0x4000u : 0x0400u;  // byte 0
-      const uint32_t vmask = vv ? 0xFF00FF00u : 0x00FF00FFu;
+      for (int b = 0; b < kDecI8BSlots; ++b) {
+        uint4* tab = reinterpret_cast<uint4*>(btabs + (size_t)b * kDecI8BSlot);
+        for (int i = lane; i < kDecI8BTable / 16; i += 32) tab[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+      const int st_l = lane >> 3;            // 16-row step of this lane's k pair
+      const int wsel = (lane >> 2) & 1;      // b0 (0) or b1 (1)
+      const int tl = lane & 3;               // t of the consumer lanes served
+      const int chunk = lane >> 2;           // 16-byte chunk of the X row (k = 2 lane)
       for (int j = 0; j < nst && ok; ++j) {
         const int sl = j % NS;
         const int bs = j % kDecI8BSlots;
@@ -312,58 +318,40 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
           ok = mbar_wait_bounded(&bempty[bs], static_cast<uint32_t>(((j / kDecI8BSlots) - 1) & 1));
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        uint8_t* sbase = smem + sl * slot;
+        const uint8_t* sbase = smem + sl * slot;
         uint8_t* tbase = btabs + (size_t)bs * kDecI8BSlot;
-        float xv[16];  // [4 st + 2 p + i]: k row 16 st + 8 p + 2 t + i of row rr
+        uint32_t* tab32 = reinterpret_cast<uint32_t*>(tbase);
+        float2* info = reinterpret_cast<float2*>(tbase + kDecI8BTable);
+        for (int r = 0; r < (int)rows_eff; ++r) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(
+              sbase + r * 128 + ((chunk ^ (r & 7)) << 4) + ((lane & 3) << 2));
+          const T* h = reinterpret_cast<const T*>(&w);
+          const float x0 = DType<DT>::to_f32(h[0]), x1 = DType<DT>::to_f32(h[1]);
+          float mx = fmaxf(fabsf(x0), fabsf(x1));
 #pragma unroll
-        for (int st = 0; st < 4; ++st) {
+          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          // e = floor(log2 mx) from the exponent field (0 and subnormals give a
+          // tiny e, clamped so that both scales stay normal floats)
+          const int e = max(static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu) - 127, -100);
+          const float scale = __uint_as_float(static_cast<uint32_t>(127 + 14 - e) << 23);
+          const float inv = __uint_as_float(static_cast<uint32_t>(127 - 14 + e) << 23);
+          const int i0 = min(__float2int_rn(x0 * scale), 32767);
+          const int i1 = min(__float2int_rn(x1 * scale), 32767);
+          int sum = i0 + i1;
 #pragma unroll
-          for (int pp = 0; pp < 2; ++pp) {
-            uint32_t w = 0u;
-            if (live) {
-              const int kk = 16 * st + 8 * pp + 2 * t;  // 16-byte chunk kk >> 3 of the row
-              w = *reinterpret_cast<const uint32_t*>(sbase + rr * 128 +
-                                                     (((kk >> 3) ^ (rr & 7)) << 4) + ((kk & 7) << 1));
-            }
-            const T* h = reinterpret_cast<const T*>(&w);
-            xv[4 * st + 2 * pp] = DType<DT>::to_f32(h[0]);
-            xv[4 * st + 2 * pp + 1] = DType<DT>::to_f32(h[1]);
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          const uint32_t hi = prmt(static_cast<uint32_t>(i0), static_cast<uint32_t>(i1), 0x0501u) &
+                              0x00FF00FFu;  // high bytes of k, k + 1 at bytes 0, 2
+          const uint32_t lo = prmt(static_cast<uint32_t>(i0), static_cast<uint32_t>(i1), 0x0400u) &
+                              0x00FF00FFu;  // low bytes
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const int cl = 4 * (2 * r + v) + tl;  // consumer lane served
+            uint32_t* ent = tab32 + ((size_t)st_l * 32 + cl) * 4;
+            ent[wsel] = hi << (8 * v);
+            ent[2 + wsel] = lo << (8 * v);
           }
-        }
-        float mx = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(xv[i]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        // e = floor(log2 mx) from the exponent field (0 and subnormals give a
-        // tiny e, clamped so that both scales stay normal floats)
-        const int e = max(static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu) - 127, -100);
-        const float scale = __uint_as_float(static_cast<uint32_t>(127 + 14 - e) << 23);
-        const float inv = __uint_as_float(static_cast<uint32_t>(127 - 14 + e) << 23);
-        int xi[16];
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          xi[i] = min(__float2int_rn(xv[i] * scale), 32767);
-          sum += xi[i];
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        uint4* btab = reinterpret_cast<uint4*>(tbase);
-#pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          const uint32_t p0 = static_cast<uint32_t>(xi[4 * st]), p1 = static_cast<uint32_t>(xi[4 * st + 1]);
-          const uint32_t q0 = static_cast<uint32_t>(xi[4 * st + 2]), q1 = static_cast<uint32_t>(xi[4 * st + 3]);
-          uint4 w;
-          w.x = prmt(p0, p1, sel_hi) & vmask;  // b0, high bytes
-          w.y = prmt(q0, q1, sel_hi) & vmask;  // b1, high bytes
-          w.z = prmt(p0, p1, sel_lo) & vmask;  // b0, low bytes
-          w.w = prmt(q0, q1, sel_lo) & vmask;  // b1, low bytes
-          btab[st * 32 + lane] = w;
-        }
-        if (t == 0 && vv == 0 && rr < kDecI8MaxRows) {
-          float2* info = reinterpret_cast<float2*>(tbase + kDecI8BTable);
-          info[rr] = make_float2(inv, static_cast<float>(sum) * inv);
+          if (lane == 0) info[r] = make_float2(inv, static_cast<float>(sum) * inv);
         }
         __syncwarp();
         if (lane == 0) {
