@@ -17,10 +17,12 @@ from . import _lib
 from .errors import (CubeAwqError, DeviceTimeoutError, DTypeError, ShapeError,
                      UnsupportedDeviceError)
 from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, awq_gemm_linear,
-                     dequantize_awq, dequantize_native, device_error, gemm, plan_cache_clear,
-                     plan_get, plan_set, select_tile_m, select_tile_n, validate_decode_launch_params,
-                     validate_launch_params, version)
-from .modules import AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear, AWQLinearConfig
+                     dequantize_awq, dequantize_native, device_error, gemm, gemm_silu_mul,
+                     interleave_gate_up, plan_cache_clear, plan_get, plan_set, select_tile_m,
+                     select_tile_n, validate_decode_launch_params, validate_launch_params,
+                     version)
+from .modules import (AWQGateUpSiluMul, AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear,
+                      AWQLinearConfig)
 from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
 from .loader import load_awq_linears
 
@@ -35,11 +37,12 @@ if _os.path.exists(_lib.LIB_PATH):
         pass
 
 __all__ = [
-    "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
+    "AWQGateUpSiluMul", "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
     "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "load_awq_linears",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
-    "dequantize_awq", "dequantize_native", "device_error", "gemm", "plan_cache_clear",
+    "dequantize_awq", "dequantize_native", "device_error", "gemm", "gemm_silu_mul",
+    "interleave_gate_up", "plan_cache_clear",
     "plan_get", "plan_set", "select_tile_m", "select_tile_n", "validate_decode_launch_params",
     "validate_launch_params", "version",
 ]

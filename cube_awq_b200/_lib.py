@@ -41,6 +41,7 @@ EXPORTED = (
     "cawq_validate_launch_params", "cawq_validate_decode_launch_params",
     "cawq_select_tile_m", "cawq_select_tile_n",
     "cawq_awq_gemm_linear", "cawq_gemm", "cawq_gemm_with_plan",
+    "cawq_gemm_silu_mul", "cawq_gemm_silu_mul_with_plan", "cawq_interleave_gate_up",
     "cawq_plan_get", "cawq_plan_set", "cawq_plan_cache_clear", "cawq_autotune",
     "cawq_dequantize_native", "cawq_dequantize",
     "cawq_tp_column_shard", "cawq_tp_row_shard", "cawq_tp_interleave_columns",
@@ -116,6 +117,13 @@ def _declare(L) -> None:
     L.cawq_gemm.restype = st
     L.cawq_gemm_with_plan.argtypes = gemm_args + [ctypes.POINTER(PlanC), vp]
     L.cawq_gemm_with_plan.restype = st
+    silu_args = [vp, u32p, u32p, vp, vp, vp, sz, sz, sz, sz, i, sz]
+    L.cawq_gemm_silu_mul.argtypes = silu_args + [vp]
+    L.cawq_gemm_silu_mul.restype = st
+    L.cawq_gemm_silu_mul_with_plan.argtypes = silu_args + [ctypes.POINTER(PlanC), vp]
+    L.cawq_gemm_silu_mul_with_plan.restype = st
+    L.cawq_interleave_gate_up.argtypes = [vp, vp, sz, sz, sz, sz, vp]
+    L.cawq_interleave_gate_up.restype = st
     L.cawq_plan_get.argtypes = [sz, sz, sz, sz, i, ctypes.POINTER(PlanC)]
     L.cawq_plan_get.restype = st
     L.cawq_plan_set.argtypes = [sz, sz, sz, sz, i, ctypes.POINTER(PlanC)]

@@ -270,7 +270,7 @@ static bool plan_supports(const GemmProblem& p, const cawq_plan& plan, const Dev
   switch (plan.path) {
     case CAWQ_PATH_DECODE: return decode_supports(p, plan, dev);
     case CAWQ_PATH_PREFILL: return prefill_supports(p, plan, dev);
-    case CAWQ_PATH_GENERIC: return generic_supports(p);
+    case CAWQ_PATH_GENERIC: return p.epi == 0 && generic_supports(p);
     default: return false;
   }
 }
@@ -341,15 +341,17 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
                                const void* scales, const void* bias, void* out, size_t rows,
                                size_t k, size_t n, size_t g, cawq_dtype dtype,
                                cawq_dtype out_dtype, cawq_order order, size_t ld_out,
-                               const cawq_plan* plan, void* stream, bool module_rules) {
+                               const cawq_plan* plan, void* stream, bool module_rules,
+                               int epi = 0) {
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype))
     return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
   if (out_dtype != dtype && out_dtype != CAWQ_F32)
     return fail(CAWQ_ERR_DTYPE, "out_dtype must equal dtype or be CAWQ_F32");
   if (order != CAWQ_ORDER_AWQ && order != CAWQ_ORDER_NATURAL)
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "order must be CAWQ_ORDER_AWQ or CAWQ_ORDER_NATURAL");
-  if (ld_out == 0) ld_out = n;
-  if (ld_out < n) return fail(CAWQ_ERR_INVALID_SHAPE, "ld_out must be >= n");
+  const size_t ocols = epi ? n / 2 : n;  // output columns
+  if (ld_out == 0) ld_out = ocols;
+  if (ld_out < ocols) return fail(CAWQ_ERR_INVALID_SHAPE, epi ? "ld_out must be >= n / 2" : "ld_out must be >= n");
   if (module_rules) {
     if (!(k > 0)) return fail(CAWQ_ERR_INVALID_SHAPE, "input last dim (K) must be > 0");
     if (order == CAWQ_ORDER_AWQ) {
@@ -372,7 +374,7 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
   DeviceInfo dev;
   if ((st = require_sm100(&dev)) != CAWQ_OK) return st;
   GemmProblem p = {x, qweight, qzeros, scales, bias, out, rows, k, n, g, ld_out,
-                   dtype, out_dtype, order, static_cast<cudaStream_t>(stream)};
+                   dtype, out_dtype, order, static_cast<cudaStream_t>(stream), epi};
   cawq_plan pl = plan ? *plan : choose_plan(p, dev);
   if (plan && !plan_supports(p, pl, dev))
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "the plan cannot run this problem");
@@ -529,6 +531,54 @@ CAWQ_API cawq_status cawq_gemm(const void* x, const uint32_t* qweight, const uin
                                void* stream) {
   return gemm_common(x, qweight, qzeros, scales, bias, out, rows, k, n, group_size, dtype,
                      out_dtype, order, ld_out, nullptr, stream, true);
+}
+
+CAWQ_API cawq_status cawq_gemm_silu_mul(const void* x, const uint32_t* qweight,
+                                        const uint32_t* qzeros, const void* scales,
+                                        const void* bias, void* out, size_t rows, size_t k,
+                                        size_t n, size_t group_size, cawq_dtype dtype,
+                                        size_t ld_out, void* stream) {
+  if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
+    return fail(CAWQ_ERR_DTYPE, "the SiLU-gated GEMM takes CAWQ_F16 or CAWQ_BF16");
+  if (n % 256 != 0)
+    return fail(CAWQ_ERR_INVALID_SHAPE,
+                fmt("n = %zu must be a multiple of 256 (128-column gate / up blocks)", n));
+  return gemm_common(x, qweight, qzeros, scales, bias, out, rows, k, n, group_size, dtype, dtype,
+                     CAWQ_ORDER_AWQ, ld_out, nullptr, stream, true, 1);
+}
+
+CAWQ_API cawq_status cawq_interleave_gate_up(const void* src, void* dst, size_t rows,
+                                             size_t width_elems, size_t block_elems,
+                                             size_t elem_size, void* stream) {
+  if (!src || !dst) return fail(CAWQ_ERR_NULL_POINTER, "src and dst must be non-null");
+  if (elem_size != 2 && elem_size != 4)
+    return fail(CAWQ_ERR_INVALID_ARGUMENT, "elem_size must be 2 or 4");
+  if (block_elems == 0 || width_elems % block_elems != 0)
+    return fail(CAWQ_ERR_INVALID_SHAPE, "width_elems must be a multiple of block_elems");
+  if (rows == 0 || width_elems == 0) return CAWQ_OK;
+  DeviceInfo dev;
+  cawq_status st = require_sm100(&dev);
+  if (st != CAWQ_OK) return st;
+  cudaError_t e = launch_interleave_gate_up(src, dst, rows, width_elems, block_elems, elem_size,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "interleave launch");
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_gemm_silu_mul_with_plan(const void* x, const uint32_t* qweight,
+                                                  const uint32_t* qzeros, const void* scales,
+                                                  const void* bias, void* out, size_t rows,
+                                                  size_t k, size_t n, size_t group_size,
+                                                  cawq_dtype dtype, size_t ld_out,
+                                                  const cawq_plan* plan, void* stream) {
+  if (!plan) return fail(CAWQ_ERR_NULL_POINTER, "plan must be non-null");
+  if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
+    return fail(CAWQ_ERR_DTYPE, "the SiLU-gated GEMM takes CAWQ_F16 or CAWQ_BF16");
+  if (n % 256 != 0)
+    return fail(CAWQ_ERR_INVALID_SHAPE,
+                fmt("n = %zu must be a multiple of 256 (128-column gate / up blocks)", n));
+  return gemm_common(x, qweight, qzeros, scales, bias, out, rows, k, n, group_size, dtype, dtype,
+                     CAWQ_ORDER_AWQ, ld_out, plan, stream, true, 1);
 }
 
 CAWQ_API cawq_status cawq_gemm_with_plan(const void* x, const uint32_t* qweight,

@@ -122,7 +122,11 @@ __host__ __device__ constexpr int dec_max_consumers(int mt) { return mt == 1 ? 1
 
 // The integer path runs at most kDecI8MaxStrips strips and keeps 3 CTAs per
 // SM within the register file.
-template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8>
+// EPI 1: gate / up columns interleaved in 128-column blocks (strips 2j and
+// 2j + 1 of a band are a gate block and its up block); the kernel writes
+// silu(gate) * up (bias, if any, added to both first) to an [rows, n / 2]
+// output, column (band column base) / 2 + pair index.
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0>
 __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
                                      : dec_max_consumers(MT) * 32 + 32,
                                   I8 ? 3 : 1)
@@ -899,6 +903,44 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   // slot [its rank] of q's receive buffer (st.async to distributed shared
   // memory, counted on q's recv_bar), then sums its own columns over the
   // slots in rank order. One wait, no cluster-wide barrier at the end.
+  // SiLU-gated output of pair index pi of this band from its gate / up sums
+  auto store_pair = [&](uint32_t row, uint32_t pi, float gv, float uv) {
+    const uint32_t wcol = pband * 8 + (pi / 128) * 256 + (pi & 127u);  // gate weight column
+    if (wcol >= n) return;
+    if (bias) {
+      gv += DType<DT>::to_f32(bias[wcol]);
+      uv += DType<DT>::to_f32(bias[wcol + 128]);
+    }
+    out[(size_t)row * ld_out + pband * 4 + pi] = DType<ODT>::from_f32(silu_mul(gv, uv));
+  };
+  if (split == 1 && EPI == 1) {
+    // the band's sums meet in the receive buffer (unused without split K):
+    // [row][band column], then the consumer threads pair gate with up
+    if (warp < consumers) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const uint32_t row = static_cast<uint32_t>(8 * m + 2 * t + e);
+          if (row >= rows_eff) continue;
+          float* dst = recv + (size_t)row * bcols + strip * kDecTileCols + 8 * oword;
+          reinterpret_cast<float4*>(dst)[0] =
+              make_float4(outv[m][e][0], outv[m][e][1], outv[m][e][2], outv[m][e][3]);
+          reinterpret_cast<float4*>(dst)[1] =
+              make_float4(outv[m][e][4], outv[m][e][5], outv[m][e][6], outv[m][e][7]);
+        }
+      }
+      named_bar_sync(1, 32 * consumers);
+      const uint32_t npairs = bcols / 2;
+      for (uint32_t idx = threadIdx.x; idx < rows_eff * npairs; idx += 32 * consumers) {
+        const uint32_t row = idx / npairs, pi = idx - row * npairs;
+        const uint32_t gb = (pi / 128) * 256 + (pi & 127u);  // band column of the gate
+        store_pair(row, pi, recv[(size_t)row * bcols + gb], recv[(size_t)row * bcols + gb + 128]);
+      }
+    }
+    drain();
+    return;
+  }
   if (split == 1) {
     if (warp < consumers) {
 #pragma unroll
@@ -934,8 +976,20 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
         if (row >= rows_eff) continue;
         const float* v = outv[m][e];  // this lane's 8 consecutive columns
         const uint32_t col8 = static_cast<uint32_t>(strip * kDecTileCols + 8 * oword);
-        const uint32_t q = col8 / ncols;
-        float* dst = recv + ((size_t)rank * XB + row) * ncols + (col8 - q * ncols);
+        // owner and place in its slot: plain, column slices of the band;
+        // EPI 1, slices of the band's gate / up pairs (gate part, then up part)
+        uint32_t q, pos;
+        if constexpr (EPI == 1) {
+          const uint32_t npair = ncols / 2;
+          const uint32_t w = col8 & 255u;
+          const uint32_t pi = (col8 / 256) * 128 + (w & 127u);
+          q = pi / npair;
+          pos = (pi - q * npair) + (w >= 128 ? npair : 0u);
+        } else {
+          q = col8 / ncols;
+          pos = col8 - q * ncols;
+        }
+        float* dst = recv + ((size_t)rank * XB + row) * ncols + pos;
         if (q == rank) {
           reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
           reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -951,14 +1005,28 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   // the peers' bytes (bounded wait), and this CTA's own stores
   if (!mbar_wait_bounded(recv_bar, 0u)) ok = false;
   __syncthreads();
-  for (uint32_t idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
-    const uint32_t row = idx / ncols, c = idx - row * ncols;
-    const uint32_t col = pband * 8 + rank * ncols + c;
-    float v = 0.f;
-    for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
-    if (col < n) {
-      if (bias) v += DType<DT>::to_f32(bias[col]);
-      out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
+  if constexpr (EPI == 1) {
+    const uint32_t npair = ncols / 2;
+    for (uint32_t idx = threadIdx.x; idx < rows_eff * npair; idx += blockDim.x) {
+      const uint32_t row = idx / npair, p = idx - row * npair;
+      float gv = 0.f, uv = 0.f;
+      for (uint32_t src = 0; src < split; ++src) {
+        const float* rp = recv + ((size_t)src * XB + row) * ncols;
+        gv += rp[p];
+        uv += rp[p + npair];
+      }
+      store_pair(row, rank * npair + p, gv, uv);
+    }
+  } else {
+    for (uint32_t idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
+      const uint32_t row = idx / ncols, c = idx - row * ncols;
+      const uint32_t col = pband * 8 + rank * ncols + c;
+      float v = 0.f;
+      for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
+      if (col < n) {
+        if (bias) v += DType<DT>::to_f32(bias[col]);
+        out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
+      }
     }
   }
   drain();
@@ -980,7 +1048,7 @@ static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 // warp hold fewer CTAs per SM, which costs more than its faster inner loop
 // gains in chains of dependent launches.
 static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
-  return plan.reserved[2] == 1 && p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
+  return plan.reserved[2] == 1 && p.epi == 0 && p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
          p.g % kDecStageRows == 0 && plan.warps <= kDecI8MaxStrips;
 }
 
@@ -1009,13 +1077,17 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
     return false;
   if (plan.stages < 1 || plan.stages > kDecMaxStages) return false;
   if (plan.reserved[2] < 0 || plan.reserved[2] > 1) return false;
+  // SiLU-gated epilogue: whole 256-column gate / up blocks, AWQ order, output
+  // in the input dtype
+  if (p.epi == 1 && (p.n % 256 != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype))
+    return false;
   const size_t bands =
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps);
   if (bands * plan.split >= (1ull << 31)) return false;
   return decode_smem(p, plan) <= dev.smem_optin && dev.cc_major == 10;
 }
 
-template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8>
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0>
 static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
@@ -1034,7 +1106,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                  CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA, I8>;
+  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA, I8, EPI>;
   const size_t smem = decode_smem(p, plan);
   // function attributes are per process; set each once (a repeat is harmless)
   static size_t smem_set = 0;
@@ -1089,6 +1161,16 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
 template <int DT, int ODT, int ORDER>
 static cudaError_t launch_decode_m(const GemmProblem& p, const cawq_plan& plan) {
   const bool ga = p.g % kDecStageRows == 0;  // groups end on stage boundaries
+  if constexpr (DT == ODT && ORDER == kOrderAwq) {
+    if (p.epi == 1) {
+      if (decode_mt(p.rows) == 1) {
+        return ga ? launch_decode_t<DT, ODT, ORDER, 1, true, false, 1>(p, plan)
+                  : launch_decode_t<DT, ODT, ORDER, 1, false, false, 1>(p, plan);
+      }
+      return ga ? launch_decode_t<DT, ODT, ORDER, 2, true, false, 1>(p, plan)
+                : launch_decode_t<DT, ODT, ORDER, 2, false, false, 1>(p, plan);
+    }
+  }
   if constexpr (DT != kF32) {
     if (decode_use_i8(p, plan)) return launch_decode_t<DT, ODT, ORDER, 1, true, true>(p, plan);
   }

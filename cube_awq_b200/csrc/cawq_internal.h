@@ -28,6 +28,9 @@ struct GemmProblem {
   size_t rows, k, n, g, ld_out;
   int dtype, out_dtype, order;
   cudaStream_t stream;
+  // epilogue: 0 = plain; 1 = SiLU-gated product of block-interleaved gate/up
+  // columns (128-column blocks: gate, up, gate, ...): out [rows, n / 2]
+  int epi = 0;
 };
 
 // Thread-local error message (cawq_last_error).
@@ -78,6 +81,8 @@ cudaError_t launch_dequant(const uint32_t* qw, const uint32_t* qz, const void* s
                            size_t k, size_t n, size_t g, int dtype, int order,
                            cudaStream_t stream, int sm_count);
 
+cudaError_t launch_interleave_gate_up(const void* src, void* dst, size_t rows, size_t width_e,
+                                      size_t block_e, size_t elem, cudaStream_t stream);
 cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, size_t n,
                                       int world, size_t elem, cudaStream_t stream);
 cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* out, size_t rows,

@@ -196,7 +196,11 @@ __device__ __forceinline__ void pf_pairs(uint32_t q, uint32_t (&t)[4]) {
   }
 }
 
-template <int DT, int ODT, int ORDER, int HALVES>
+// EPI 1: gate / up columns interleaved in 128-column blocks, so each 256-column
+// tile holds 128 gate columns and their 128 up columns; the epilogue writes
+// silu(gate) * up (bias, if any, added to both first) to output columns
+// [n0 / 2, n0 / 2 + 128) of an [rows, n / 2] output.
+template <int DT, int ODT, int ORDER, int HALVES, int EPI = 0>
 __global__ void __launch_bounds__(pf_threads(HALVES), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
@@ -474,14 +478,57 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
         }
       }
     };
+    // EPI 1: weight columns gcol (gate) and gcol + 128 (up) of tile n0 ->
+    // output column (n0 / 2) + (gcol - n0), written 32 at a time
+    auto store_silu = [&](uint32_t row, uint32_t gcol, float (&v)[32], float (&u)[32]) {
+      if (row >= rows || gcol >= n) return;
+      const uint32_t ocol = n0 / 2 + (gcol - n0);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float gv = v[i], uv = u[i];
+        if (bias) {
+          gv += DType<DT>::to_f32(bias[gcol + i]);
+          uv += DType<DT>::to_f32(bias[gcol + 128 + i]);
+        }
+        v[i] = silu_mul(gv, uv);
+      }
+      using OT = typename DType<ODT>::T;
+      OT* o = out + (size_t)row * ld_out + ocol;
+      // 16-byte stores: a lane owns one row, so 2-byte stores would reach L2
+      // as 16 partial writes of each 32-byte sector
+      if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 pk;
+          OT* hp = reinterpret_cast<OT*>(&pk);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hp[e] = DType<ODT>::from_f32(v[i + e]);
+          *reinterpret_cast<uint4*>(o + i) = pk;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = DType<ODT>::from_f32(v[i]);
+      }
+    };
     if (split == 1) {
-      if (ok) {
+      if (ok && EPI == 0) {
 #pragma unroll 1
         for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
           const int h = cc >> 3, c = cc & 7;
           float v[32];
           tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
           store(m0 + 128 * h + 32 * lq + lane, n0 + 32 * c, v);
+        }
+      } else if (ok) {
+        // gate chunk c (columns 32c) with its up chunk (128 + 32c)
+        constexpr int kGate = HALVES * 4 / (kPfDqWarps / 4);
+#pragma unroll 1
+        for (int gc = part * kGate; gc < (part + 1) * kGate; ++gc) {
+          const int h = gc >> 2, c = gc & 3;
+          float v[32], u[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 32 * c, v);
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(32 * lq) << 16) + h * kPfBN + 128 + 32 * c, u);
+          store_silu(m0 + 128 * h + 32 * lq + lane, n0 + 32 * c, v, u);
         }
       }
     } else {
@@ -526,7 +573,37 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
       }
       const bool got = mbar_wait_bounded(recv_bar, 0u);
       named_bar_sync(1, 32 * kPfDqWarps);  // this CTA's own rows are in place
-      if (ok && got) {
+      if (ok && got && EPI == 1) {
+        // owned rows x 32 gate column quads (each with its up quad)
+        const int tid = threadIdx.x - 96;
+        for (int idx = tid; idx < own_rows * (kPfBN / 8); idx += 32 * kPfDqWarps) {
+          const int i = idx / (kPfBN / 8), c4 = idx - i * (kPfBN / 8);
+          float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), ua = ga;
+          const int pg = c4 ^ (i & 7), pu = (c4 + 32) ^ (i & 7);
+          for (uint32_t src = 0; src < split; ++src) {
+            const float* rowp = recv + ((size_t)src * rpo + i) * kPfBN;
+            const float4 f = *reinterpret_cast<const float4*>(rowp + 4 * pg);
+            const float4 e = *reinterpret_cast<const float4*>(rowp + 4 * pu);
+            ga.x += f.x; ga.y += f.y; ga.z += f.z; ga.w += f.w;
+            ua.x += e.x; ua.y += e.y; ua.z += e.z; ua.w += e.w;
+          }
+          const uint32_t row = m0 + rank * rpo + i;
+          const uint32_t gcol = n0 + 4 * c4;
+          if (row < rows && gcol < n) {
+            const float gv[4] = {ga.x, ga.y, ga.z, ga.w}, uv[4] = {ua.x, ua.y, ua.z, ua.w};
+            typename DType<ODT>::T* o = out + (size_t)row * ld_out + n0 / 2 + 4 * c4;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float g1 = gv[e], u1 = uv[e];
+              if (bias) {
+                g1 += DType<DT>::to_f32(bias[gcol + e]);
+                u1 += DType<DT>::to_f32(bias[gcol + 128 + e]);
+              }
+              o[e] = DType<ODT>::from_f32(silu_mul(g1, u1));
+            }
+          }
+        }
+      } else if (ok && got) {
         // owned rows x 64 column quads, spread over the epilogue threads
         const int tid = threadIdx.x - 96;
         for (int idx = tid; idx < own_rows * (kPfBN / 4); idx += 32 * kPfDqWarps) {
@@ -666,12 +743,17 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
       p.ld_out >= (1ull << 31))
     return false;
   if ((p.rows + 128 * halves - 1) / (128 * halves) > 65535) return false;
+  // SiLU-gated epilogue: whole 256-column gate/up tiles, AWQ order, output in
+  // the input dtype; 256-row tiles only without split K
+  if (p.epi == 1 && (p.n % kPfBN != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype ||
+                     (halves == 2 && split > 1)))
+    return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
 }
 
-template <int DT, int ODT, int ORDER, int HALVES>
+template <int DT, int ODT, int ORDER, int HALVES, int EPI = 0>
 static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
   using T = typename DType<DT>::T;
   using OT = typename DType<ODT>::T;
@@ -688,7 +770,7 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
                  CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = prefill_kernel<DT, ODT, ORDER, HALVES>;
+  auto kern = prefill_kernel<DT, ODT, ORDER, HALVES, EPI>;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -723,6 +805,12 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
 
 template <int DT, int ODT>
 static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split) {
+  if constexpr (DT == ODT) {
+    if (p.epi == 1) {
+      return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 1>(p, split)
+                         : launch_prefill_t<DT, ODT, kOrderAwq, 2, 1>(p, split);
+    }
+  }
   if (halves == 1) {
     return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 1>(p, split)
                                     : launch_prefill_t<DT, ODT, kOrderAwq, 1>(p, split);
@@ -745,8 +833,6 @@ cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const De
   return cudaErrorNotSupported;
 }
 
-// One 128-row half up to 128 rows, else two; split K over a cluster while the
-// tiles alone would leave more than half of the SMs idle.
 // Clusters of `split` CTAs (one per SM: the tile's shared memory) that can be
 // resident at once on the current device, from the occupancy calculator;
 // cached per (device, tile height, split). 0 if the query fails.
@@ -786,27 +872,40 @@ static int pf_max_active_clusters(int device, int split) {
   return n;
 }
 
+// One 128-row half up to 128 rows, else two; split K over a cluster while the
+// tiles alone would leave more than half of the SMs idle.
 cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   cawq_plan pl = {};
   pl.path = CAWQ_PATH_PREFILL;
   pl.tile_n = kPfBN;
   pl.stages = kPfBStages;
   pl.warps = p.rows <= 128 ? 1 : 2;
-  const size_t bm = 128 * (size_t)pl.warps;
-  const size_t tiles = ((p.n + kPfBN - 1) / kPfBN) * ((p.rows + bm - 1) / bm);
   const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
   const size_t kt = p.k / kPfBK;
-  const int max_split = pl.warps == 1 ? kPfMaxSplit : 4;
-  int split = 1;
-  while (split < max_split && tiles * split * 2 <= sms && kt >= (size_t)split * 2 * 4) split *= 2;
-  // all clusters in one wave: a cluster needs `split` SMs of one GPC at once,
-  // and a tile count above what fits leaves the last clusters for a second
-  // wave (measured: Qwen2 qkv at M = 64, 18 clusters of 8 -> 24 us, of 4 -> 17 us)
-  while (split > 1) {
-    const int act = pl.warps == 1 ? pf_max_active_clusters<1>(dev.device, split)
-                                  : pf_max_active_clusters<2>(dev.device, split);
-    if (act <= 0 || tiles <= (size_t)act) break;
-    split /= 2;
+  auto split_for = [&](int warps) {
+    const size_t bm = 128 * (size_t)warps;
+    const size_t tiles = ((p.n + kPfBN - 1) / kPfBN) * ((p.rows + bm - 1) / bm);
+    const int max_split = warps == 1 ? kPfMaxSplit : 4;
+    int split = 1;
+    while (split < max_split && tiles * split * 2 <= sms && kt >= (size_t)split * 2 * 4) split *= 2;
+    // all clusters in one wave: a cluster needs `split` SMs of one GPC at
+    // once, and a tile count above what fits leaves the last clusters for a
+    // second wave (measured: Qwen2 qkv at M = 64, 18 clusters of 8 -> 24 us,
+    // of 4 -> 17 us)
+    while (split > 1) {
+      const int act = warps == 1 ? pf_max_active_clusters<1>(dev.device, split)
+                                 : pf_max_active_clusters<2>(dev.device, split);
+      if (act <= 0 || tiles <= (size_t)act) break;
+      split /= 2;
+    }
+    return split;
+  };
+  int split = split_for(pl.warps);
+  if (p.epi == 1 && pl.warps == 2 && split > 1) {
+    // the 256-row tile's split-K hand-off has no SiLU epilogue: 128-row
+    // tiles with their own split instead
+    pl.warps = 1;
+    split = split_for(1);
   }
   pl.split = split;
   return pl;

@@ -4,7 +4,9 @@
 //     output dst[rows][n];
 //   * rowpar_finish: out[rows][n] = F(partial + bias) after the fp32
 //     all-reduce of a row-parallel layer (the bias is added once, after the
-//     full sum, as the single-device layer does).
+//     full sum, as the single-device layer does);
+//   * interleave_gate_up: the block-interleaved gate / up column order of
+//     the SiLU-gated GEMM, from the plain [gate | up] layout.
 #pragma once
 
 #include <mutex>
@@ -83,6 +85,39 @@ cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* o
     rowpar_finish_kernel<kBF16><<<b, 256, 0, stream>>>(
         partial, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), rows,
         n);
+  }
+  return cudaGetLastError();
+}
+
+// [gate | up] (width_e elements each per row) -> blocks of block_e elements
+// alternating gate, up, gate, ... (the column order of cawq_gemm_silu_mul).
+template <typename V>
+__global__ void __launch_bounds__(256)
+    interleave_gate_up_kernel(const V* __restrict__ src, V* __restrict__ dst, size_t rows,
+                              size_t width_e, size_t block_e) {
+  const size_t row_e = 2 * width_e;
+  const size_t total = rows * row_e;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / row_e, c = i - r * row_e;  // destination element
+    const size_t j = c / (2 * block_e), w = c - j * 2 * block_e;
+    const size_t half = w / block_e, e = w - half * block_e;
+    dst[i] = src[r * row_e + half * width_e + j * block_e + e];
+  }
+}
+
+cudaError_t launch_interleave_gate_up(const void* src, void* dst, size_t rows, size_t width_e,
+                                      size_t block_e, size_t elem, cudaStream_t stream) {
+  const size_t total = rows * 2 * width_e;
+  size_t blocks = (total + 255) / 256;
+  if (blocks > 65535 * 16) blocks = 65535 * 16;
+  if (blocks == 0) return cudaSuccess;
+  if (elem == 4) {
+    interleave_gate_up_kernel<uint32_t><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), rows, width_e, block_e);
+  } else {
+    interleave_gate_up_kernel<uint16_t><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), rows, width_e, block_e);
   }
   return cudaGetLastError();
 }

@@ -248,6 +248,72 @@ def gemm(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: t
     return out
 
 
+def interleave_gate_up(t: torch.Tensor) -> torch.Tensor:
+    """[..rows.., gate | up] columns -> the block-interleaved order of
+    :func:`gemm_silu_mul` (cawq_interleave_gate_up): blocks of 128 columns
+    alternate gate, up, gate, ... For packed tensors (qweight / qzeros, 8
+    columns per int32 word) the blocks are 16 words; for scales / bias, 128
+    elements. Returns a new contiguous tensor on the same device."""
+    _require_cuda(t)
+    t = t.contiguous()
+    packed = t.dtype in _PACKED
+    block = 16 if packed else 128
+    cols = t.shape[-1]
+    if cols % (2 * block) != 0:
+        raise ShapeError(f"the last dim ({cols}) must be two halves of whole {block}-element blocks",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    if t.element_size() not in (2, 4):
+        raise DTypeError("elements must be 2 or 4 bytes", _lib.CAWQ_ERR_DTYPE)
+    rows = t.numel() // cols
+    out = torch.empty_like(t)
+    check(_lib.lib().cawq_interleave_gate_up(t.data_ptr(), out.data_ptr(), rows, cols // 2, block,
+                                              t.element_size(), stream_handle(t)))
+    return out
+
+
+def gemm_silu_mul(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                  scales: torch.Tensor, group_size: int, bias: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None, plan: Optional[dict] = None) -> torch.Tensor:
+    """gate_up GEMM with the SiLU gate in its epilogue (cawq_gemm_silu_mul):
+    out[rows, N/2] = silu(x · W_gate + b_gate) * (x · W_up + b_up), with the
+    weights (and bias) in the block-interleaved column order of
+    :func:`interleave_gate_up`. f16 / bf16."""
+    _require_cuda(x, qweight, qzeros, scales, bias, out)
+    if x.dim() != 2 or not x.is_contiguous():
+        raise ShapeError("x must be a contiguous [rows, K] tensor", _lib.CAWQ_ERR_INVALID_SHAPE)
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise DTypeError("the SiLU-gated GEMM takes f16 or bf16 input", _lib.CAWQ_ERR_DTYPE)
+    rows, k = x.shape
+    n = qweight.shape[1] * 8
+    if out is None:
+        out = torch.empty((rows, n // 2), dtype=x.dtype, device=x.device)
+    if out.dtype != x.dtype or out.dim() != 2 or out.shape[0] != rows or out.shape[1] < n // 2 or \
+            (rows > 0 and out.stride(1) != 1):
+        raise ShapeError("out must be a [rows, >= N/2] tensor with unit column stride",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    for name, t in (("qweight", qweight), ("qzeros", qzeros), ("scales", scales), ("bias", bias)):
+        if t is not None and not t.is_contiguous():
+            raise ShapeError(f"{name} must be contiguous", _lib.CAWQ_ERR_INVALID_SHAPE)
+    if scales.dtype != x.dtype or (bias is not None and bias.dtype != x.dtype):
+        raise DTypeError("scales and bias must have the input's float dtype (F)", _lib.CAWQ_ERR_DTYPE)
+    groups = scales.shape[0]
+    if qweight.shape[0] != k or groups == 0 or qzeros.shape[0] != groups or \
+            scales.shape[1] != n or qzeros.shape[1] * 8 != n or group_size * groups != k:
+        raise ShapeError("qweight [K, N/8], qzeros [K/g, N/8], scales [K/g, N] expected",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    lib = _lib.lib()
+    ld_out = out.stride(0) if rows > 0 else n // 2
+    args = (x.data_ptr(), qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+            bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, k, n, group_size,
+            cawq_dtype(x.dtype), ld_out)
+    if plan is None:
+        check(lib.cawq_gemm_silu_mul(*args, stream_handle(x)))
+    else:
+        p = _plan_c(plan)
+        check(lib.cawq_gemm_silu_mul_with_plan(*args, ctypes.byref(p), stream_handle(x)))
+    return out
+
+
 class PreparedWeights:
     """Validated weights of one layer and the constant part of its cawq_gemm
     call, so a forward pass only checks the input and makes one C call. It

@@ -18,7 +18,8 @@ import torch
 
 from . import _lib
 from .errors import CubeAwqError, DTypeError, ShapeError
-from .kernel import PreparedWeights, dequantize_awq, gemm, gemm_prepared
+from .kernel import (PreparedWeights, dequantize_awq, gemm, gemm_prepared, gemm_silu_mul,
+                     interleave_gate_up)
 
 AWQ_PACK_FACTOR = 8  # awq_gemm.rs:12
 TILE_N_BASE = 32     # awq_gemm.rs:13
@@ -158,5 +159,58 @@ class AWQLinear:
             w = self._prep = PreparedWeights(self.qweight, self.qzeros, self.scales,
                                              self.group_size(), order="natural")
         return gemm_prepared(w, x)
+
+    __call__ = forward
+
+
+class AWQGateUpSiluMul:
+    """The gate and up projections of a gated MLP in one fused GEMM with the
+    SiLU gate in its epilogue: forward(x) = silu(x·W_gate + b_gate) *
+    (x·W_up + b_up), [..., K] -> [..., I]. The reference runs gate_proj and
+    up_proj as two AWQGEMMLinear calls (awq_gemm.rs:146-232) and leaves the
+    activation to its caller; this layer reads each weight once, never writes
+    the [.., 2I] pre-activation and makes one launch.
+
+    The two layers' AutoAWQ tensors are packed once, at construction, into
+    the block-interleaved column order of the fused kernel (128 gate columns,
+    128 up columns, ...); I must be a multiple of 128 and F f16 or bf16.
+    """
+
+    def __init__(self, gate: "AWQGEMMLinear", up: "AWQGEMMLinear"):
+        _shape_assert(gate.qweight.shape == up.qweight.shape and
+                      gate.scales.shape == up.scales.shape and
+                      gate.qzeros.shape == up.qzeros.shape,
+                      "gate and up projections must have the same shapes")
+        _shape_assert((gate.bias is None) == (up.bias is None),
+                      "gate and up projections must both have a bias or both have none")
+        if gate.scales.dtype not in (torch.float16, torch.bfloat16) or \
+                up.scales.dtype != gate.scales.dtype:
+            raise DTypeError("the SiLU-gated GEMM takes f16 or bf16 scales", _lib.CAWQ_ERR_DTYPE)
+        inter = gate.scales.shape[1]
+        _shape_assert(inter % 128 == 0,
+                      f"the intermediate size ({inter}) must be a multiple of 128")
+        self.d_input = gate.qweight.shape[0]
+        self.d_output = inter
+        self._group_size = gate.group_size()
+        _shape_assert(self._group_size == up.group_size(), "gate and up group sizes differ")
+        cat = lambda a, b: interleave_gate_up(torch.cat([a, b], dim=-1))
+        self.qweight = cat(gate.qweight, up.qweight)
+        self.qzeros = cat(gate.qzeros, up.qzeros)
+        self.scales = cat(gate.scales, up.scales)
+        self.bias = cat(gate.bias, up.bias) if gate.bias is not None else None
+
+    def group_size(self) -> int:
+        return self._group_size
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
+        k = input.shape[-1]
+        _shape_assert(k == self.d_input, "input last dim (K) must match qweight rows")
+        x = input.reshape(-1, k)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        out = gemm_silu_mul(x, self.qweight, self.qzeros, self.scales, self._group_size,
+                            bias=self.bias)
+        return out.reshape(*input.shape[:-1], self.d_output)
 
     __call__ = forward

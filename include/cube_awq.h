@@ -215,6 +215,45 @@ cawq_status cawq_gemm_with_plan(const void* x, const uint32_t* qweight,
                                 cawq_order order, size_t ld_out,
                                 const cawq_plan* plan, void* stream);
 
+/*
+ * gate_up with its SiLU gate fused into the epilogue (the next step of a
+ * SwiGLU MLP): out[rows, n / 2] = silu(x · W_gate + b_gate) * (x · W_up + b_up),
+ * computed from the fp32 sums and rounded once to `dtype`. No counterpart
+ * kernel in the reference (its decoder runs the GEMM, then the activation).
+ * The weights are the gate and up projections with their columns interleaved
+ * in 128-column blocks — W columns [256 j, 256 j + 128) are gate columns
+ * [128 j, 128 j + 128), the next 128 the matching up columns — so n (= 2 x
+ * the MLP width) must be a multiple of 256; qweight / qzeros / scales / bias
+ * follow the same column order (cawq_interleave_gate_up builds it from the
+ * plain [gate | up] layout). dtype CAWQ_F16 or CAWQ_BF16; ld_out >= n / 2
+ * (0 = n / 2). Output column c of row r sits at out[r * ld_out + c].
+ */
+cawq_status cawq_gemm_silu_mul(const void* x, const uint32_t* qweight,
+                               const uint32_t* qzeros, const void* scales,
+                               const void* bias, void* out, size_t rows, size_t k,
+                               size_t n, size_t group_size, cawq_dtype dtype,
+                               size_t ld_out, void* stream);
+
+/* The same with an explicit plan (decode or prefill path). */
+cawq_status cawq_gemm_silu_mul_with_plan(const void* x, const uint32_t* qweight,
+                                         const uint32_t* qzeros, const void* scales,
+                                         const void* bias, void* out, size_t rows,
+                                         size_t k, size_t n, size_t group_size,
+                                         cawq_dtype dtype, size_t ld_out,
+                                         const cawq_plan* plan, void* stream);
+
+/*
+ * Reorders the columns of a [gate | up] projection (`width` columns each,
+ * width % 128 == 0) into the block-interleaved layout cawq_gemm_silu_mul
+ * reads: `rows` rows of `elem_size`-byte elements (4 for packed qweight /
+ * qzeros rows with width / 8 words per half, 2 or 4 for scales / bias), row
+ * pitch `2 * width_elems * elem_size` bytes in both buffers, where
+ * width_elems is the half's element count (width for scales and bias,
+ * width / 8 for packed rows). src and dst must not overlap.
+ */
+cawq_status cawq_interleave_gate_up(const void* src, void* dst, size_t rows, size_t width_elems,
+                                    size_t block_elems, size_t elem_size, void* stream);
+
 /* ----------------------------------------------------------------------- */
 /* Planner / autotuner                                                     */
 /* ----------------------------------------------------------------------- */

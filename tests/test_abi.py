@@ -76,3 +76,19 @@ def test_row_shards_follow_group_boundaries():
     assert "world" in _lib.last_error()
     assert lib.cawq_tp_column_shard(4096, 3, 0, ctypes.byref(b), ctypes.byref(l)) == \
         _lib.CAWQ_ERR_INVALID_SHAPE
+
+
+def test_silu_mul_entry_checks_arguments_before_the_device():
+    # dtype and the 256-column rule are checked before any device call, so the
+    # errors are the same on a CPU box
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+    st = lib.cawq_gemm_silu_mul(p, p, p, p, None, p, 1, 128, 512, 128, _lib.CAWQ_F32, 0, None)
+    assert st == _lib.CAWQ_ERR_DTYPE and "F16" in _lib.last_error()
+    st = lib.cawq_gemm_silu_mul(p, p, p, p, None, p, 1, 128, 384, 128, _lib.CAWQ_F16, 0, None)
+    assert st == _lib.CAWQ_ERR_INVALID_SHAPE and "256" in _lib.last_error()
+    st = lib.cawq_interleave_gate_up(p, p, 4, 96, 64, 2, None)
+    assert st == _lib.CAWQ_ERR_INVALID_SHAPE
+    st = lib.cawq_interleave_gate_up(p, p, 4, 128, 64, 8, None)
+    assert st == _lib.CAWQ_ERR_INVALID_ARGUMENT
+    assert lib.cawq_interleave_gate_up(p, p, 0, 128, 64, 2, None) == 0  # nothing to move
