@@ -17,12 +17,12 @@ from . import _lib
 from .errors import (CubeAwqError, DeviceTimeoutError, DTypeError, ShapeError,
                      UnsupportedDeviceError)
 from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, awq_gemm_linear,
-                     dequantize_awq, dequantize_native, device_error, gemm, gemm_silu_mul,
-                     interleave_gate_up, plan_cache_clear, plan_get, plan_set, select_tile_m,
-                     select_tile_n, validate_decode_launch_params, validate_launch_params,
-                     version)
+                     dequantize_awq, dequantize_native, device_error, gemm, gemm_qkv,
+                     gemm_silu_mul, interleave_gate_up, plan_cache_clear, plan_get, plan_set,
+                     select_tile_m, select_tile_n, validate_decode_launch_params,
+                     validate_launch_params, version)
 from .modules import (AWQGateUpSiluMul, AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear,
-                      AWQLinearConfig)
+                      AWQLinearConfig, AWQQKVLinear)
 from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
 from .loader import load_awq_linears
 
@@ -38,10 +38,11 @@ if _os.path.exists(_lib.LIB_PATH):
 
 __all__ = [
     "AWQGateUpSiluMul", "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
+    "AWQQKVLinear",
     "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "load_awq_linears",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
-    "dequantize_awq", "dequantize_native", "device_error", "gemm", "gemm_silu_mul",
+    "dequantize_awq", "dequantize_native", "device_error", "gemm", "gemm_qkv", "gemm_silu_mul",
     "interleave_gate_up", "plan_cache_clear",
     "plan_get", "plan_set", "select_tile_m", "select_tile_n", "validate_decode_launch_params",
     "validate_launch_params", "version",

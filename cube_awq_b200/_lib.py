@@ -42,6 +42,7 @@ EXPORTED = (
     "cawq_select_tile_m", "cawq_select_tile_n",
     "cawq_awq_gemm_linear", "cawq_gemm", "cawq_gemm_with_plan",
     "cawq_gemm_silu_mul", "cawq_gemm_silu_mul_with_plan", "cawq_interleave_gate_up",
+    "cawq_gemm_qkv",
     "cawq_plan_get", "cawq_plan_set", "cawq_plan_cache_clear", "cawq_autotune",
     "cawq_dequantize_native", "cawq_dequantize",
     "cawq_tp_column_shard", "cawq_tp_row_shard", "cawq_tp_interleave_columns",
@@ -124,6 +125,9 @@ def _declare(L) -> None:
     L.cawq_gemm_silu_mul_with_plan.restype = st
     L.cawq_interleave_gate_up.argtypes = [vp, vp, sz, sz, sz, sz, vp]
     L.cawq_interleave_gate_up.restype = st
+    L.cawq_gemm_qkv.argtypes = [vp, u32p, u32p, vp, vp, vp, vp, vp, sz, sz, sz, sz, sz, i, i,
+                                sz, sz, sz, vp]
+    L.cawq_gemm_qkv.restype = st
     L.cawq_plan_get.argtypes = [sz, sz, sz, sz, i, ctypes.POINTER(PlanC)]
     L.cawq_plan_get.restype = st
     L.cawq_plan_set.argtypes = [sz, sz, sz, sz, i, ctypes.POINTER(PlanC)]

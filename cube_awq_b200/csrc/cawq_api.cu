@@ -337,21 +337,30 @@ static cawq_status check_gemm_pointers(const void* x, const void* qw, const void
   return CAWQ_OK;
 }
 
+// The k and v outputs of cawq_gemm_qkv (out / ld_out hold q).
+struct QkvOut {
+  void* out_k;
+  void* out_v;
+  size_t ld_k, ld_v, col_k, col_v;
+};
+
 static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uint32_t* qzeros,
                                const void* scales, const void* bias, void* out, size_t rows,
                                size_t k, size_t n, size_t g, cawq_dtype dtype,
                                cawq_dtype out_dtype, cawq_order order, size_t ld_out,
                                const cawq_plan* plan, void* stream, bool module_rules,
-                               int epi = 0) {
+                               int epi = 0, const QkvOut* qkv = nullptr) {
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype))
     return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
   if (out_dtype != dtype && out_dtype != CAWQ_F32)
     return fail(CAWQ_ERR_DTYPE, "out_dtype must equal dtype or be CAWQ_F32");
   if (order != CAWQ_ORDER_AWQ && order != CAWQ_ORDER_NATURAL)
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "order must be CAWQ_ORDER_AWQ or CAWQ_ORDER_NATURAL");
-  const size_t ocols = epi ? n / 2 : n;  // output columns
+  const size_t ocols = qkv ? qkv->col_k : epi ? n / 2 : n;  // columns of `out`
   if (ld_out == 0) ld_out = ocols;
-  if (ld_out < ocols) return fail(CAWQ_ERR_INVALID_SHAPE, epi ? "ld_out must be >= n / 2" : "ld_out must be >= n");
+  if (ld_out < ocols)
+    return fail(CAWQ_ERR_INVALID_SHAPE, qkv ? "ld_q must be >= n_q"
+                                        : epi ? "ld_out must be >= n / 2" : "ld_out must be >= n");
   if (module_rules) {
     if (!(k > 0)) return fail(CAWQ_ERR_INVALID_SHAPE, "input last dim (K) must be > 0");
     if (order == CAWQ_ORDER_AWQ) {
@@ -375,6 +384,16 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
   if ((st = require_sm100(&dev)) != CAWQ_OK) return st;
   GemmProblem p = {x, qweight, qzeros, scales, bias, out, rows, k, n, g, ld_out,
                    dtype, out_dtype, order, static_cast<cudaStream_t>(stream), epi};
+  if (qkv) {
+    if (!qkv->out_k || !qkv->out_v)
+      return fail(CAWQ_ERR_NULL_POINTER, "q_out, k_out and v_out must be non-null");
+    p.out_k = qkv->out_k;
+    p.out_v = qkv->out_v;
+    p.ld_k = qkv->ld_k;
+    p.ld_v = qkv->ld_v;
+    p.col_k = qkv->col_k;
+    p.col_v = qkv->col_v;
+  }
   cawq_plan pl = plan ? *plan : choose_plan(p, dev);
   if (plan && !plan_supports(p, pl, dev))
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "the plan cannot run this problem");
@@ -545,6 +564,25 @@ CAWQ_API cawq_status cawq_gemm_silu_mul(const void* x, const uint32_t* qweight,
                 fmt("n = %zu must be a multiple of 256 (128-column gate / up blocks)", n));
   return gemm_common(x, qweight, qzeros, scales, bias, out, rows, k, n, group_size, dtype, dtype,
                      CAWQ_ORDER_AWQ, ld_out, nullptr, stream, true, 1);
+}
+
+CAWQ_API cawq_status cawq_gemm_qkv(const void* x, const uint32_t* qweight, const uint32_t* qzeros,
+                                   const void* scales, const void* bias, void* q_out, void* k_out,
+                                   void* v_out, size_t rows, size_t k, size_t n_q, size_t n_kv,
+                                   size_t group_size, cawq_dtype dtype, cawq_dtype out_dtype,
+                                   size_t ld_q, size_t ld_k, size_t ld_v, void* stream) {
+  if (n_q == 0 || n_kv == 0 || n_q % 32 != 0 || n_kv % 32 != 0)
+    return fail(CAWQ_ERR_INVALID_SHAPE,
+                fmt("n_q = %zu and n_kv = %zu must be positive multiples of 32", n_q, n_kv));
+  if (ld_k == 0) ld_k = n_kv;
+  if (ld_v == 0) ld_v = n_kv;
+  if (ld_k < n_kv || ld_v < n_kv)
+    return fail(CAWQ_ERR_INVALID_SHAPE, "ld_k and ld_v must be >= n_kv");
+  if (ld_q >= (1ull << 31) || ld_k >= (1ull << 31) || ld_v >= (1ull << 31))
+    return fail(CAWQ_ERR_INVALID_SHAPE, "row strides must be below 2^31 elements");
+  const QkvOut qkv = {k_out, v_out, ld_k, ld_v, n_q, n_q + n_kv};
+  return gemm_common(x, qweight, qzeros, scales, bias, q_out, rows, k, n_q + 2 * n_kv, group_size,
+                     dtype, out_dtype, CAWQ_ORDER_AWQ, ld_q, nullptr, stream, true, 0, &qkv);
 }
 
 CAWQ_API cawq_status cawq_interleave_gate_up(const void* src, void* dst, size_t rows,

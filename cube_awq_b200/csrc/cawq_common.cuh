@@ -172,6 +172,43 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Address of output element (row, col): columns [0, c1) live in p0 (row
+// stride ld0), [c1, c2) in p1 and [c2, n) in p2 (the q / k / v outputs of a
+// fused qkv projection); a single output has c1 = c2 = 0xFFFFFFFF. Fields,
+// not arrays, so the choice compiles to selects on kernel parameters.
+template <typename OT>
+struct OutMap {
+  OT* p0;
+  OT* p1;
+  OT* p2;
+  uint32_t ld0, ld1, ld2, c1, c2;
+  __device__ __forceinline__ OT* at(uint32_t row, uint32_t col) const {
+    if (col < c1) return p0 + (size_t)row * ld0 + col;
+    if (col < c2) return p1 + (size_t)row * ld1 + (col - c1);
+    return p2 + (size_t)row * ld2 + (col - c2);
+  }
+};
+
+template <typename OT>
+inline OutMap<OT> out_map(const GemmProblem& p) {
+  OutMap<OT> m;
+  m.p0 = static_cast<OT*>(p.out);
+  m.ld0 = static_cast<uint32_t>(p.ld_out);
+  if (p.out_k) {
+    m.p1 = static_cast<OT*>(p.out_k);
+    m.p2 = static_cast<OT*>(p.out_v);
+    m.ld1 = static_cast<uint32_t>(p.ld_k);
+    m.ld2 = static_cast<uint32_t>(p.ld_v);
+    m.c1 = static_cast<uint32_t>(p.col_k);
+    m.c2 = static_cast<uint32_t>(p.col_v);
+  } else {
+    m.p1 = m.p2 = m.p0;
+    m.ld1 = m.ld2 = m.ld0;
+    m.c1 = m.c2 = 0xFFFFFFFFu;
+  }
+  return m;
+}
+
 // silu(g) * u, the gate of a gated MLP, with the fast-math intrinsics
 // (exp and divide; a few ulp in fp32, far below the f16 / bf16 output's
 // rounding). A gate below about -88 makes the denominator infinite and the

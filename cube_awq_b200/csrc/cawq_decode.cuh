@@ -133,8 +133,8 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     decode_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                   const uint32_t* __restrict__ qz, const typename DType<DT>::T* __restrict__ sc,
                   const typename DType<DT>::T* __restrict__ bias,
-                  typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
-                  uint32_t g, uint32_t ld_out, uint32_t split, uint32_t nstage_ring,
+                  const OutMap<typename DType<ODT>::T> om, uint32_t rows, uint32_t k, uint32_t n,
+                  uint32_t g, uint32_t split, uint32_t nstage_ring,
                   uint32_t strips_u, uint32_t pf_stages) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
@@ -911,7 +911,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       gv += DType<DT>::to_f32(bias[wcol]);
       uv += DType<DT>::to_f32(bias[wcol + 128]);
     }
-    out[(size_t)row * ld_out + pband * 4 + pi] = DType<ODT>::from_f32(silu_mul(gv, uv));
+    om.p0[(size_t)row * om.ld0 + pband * 4 + pi] = DType<ODT>::from_f32(silu_mul(gv, uv));
   };
   if (split == 1 && EPI == 1) {
     // the band's sums meet in the receive buffer (unused without split K):
@@ -956,7 +956,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
             if (col < n) {
               float v = outv[m][e][c];
               if (bias) v += DType<DT>::to_f32(bias[col]);
-              out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
+              *om.at(row, col) = DType<ODT>::from_f32(v);
             }
           }
         }
@@ -1025,7 +1025,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
       if (col < n) {
         if (bias) v += DType<DT>::to_f32(bias[col]);
-        out[(size_t)row * ld_out + col] = DType<ODT>::from_f32(v);
+        *om.at(row, col) = DType<ODT>::from_f32(v);
       }
     }
   }
@@ -1150,10 +1150,10 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kern, tm_w, tm_x, p.qz, static_cast<const T*>(p.sc),
-                            static_cast<const T*>(p.bias), static_cast<OT*>(p.out),
+                            static_cast<const T*>(p.bias), out_map<OT>(p),
                             static_cast<uint32_t>(p.rows), static_cast<uint32_t>(p.k),
                             static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g),
-                            static_cast<uint32_t>(p.ld_out), static_cast<uint32_t>(plan.split),
+                            static_cast<uint32_t>(plan.split),
                             static_cast<uint32_t>(plan.stages), static_cast<uint32_t>(plan.warps),
                             static_cast<uint32_t>(plan.reserved[1] > 0 ? plan.reserved[1] : 0));
 }

@@ -20,8 +20,8 @@ __global__ void __launch_bounds__(kGenericCols)
                         const uint32_t* __restrict__ qw, const uint32_t* __restrict__ qz,
                         const typename DType<DT>::T* __restrict__ sc,
                         const typename DType<DT>::T* __restrict__ bias,
-                        typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k,
-                        uint32_t n, uint32_t g, size_t ld_out) {
+                        const OutMap<typename DType<ODT>::T> om, uint32_t rows, uint32_t k,
+                        uint32_t n, uint32_t g) {
   const uint32_t col = blockIdx.x * kGenericCols + threadIdx.x;
   const uint32_t r0 = blockIdx.y * kGenericRows;
   if (col >= n) return;
@@ -55,14 +55,15 @@ __global__ void __launch_bounds__(kGenericCols)
 #pragma unroll
   for (int r = 0; r < kGenericRows; ++r) {
     if (static_cast<uint32_t>(r) < nr) {
-      out[(size_t)(r0 + r) * ld_out + col] = DType<ODT>::from_f32(acc[r] + b);
+      *om.at(r0 + r, col) = DType<ODT>::from_f32(acc[r] + b);
     }
   }
 }
 
 bool generic_supports(const GemmProblem& p) {
   return p.rows > 0 && p.k > 0 && p.n % 8 == 0 && p.g > 0 && p.k % p.g == 0 &&
-         p.rows <= 65535ull * kGenericRows && p.k < (1ull << 31) && p.n < (1ull << 31);
+         p.rows <= 65535ull * kGenericRows && p.k < (1ull << 31) && p.n < (1ull << 31) &&
+         p.ld_out < (1ull << 31);
 }
 
 template <int DT, int ODT, int ORDER>
@@ -73,9 +74,8 @@ static cudaError_t launch_generic_t(const GemmProblem& p) {
             static_cast<uint32_t>((p.rows + kGenericRows - 1) / kGenericRows));
   generic_gemm_kernel<DT, ODT, ORDER><<<grid, kGenericCols, 0, p.stream>>>(
       static_cast<const T*>(p.x), p.qw, p.qz, static_cast<const T*>(p.sc),
-      static_cast<const T*>(p.bias), static_cast<OT*>(p.out), static_cast<uint32_t>(p.rows),
-      static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g),
-      p.ld_out);
+      static_cast<const T*>(p.bias), out_map<OT>(p), static_cast<uint32_t>(p.rows),
+      static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g));
   return cudaGetLastError();
 }
 

@@ -31,6 +31,13 @@ struct GemmProblem {
   // epilogue: 0 = plain; 1 = SiLU-gated product of block-interleaved gate/up
   // columns (128-column blocks: gate, up, gate, ...): out [rows, n / 2]
   int epi = 0;
+  // column split of the output (qkv projection): columns [0, col_k) go to
+  // `out` (row stride ld_out), [col_k, col_v) to out_k (ld_k), [col_v, n) to
+  // out_v (ld_v); out_k == nullptr: one output. col_k and col_v are multiples
+  // of 32, so no 32-column store chunk straddles two outputs.
+  void* out_k = nullptr;
+  void* out_v = nullptr;
+  size_t ld_k = 0, ld_v = 0, col_k = 0, col_v = 0;
 };
 
 // Thread-local error message (cawq_last_error).

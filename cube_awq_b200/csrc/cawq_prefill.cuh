@@ -205,8 +205,8 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                    const typename DType<DT>::T* __restrict__ bias,
-                   typename DType<ODT>::T* __restrict__ out, uint32_t rows, uint32_t k, uint32_t n,
-                   uint32_t g, uint32_t ld_out, uint32_t split) {
+                   const OutMap<typename DType<ODT>::T> om, uint32_t rows, uint32_t k, uint32_t n,
+                   uint32_t g, uint32_t split) {
   using L = PrefillLayout<HALVES>;
   constexpr int BM = L::kBM;
   constexpr int kPfDqWarps = pf_dq_warps(HALVES);
@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] += DType<DT>::to_f32(bias[col0 + i]);
       }
-      typename DType<ODT>::T* o = out + (size_t)row * ld_out + col0;
+      typename DType<ODT>::T* o = om.at(row, col0);  // the chunk lies in one output
       if constexpr (ODT == kF32) {
         if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
@@ -493,7 +493,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
         v[i] = silu_mul(gv, uv);
       }
       using OT = typename DType<ODT>::T;
-      OT* o = out + (size_t)row * ld_out + ocol;
+      OT* o = om.p0 + (size_t)row * om.ld0 + ocol;
       // 16-byte stores: a lane owns one row, so 2-byte stores would reach L2
       // as 16 partial writes of each 32-byte sector
       if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
@@ -591,7 +591,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
           const uint32_t gcol = n0 + 4 * c4;
           if (row < rows && gcol < n) {
             const float gv[4] = {ga.x, ga.y, ga.z, ga.w}, uv[4] = {ua.x, ua.y, ua.z, ua.w};
-            typename DType<ODT>::T* o = out + (size_t)row * ld_out + n0 / 2 + 4 * c4;
+            typename DType<ODT>::T* o = om.p0 + (size_t)row * om.ld0 + n0 / 2 + 4 * c4;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               float g1 = gv[e], u1 = uv[e];
@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
           const uint32_t col = n0 + 4 * c4;
           if (row < rows && col < n) {
             float v4[4] = {acc.x, acc.y, acc.z, acc.w};
-            typename DType<ODT>::T* o = out + (size_t)row * ld_out + col;
+            typename DType<ODT>::T* o = om.at(row, col);  // the quad lies in one output
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               if (col + e < n) {
@@ -797,10 +797,9 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, tz, static_cast<const T*>(p.bias),
-                            static_cast<OT*>(p.out), static_cast<uint32_t>(p.rows),
+                            out_map<OT>(p), static_cast<uint32_t>(p.rows),
                             static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n),
-                            static_cast<uint32_t>(p.g), static_cast<uint32_t>(p.ld_out),
-                            static_cast<uint32_t>(split));
+                            static_cast<uint32_t>(p.g), static_cast<uint32_t>(split));
 }
 
 template <int DT, int ODT>

@@ -248,6 +248,56 @@ def gemm(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: t
     return out
 
 
+def gemm_qkv(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+             group_size: int, n_q: int, n_kv: int, bias: Optional[torch.Tensor] = None,
+             out: Optional[tuple] = None, out_dtype: Optional[torch.dtype] = None) -> tuple:
+    """Fused qkv projection with a split epilogue (cawq_gemm_qkv): one GEMM
+    over the concatenated [q | k | v] weights (AutoAWQ layout, N = n_q +
+    2 n_kv) that writes q [rows, n_q], k and v [rows, n_kv] to three outputs.
+    ``out`` = (q, k, v) may be views with a unit column stride (for example
+    rows of a key / value cache); each output element equals the one
+    :func:`gemm` writes for that column. Returns (q, k, v)."""
+    _require_cuda(x, qweight, qzeros, scales, bias)
+    if x.dim() != 2 or not x.is_contiguous():
+        raise ShapeError("x must be a contiguous [rows, K] tensor", _lib.CAWQ_ERR_INVALID_SHAPE)
+    rows, k = x.shape
+    n = qweight.shape[1] * 8
+    if n_q <= 0 or n_kv <= 0 or n_q + 2 * n_kv != n:
+        raise ShapeError(f"n_q + 2 n_kv must equal the weight's {n} columns",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    odt = out_dtype or x.dtype
+    if out is None:
+        out = tuple(torch.empty((rows, w), dtype=odt, device=x.device) for w in (n_q, n_kv, n_kv))
+    if len(out) != 3:
+        raise ShapeError("out must be a (q, k, v) triple", _lib.CAWQ_ERR_INVALID_SHAPE)
+    _require_cuda(*out)
+    for t, w in zip(out, (n_q, n_kv, n_kv)):
+        if t.dtype != odt or t.dim() != 2 or t.shape[0] != rows or t.shape[1] < w or \
+                (rows > 0 and t.stride(1) != 1):
+            raise ShapeError("each output must be a [rows, >= width] tensor with unit column "
+                             "stride", _lib.CAWQ_ERR_INVALID_SHAPE)
+    for name, t in (("qweight", qweight), ("qzeros", qzeros), ("scales", scales), ("bias", bias)):
+        if t is not None and not t.is_contiguous():
+            raise ShapeError(f"{name} must be contiguous", _lib.CAWQ_ERR_INVALID_SHAPE)
+    if qweight.dtype not in _PACKED or qzeros.dtype not in _PACKED:
+        raise DTypeError("qweight and qzeros must have i32/u32 dtype", _lib.CAWQ_ERR_DTYPE)
+    if scales.dtype != x.dtype or (bias is not None and bias.dtype != x.dtype):
+        raise DTypeError("scales and bias must have the input's float dtype (F)", _lib.CAWQ_ERR_DTYPE)
+    groups = scales.shape[0]
+    if qweight.shape[0] != k or groups == 0 or qzeros.shape[0] != groups or \
+            scales.shape[1] != n or qzeros.shape[1] * 8 != n or group_size * groups != k:
+        raise ShapeError("qweight [K, N/8], qzeros [K/g, N/8], scales [K/g, N] expected",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    q, kk, v = out
+    lds = [t.stride(0) if rows > 0 else w for t, w in zip(out, (n_q, n_kv, n_kv))]
+    check(_lib.lib().cawq_gemm_qkv(
+        x.data_ptr(), qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+        bias.data_ptr() if bias is not None else None, q.data_ptr(), kk.data_ptr(), v.data_ptr(),
+        rows, k, n_q, n_kv, group_size, cawq_dtype(x.dtype), cawq_dtype(odt), *lds,
+        stream_handle(x)))
+    return q, kk, v
+
+
 def interleave_gate_up(t: torch.Tensor) -> torch.Tensor:
     """[..rows.., gate | up] columns -> the block-interleaved order of
     :func:`gemm_silu_mul` (cawq_interleave_gate_up): blocks of 128 columns

@@ -18,8 +18,8 @@ import torch
 
 from . import _lib
 from .errors import CubeAwqError, DTypeError, ShapeError
-from .kernel import (PreparedWeights, dequantize_awq, gemm, gemm_prepared, gemm_silu_mul,
-                     interleave_gate_up)
+from .kernel import (PreparedWeights, dequantize_awq, gemm, gemm_prepared, gemm_qkv,
+                     gemm_silu_mul, interleave_gate_up)
 
 AWQ_PACK_FACTOR = 8  # awq_gemm.rs:12
 TILE_N_BASE = 32     # awq_gemm.rs:13
@@ -212,5 +212,61 @@ class AWQGateUpSiluMul:
         out = gemm_silu_mul(x, self.qweight, self.qzeros, self.scales, self._group_size,
                             bias=self.bias)
         return out.reshape(*input.shape[:-1], self.d_output)
+
+    __call__ = forward
+
+
+class AWQQKVLinear:
+    """The q, k and v projections of an attention block in one fused GEMM
+    with a split epilogue: forward(x) -> (q [..., n_q], k [..., n_kv],
+    v [..., n_kv]). The reference runs them as three AWQGEMMLinear forwards
+    (awq_gemm.rs:146-232), each reading x and paying a launch; here the three
+    layers' AutoAWQ tensors are concatenated once along the output columns
+    and one launch writes the three outputs, optionally into caller-given
+    views (``out=``, e.g. rows of a key / value cache). Every element equals
+    the one the single-layer forward of the concatenated layer writes.
+    n_q and n_kv: multiples of 32.
+    """
+
+    def __init__(self, q: "AWQGEMMLinear", k: "AWQGEMMLinear", v: "AWQGEMMLinear"):
+        layers = (q, k, v)
+        _shape_assert(q.qweight.shape[0] == k.qweight.shape[0] == v.qweight.shape[0],
+                      "q, k and v projections must have the same input size")
+        _shape_assert(k.scales.shape == v.scales.shape,
+                      "k and v projections must have the same shapes")
+        _shape_assert(len({l.group_size() for l in layers}) == 1,
+                      "q, k and v projections must have the same group size")
+        _shape_assert(len({l.bias is None for l in layers}) == 1,
+                      "q, k and v projections must all have a bias or all have none")
+        _shape_assert(len({l.scales.dtype for l in layers}) == 1,
+                      "q, k and v projections must have the same float dtype")
+        self.n_q = q.scales.shape[1]
+        self.n_kv = k.scales.shape[1]
+        _shape_assert(self.n_q % 32 == 0 and self.n_kv % 32 == 0,
+                      "q and k/v output sizes must be multiples of 32")
+        self.d_input = q.qweight.shape[0]
+        self._group_size = q.group_size()
+        cat = lambda name: torch.cat([getattr(l, name) for l in layers], dim=-1).contiguous()
+        self.qweight = cat("qweight")
+        self.qzeros = cat("qzeros")
+        self.scales = cat("scales")
+        self.bias = cat("bias") if q.bias is not None else None
+
+    def group_size(self) -> int:
+        return self._group_size
+
+    def forward(self, input: torch.Tensor, out: Optional[tuple] = None) -> tuple:
+        _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
+        k = input.shape[-1]
+        _shape_assert(k == self.d_input, "input last dim (K) must match qweight rows")
+        x = input.reshape(-1, k)
+        if not x.is_contiguous():
+            x = x.contiguous()
+        q, kk, v = gemm_qkv(x, self.qweight, self.qzeros, self.scales, self._group_size,
+                            self.n_q, self.n_kv, bias=self.bias, out=out)
+        if out is not None:
+            return q, kk, v
+        lead = input.shape[:-1]
+        return q.reshape(*lead, self.n_q), kk.reshape(*lead, self.n_kv), v.reshape(*lead, self.n_kv)
 
     __call__ = forward

@@ -254,6 +254,25 @@ cawq_status cawq_gemm_silu_mul_with_plan(const void* x, const uint32_t* qweight,
 cawq_status cawq_interleave_gate_up(const void* src, void* dst, size_t rows, size_t width_elems,
                                     size_t block_elems, size_t elem_size, void* stream);
 
+/*
+ * Fused qkv projection with a split epilogue (no counterpart kernel in the
+ * reference, which runs q_proj, k_proj and v_proj as three AWQGEMMLinear
+ * forwards, src/modules/awq_gemm.rs:146-232). One cawq_gemm over the
+ * concatenated [q | k | v] weights (AutoAWQ layout, n = n_q + 2 * n_kv
+ * columns; bias likewise concatenated or NULL) whose epilogue writes columns
+ * [0, n_q) to q_out (row stride ld_q), [n_q, n_q + n_kv) to k_out (ld_k) and
+ * the rest to v_out (ld_v): each output can be a slice of a larger buffer,
+ * such as a key / value cache row. n_q and n_kv: positive multiples of 32;
+ * a stride of 0 means the output's width. Same rules, plans and dtypes as
+ * cawq_gemm with CAWQ_ORDER_AWQ; every output element is the value cawq_gemm
+ * writes for that column.
+ */
+cawq_status cawq_gemm_qkv(const void* x, const uint32_t* qweight, const uint32_t* qzeros,
+                          const void* scales, const void* bias, void* q_out, void* k_out,
+                          void* v_out, size_t rows, size_t k, size_t n_q, size_t n_kv,
+                          size_t group_size, cawq_dtype dtype, cawq_dtype out_dtype,
+                          size_t ld_q, size_t ld_k, size_t ld_v, void* stream);
+
 /* ----------------------------------------------------------------------- */
 /* Planner / autotuner                                                     */
 /* ----------------------------------------------------------------------- */

@@ -92,3 +92,17 @@ def test_silu_mul_entry_checks_arguments_before_the_device():
     st = lib.cawq_interleave_gate_up(p, p, 4, 128, 64, 8, None)
     assert st == _lib.CAWQ_ERR_INVALID_ARGUMENT
     assert lib.cawq_interleave_gate_up(p, p, 0, 128, 64, 2, None) == 0  # nothing to move
+
+
+def test_qkv_entry_checks_split_before_the_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+    args = lambda nq, nkv, ldk: (p, p, p, p, None, p, p, p, 1, 128, nq, nkv, 128, _lib.CAWQ_F16,
+                                 _lib.CAWQ_F16, 0, ldk, 0, None)
+    assert lib.cawq_gemm_qkv(*args(496, 136, 0)) == _lib.CAWQ_ERR_INVALID_SHAPE
+    assert "multiples of 32" in _lib.last_error()
+    assert lib.cawq_gemm_qkv(*args(512, 128, 64)) == _lib.CAWQ_ERR_INVALID_SHAPE
+    assert "ld_k" in _lib.last_error()
+    a = list(args(512, 128, 0))
+    a[8] = 0  # no rows: nothing to do, no device needed
+    assert lib.cawq_gemm_qkv(*a) == 0
