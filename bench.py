@@ -327,6 +327,7 @@ def run_ours(a, rank, local_rank, world):
         extras["prefill_m2048"] = prefill_numbers(a, dev, peaks)
         extras["dequantize"] = dequant_numbers(dev, peaks)
         extras["qwen2_m_sweep"] = qwen2_sweep(dev)
+        extras["fused_neighbours"] = fused_neighbour_numbers(dev)
         extras["tp_llama3_70b_mlp"] = tp_mlp_numbers(dev, world, max_over_ranks)
 
     if world > 1:
@@ -491,6 +492,76 @@ def qwen2_sweep(dev, reps=10):
                        "paths": sorted(set(paths.values()))}
         del xs, ys
     del ws
+    return res
+
+
+def fused_neighbour_numbers(dev, reps=10):
+    """The fused neighbours of the GEMM, graph-timed, us per call (weight
+    copies rotated so they come from HBM at small M):
+    * gate_up: cawq_gemm_silu_mul against cawq_gemm + torch silu * mul and
+      against cawq_gemm alone (Llama-2-7B 4096 -> 2 x 11008, g 128; Qwen2-7B
+      3584 -> 2 x 18944, g 64);
+    * qkv: cawq_gemm_qkv into three outputs against three cawq_gemm calls
+      (Qwen2-7B 3584 -> 3584 + 2 x 512, g 64)."""
+    import torch
+
+    import cube_awq_b200 as cawq
+    from cube_awq_b200 import synth
+    dt = torch.float16
+    stream = torch.cuda.Stream(dev)
+    res = {}
+    for name, k, inter, g, copies in (("llama2_7b_gate_up", 4096, 11008, 128, 4),
+                                      ("qwen2_7b_gate_up", 3584, 18944, 64, 3)):
+        ws = [synth.make_weights(k, 2 * inter, g, dt, dev, seed=900 + c) for c in range(copies)]
+        fz = [tuple(cawq.interleave_gate_up(t) for t in (w.qweight, w.qzeros, w.scales))
+              for w in ws]
+        r = {}
+        for m in (1, 16, 64, 2048):
+            x = synth.make_input(m, k, dt, dev, seed=950)
+            y = torch.empty(m, 2 * inter, dtype=dt, device=dev)
+            h = torch.empty(m, inter, dtype=dt, device=dev)
+
+            def unfused():
+                for w in ws:
+                    cawq.gemm(x, w.qweight, w.qzeros, w.scales, g, out=y)
+                    torch.mul(torch.nn.functional.silu(y[:, :inter]), y[:, inter:], out=h)
+
+            def gemm_only():
+                for w in ws:
+                    cawq.gemm(x, w.qweight, w.qzeros, w.scales, g, out=y)
+
+            def fused():
+                for q, z, sc in fz:
+                    cawq.gemm_silu_mul(x, q, z, sc, g, out=h)
+            n = 2 if m >= 2048 else reps
+            r[f"M={m}"] = {lab: round(_graph_us(fn, n, stream) / copies, 2) for lab, fn in
+                           (("gemm_then_torch_silu_mul_us", unfused), ("gemm_only_us", gemm_only),
+                            ("fused_silu_mul_us", fused))}
+        res[name] = r
+        del ws, fz
+    k, nq, nkv, g, copies = 3584, 3584, 512, 64, 6
+    ws = [synth.make_weights(k, nq + 2 * nkv, g, dt, dev, seed=960 + c) for c in range(copies)]
+    parts = [[(w.qweight[:, a // 8:b // 8].contiguous(), w.qzeros[:, a // 8:b // 8].contiguous(),
+               w.scales[:, a:b].contiguous())
+              for a, b in ((0, nq), (nq, nq + nkv), (nq + nkv, nq + 2 * nkv))] for w in ws]
+    r = {}
+    for m in (1, 16, 2048):
+        x = synth.make_input(m, k, dt, dev, seed=970)
+        outs = [torch.empty(m, c, dtype=dt, device=dev) for c in (nq, nkv, nkv)]
+
+        def three():
+            for pw in parts:
+                for (q, z, sc), o in zip(pw, outs):
+                    cawq.gemm(x, q, z, sc, g, out=o)
+
+        def split():
+            for w in ws:
+                cawq.gemm_qkv(x, w.qweight, w.qzeros, w.scales, g, nq, nkv, out=tuple(outs))
+        n = 2 if m >= 2048 else reps
+        r[f"M={m}"] = {lab: round(_graph_us(fn, n, stream) / copies, 2) for lab, fn in
+                       (("three_gemms_us", three), ("fused_qkv_split_us", split))}
+    res["qwen2_7b_qkv"] = r
+    del ws, parts
     return res
 
 
