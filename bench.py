@@ -329,6 +329,7 @@ def run_ours(a, rank, local_rank, world):
         extras["qwen2_m_sweep"] = qwen2_sweep(dev)
         extras["fused_neighbours"] = fused_neighbour_numbers(dev)
         extras["tp_llama3_70b_mlp"] = tp_mlp_numbers(dev, world, max_over_ranks)
+        extras["tp_fused_collectives"] = tp_fused_numbers(dev, world, max_over_ranks)
 
     if world > 1:
         del graph
@@ -562,6 +563,59 @@ def fused_neighbour_numbers(dev, reps=10):
                        (("three_gemms_us", three), ("fused_qkv_split_us", split))}
     res["qwen2_7b_qkv"] = r
     del ws, parts
+    return res
+
+
+def tp_fused_numbers(dev, world, max_over_ranks, reps=10):
+    """configs[4] layers with the collective fused into the GEMM's epilogue
+    (backend "p2p": pushes over NVLink + flag exchange) against the GEMM
+    followed by NCCL (backend "native"): gate_up column-parallel WITH the
+    all-gather (full [M, 57344] on every rank) and down row-parallel
+    (all-reduce). us per call, back-to-back calls, max over ranks."""
+    import torch
+
+    from cube_awq_b200 import synth, tp
+    k1, n1, k2, n2, g, dt = 8192, 57344, 28672, 8192, GROUP, torch.float16
+    comm = tp.TPComm(timeout_ms=120000)
+    slot = max(2048 * n1 * 2, world * 2048 * n2 * 4)
+    peers = tp.TPPeers(comm, 256 + 2 * slot + 4096, timeout_ms=10000)
+    w1 = synth.make_weights(k1, n1, g, dt, dev, seed=4101)
+    w2 = synth.make_weights(k2, n2, g, dt, dev, seed=4102)
+    mk_col = lambda be: tp.ColumnParallelAWQLinear(w1.qweight, w1.qzeros, w1.scales, backend=be,
+                                                   comm=comm, peers=peers)
+    mk_row = lambda be: tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend=be,
+                                                comm=comm, peers=peers)
+    layers = {"gate_up_colpar": (mk_col("native"), mk_col("p2p"), k1),
+              "down_rowpar": (mk_row("native"), mk_row("p2p"), k2 // world)}
+    del w1, w2
+    torch.cuda.empty_cache()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    res = {"n_gpus": world, "p2p": "GEMM epilogue pushes to peer buffers (CUDA IPC) + flags",
+           "native": "GEMM then NCCL (all-gather + interleave / fp32 all-reduce + epilogue)"}
+    for m in (1, 8, 2048):
+        r = {}
+        for name, (ln, lp, kin) in layers.items():
+            x = synth.make_input(m, kin, dt, dev, seed=4103)
+            for lab, layer in (("nccl_us", ln), ("fused_p2p_us", lp)):
+                for _ in range(3):
+                    layer.forward(x)
+                torch.cuda.synchronize()
+                n_it = 3 if m >= 2048 else reps
+                e0.record()
+                for _ in range(n_it):
+                    layer.forward(x)
+                e1.record()
+                e1.synchronize()
+                r.setdefault(name, {})[lab] = round(
+                    max_over_ranks(e0.elapsed_time(e1) / n_it) * 1e3, 2)
+        res[f"M={m}"] = r
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()  # every rank's last fused call has completed
+    peers.close()
+    comm.close()
+    del layers
     return res
 
 

@@ -23,7 +23,7 @@ from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, a
                      validate_launch_params, version)
 from .modules import (AWQGateUpSiluMul, AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear,
                       AWQLinearConfig, AWQQKVLinear)
-from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm
+from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm, TPPeers
 from .loader import load_awq_linears
 
 import os as _os
@@ -39,7 +39,7 @@ if _os.path.exists(_lib.LIB_PATH):
 __all__ = [
     "AWQGateUpSiluMul", "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
     "AWQQKVLinear",
-    "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "load_awq_linears",
+    "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "TPPeers", "load_awq_linears",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
     "dequantize_awq", "dequantize_native", "device_error", "gemm", "gemm_qkv", "gemm_silu_mul",

@@ -48,11 +48,21 @@ EXPORTED = (
     "cawq_tp_column_shard", "cawq_tp_row_shard", "cawq_tp_interleave_columns",
     "cawq_tp_unique_id", "cawq_tp_init", "cawq_tp_destroy", "cawq_tp_info",
     "cawq_gemm_colpar", "cawq_gemm_rowpar", "cawq_gemm_rowpar_noalloc",
+    "cawq_tp_p2p_create", "cawq_tp_p2p_destroy", "cawq_gemm_colpar_p2p", "cawq_gemm_rowpar_p2p",
 )
 
 CAWQ_ROWPAR_SCRATCH_FLOATS = 1 << 20
 
 CAWQ_TP_ID_BYTES = 128
+CAWQ_TP_MAX_PEERS = 8
+CAWQ_TP_P2P_HEADER = 256
+
+
+class PeersC(ctypes.Structure):
+    """cawq_tp_peers: every rank's peer buffer as mapped in this process."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("base", ctypes.c_void_p * CAWQ_TP_MAX_PEERS), ("bytes", ctypes.c_size_t),
+                ("timeout_ms", ctypes.c_int)]
 
 
 class ShapeConfigC(ctypes.Structure):
@@ -163,6 +173,16 @@ def _declare(L) -> None:
     L.cawq_gemm_rowpar.restype = st
     L.cawq_gemm_rowpar_noalloc.argtypes = tp_args[:7] + tp_args[8:]
     L.cawq_gemm_rowpar_noalloc.restype = st
+    peers_p = ctypes.POINTER(PeersC)
+    L.cawq_tp_p2p_create.argtypes = [vp, sz, i, ctypes.POINTER(peers_p)]
+    L.cawq_tp_p2p_create.restype = st
+    L.cawq_tp_p2p_destroy.argtypes = [peers_p]
+    L.cawq_tp_p2p_destroy.restype = st
+    p2p_args = [peers_p, ctypes.c_uint32, vp, vp, vp, vp, vp, vp, sz, sz, sz, sz, i, vp]
+    L.cawq_gemm_colpar_p2p.argtypes = p2p_args
+    L.cawq_gemm_colpar_p2p.restype = st
+    L.cawq_gemm_rowpar_p2p.argtypes = p2p_args
+    L.cawq_gemm_rowpar_p2p.restype = st
 
 
 def lib():

@@ -17,6 +17,7 @@
 #include <string>
 #include <thread>
 #include <tuple>
+#include <vector>
 
 #include "cawq_internal.h"
 
@@ -270,7 +271,7 @@ static bool plan_supports(const GemmProblem& p, const cawq_plan& plan, const Dev
   switch (plan.path) {
     case CAWQ_PATH_DECODE: return decode_supports(p, plan, dev);
     case CAWQ_PATH_PREFILL: return prefill_supports(p, plan, dev);
-    case CAWQ_PATH_GENERIC: return p.epi == 0 && generic_supports(p);
+    case CAWQ_PATH_GENERIC: return p.epi == 0 && p.nrep == 0 && generic_supports(p);
     default: return false;
   }
 }
@@ -349,7 +350,8 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
                                size_t k, size_t n, size_t g, cawq_dtype dtype,
                                cawq_dtype out_dtype, cawq_order order, size_t ld_out,
                                const cawq_plan* plan, void* stream, bool module_rules,
-                               int epi = 0, const QkvOut* qkv = nullptr) {
+                               int epi = 0, const QkvOut* qkv = nullptr,
+                               void* const* reps = nullptr, int nrep = 0) {
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype))
     return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
   if (out_dtype != dtype && out_dtype != CAWQ_F32)
@@ -394,6 +396,8 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
     p.col_k = qkv->col_k;
     p.col_v = qkv->col_v;
   }
+  for (int i = 0; i < nrep; ++i) p.rep[i] = reps[i];
+  p.nrep = nrep;
   cawq_plan pl = plan ? *plan : choose_plan(p, dev);
   if (plan && !plan_supports(p, pl, dev))
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "the plan cannot run this problem");
@@ -1058,6 +1062,223 @@ CAWQ_API cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x,
   if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
   cudaError_t e = launch_rowpar_finish(partial, bias, out, rows, n, dtype, s);
   if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
+  return CAWQ_OK;
+}
+
+// ------------------------------------------ fused tensor-parallel push
+// A cawq_tp_peers made by cawq_tp_p2p_create: the public struct first, then
+// what the library needs to release it.
+struct P2POwned {
+  cawq_tp_peers pub;
+  void* own = nullptr;
+  bool opened[CAWQ_TP_MAX_PEERS] = {};
+};
+
+// An NCCL all-reduce of one float, as a barrier on the communicator's ranks.
+static cawq_status tp_barrier(const cawq_tp_comm* comm, float* dev_word, cudaStream_t s) {
+  ncclResult_t r = nccl().all_reduce(dev_word, dev_word, 1, ncclFloat32, ncclSum, comm->comm, s);
+  if (r == ncclInProgress) {
+    cawq_status st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
+    if (st != CAWQ_OK) return st;
+  } else if (r != ncclSuccess) {
+    return nccl_fail(r, "ncclAllReduce");
+  }
+  cudaError_t e = cudaStreamSynchronize(s);
+  return e == cudaSuccess ? CAWQ_OK : cuda_fail(e, "barrier");
+}
+
+static void p2p_release(P2POwned* o) {
+  for (int j = 0; j < CAWQ_TP_MAX_PEERS; ++j)
+    if (o->opened[j]) cudaIpcCloseMemHandle(o->pub.base[j]);
+  if (o->own) cudaFree(o->own);
+  delete o;
+}
+
+CAWQ_API cawq_status cawq_tp_p2p_create(const cawq_tp_comm* comm, size_t bytes, int timeout_ms,
+                                        cawq_tp_peers** peers) {
+  cawq_status st = tp_check(comm);
+  if (st != CAWQ_OK) return st;
+  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  if (comm->world > CAWQ_TP_MAX_PEERS)
+    return fail(CAWQ_ERR_INVALID_ARGUMENT, fmt("world %d above %d", comm->world, CAWQ_TP_MAX_PEERS));
+  if (bytes < CAWQ_TP_P2P_HEADER + 512)
+    return fail(CAWQ_ERR_INVALID_SHAPE, "bytes must hold the flag header and two slots");
+  auto* o = new P2POwned();
+  o->pub.world = comm->world;
+  o->pub.rank = comm->rank;
+  o->pub.bytes = bytes;
+  o->pub.timeout_ms = timeout_ms;
+  cudaStream_t s = nullptr;
+  void* tmp = nullptr;
+  auto bail = [&](cawq_status r) {
+    if (tmp) cudaFree(tmp);
+    if (s) cudaStreamDestroy(s);
+    p2p_release(o);
+    return r;
+  };
+  cudaError_t e = cudaMalloc(&o->own, bytes);
+  if (e != cudaSuccess) { o->own = nullptr; return bail(cuda_fail(e, "cudaMalloc (peer buffer)")); }
+  // zero before any peer can see the buffer: flags start below every epoch
+  if ((e = cudaMemset(o->own, 0, bytes)) != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) return bail(cuda_fail(e, "cudaDeviceSynchronize"));
+  o->pub.base[comm->rank] = o->own;
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, o->own)) != cudaSuccess)
+    return bail(cuda_fail(e, "cudaIpcGetMemHandle"));
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  if ((e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess)
+    return bail(cuda_fail(e, "cudaStreamCreate"));
+  if ((e = cudaMalloc(&tmp, hb * comm->world + 16)) != cudaSuccess) {
+    tmp = nullptr;
+    return bail(cuda_fail(e, "cudaMalloc (handle exchange)"));
+  }
+  uint8_t* dh = static_cast<uint8_t*>(tmp);
+  if ((e = cudaMemcpy(dh + comm->rank * hb, &h, hb, cudaMemcpyHostToDevice)) != cudaSuccess)
+    return bail(cuda_fail(e, "cudaMemcpy"));
+  ncclResult_t r = nccl().all_gather(dh + comm->rank * hb, dh, hb, ncclUint8, comm->comm, s);
+  if (r == ncclInProgress) {
+    if ((st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllGather")) != CAWQ_OK)
+      return bail(st);
+  } else if (r != ncclSuccess) {
+    return bail(nccl_fail(r, "ncclAllGather"));
+  }
+  if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return bail(cuda_fail(e, "handle exchange"));
+  std::vector<cudaIpcMemHandle_t> all(comm->world);
+  if ((e = cudaMemcpy(all.data(), dh, hb * comm->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return bail(cuda_fail(e, "cudaMemcpy"));
+  for (int j = 0; j < comm->world; ++j) {
+    if (j == comm->rank) continue;
+    e = cudaIpcOpenMemHandle(&o->pub.base[j], all[j], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaIpcOpenMemHandle"));
+    o->opened[j] = true;
+  }
+  // every rank has mapped every buffer before any push
+  float* word = reinterpret_cast<float*>(dh + hb * comm->world);
+  if ((e = cudaMemsetAsync(word, 0, sizeof(float), s)) != cudaSuccess)
+    return bail(cuda_fail(e, "cudaMemsetAsync"));
+  if ((st = tp_barrier(comm, word, s)) != CAWQ_OK) return bail(st);
+  cudaFree(tmp);
+  cudaStreamDestroy(s);
+  *peers = &o->pub;
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_tp_p2p_destroy(cawq_tp_peers* peers) {
+  if (!peers) return CAWQ_OK;
+  auto* o = reinterpret_cast<P2POwned*>(peers);
+  // A rank's last fused call ended only after every peer's last push into
+  // this buffer had completed (its finish step waits for all of them), so
+  // once this device is idle nothing writes here any more.
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  p2p_release(o);
+  return CAWQ_OK;
+}
+
+// Checks a peer table for one fused call and returns this call's slot
+// offset (the slot alternates with the epoch's parity).
+static cawq_status p2p_check(const cawq_tp_peers* peers, uint32_t epoch, size_t need,
+                             size_t* slot_off) {
+  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  if (peers->world < 1 || peers->world > CAWQ_TP_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world)
+    return fail(CAWQ_ERR_INVALID_ARGUMENT, "peers: world must be 1..8 and rank below it");
+  for (int j = 0; j < peers->world; ++j)
+    if (!peers->base[j] || reinterpret_cast<uintptr_t>(peers->base[j]) % 256 != 0)
+      return fail(CAWQ_ERR_ALIGNMENT, "peers: every base must be non-null and 256-byte aligned");
+  if (epoch == 0) return fail(CAWQ_ERR_INVALID_ARGUMENT, "epoch must start at 1");
+  const size_t slot = peers->bytes > CAWQ_TP_P2P_HEADER
+                          ? ((peers->bytes - CAWQ_TP_P2P_HEADER) / 2) & ~static_cast<size_t>(255)
+                          : 0;
+  if (need > slot)
+    return fail(CAWQ_ERR_INVALID_SHAPE,
+                fmt("the call needs %zu bytes per slot, the peer buffers have %zu", need, slot));
+  *slot_off = CAWQ_TP_P2P_HEADER + (epoch & 1u) * slot;
+  return CAWQ_OK;
+}
+
+static P2PSync p2p_sync(const cawq_tp_peers* peers, uint32_t epoch) {
+  P2PSync s = {};
+  for (int j = 0; j < peers->world; ++j) s.flags[j] = static_cast<uint32_t*>(peers->base[j]);
+  s.world = peers->world;
+  s.rank = peers->rank;
+  s.epoch = epoch;
+  const int ms = peers->timeout_ms > 0 ? peers->timeout_ms : 2000;
+  s.timeout_ns = static_cast<uint64_t>(ms) * 1000000ull;
+  return s;
+}
+
+CAWQ_API cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch,
+                                          const void* x, const uint32_t* qweight,
+                                          const uint32_t* qzeros, const void* scales,
+                                          const void* bias, void* out, size_t rows, size_t k,
+                                          size_t n, size_t group_size, cawq_dtype dtype,
+                                          void* stream) {
+  if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
+    return fail(CAWQ_ERR_DTYPE, "the fused tensor-parallel layers take CAWQ_F16 or CAWQ_BF16");
+  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  size_t n0 = 0, nl = 0;
+  cawq_status st = cawq_tp_column_shard(n, peers->world, peers->rank, &n0, &nl);
+  if (st != CAWQ_OK) return st;
+  const size_t es = dtype_size(dtype);
+  size_t off = 0;
+  if ((st = p2p_check(peers, epoch, rows * n * es, &off)) != CAWQ_OK) return st;
+  if (rows == 0) return CAWQ_OK;
+  if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+  // this rank's columns of the gathered [rows, n] result, in every buffer
+  void* dst[CAWQ_TP_MAX_PEERS];
+  int nrep = 0;
+  for (int j = 0; j < peers->world; ++j) {
+    void* d = static_cast<uint8_t*>(peers->base[j]) + off + n0 * es;
+    if (j == peers->rank) dst[CAWQ_TP_MAX_PEERS - 1] = d;
+    else dst[nrep++] = d;
+  }
+  st = gemm_common(x, qweight, qzeros, scales, bias, dst[CAWQ_TP_MAX_PEERS - 1], rows, k, nl,
+                   group_size, dtype, dtype, CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0, nullptr,
+                   dst, nrep);
+  if (st != CAWQ_OK) return st;
+  const void* slot = static_cast<uint8_t*>(peers->base[peers->rank]) + off;
+  cudaError_t e = launch_p2p_colpar_finish(p2p_sync(peers, epoch), slot, out, rows, n, n, dtype,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  return CAWQ_OK;
+}
+
+CAWQ_API cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t epoch,
+                                          const void* x, const uint32_t* qweight,
+                                          const uint32_t* qzeros, const void* scales,
+                                          const void* bias, void* out, size_t rows, size_t k,
+                                          size_t n, size_t group_size, cawq_dtype dtype,
+                                          void* stream) {
+  if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
+    return fail(CAWQ_ERR_DTYPE, "the fused tensor-parallel layers take CAWQ_F16 or CAWQ_BF16");
+  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  size_t k0 = 0, kl = 0;
+  cawq_status st = cawq_tp_row_shard(k, group_size, peers->world, peers->rank, &k0, &kl);
+  if (st != CAWQ_OK) return st;
+  if (n % 32 != 0) return fail(CAWQ_ERR_INVALID_SHAPE, "n must be a multiple of 32");
+  size_t off = 0;
+  const size_t plane = rows * n * sizeof(float);
+  if ((st = p2p_check(peers, epoch, plane * peers->world, &off)) != CAWQ_OK) return st;
+  if (rows == 0) return CAWQ_OK;
+  if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+  // this rank's fp32 partial into plane [rank] of every buffer's slot
+  void* dst[CAWQ_TP_MAX_PEERS];
+  int nrep = 0;
+  for (int j = 0; j < peers->world; ++j) {
+    void* d = static_cast<uint8_t*>(peers->base[j]) + off + peers->rank * plane;
+    if (j == peers->rank) dst[CAWQ_TP_MAX_PEERS - 1] = d;
+    else dst[nrep++] = d;
+  }
+  st = gemm_common(x, qweight, qzeros, scales, nullptr, dst[CAWQ_TP_MAX_PEERS - 1], rows, kl, n,
+                   group_size, dtype, CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0,
+                   nullptr, dst, nrep);
+  if (st != CAWQ_OK) return st;
+  const float* slot = reinterpret_cast<const float*>(
+      static_cast<uint8_t*>(peers->base[peers->rank]) + off);
+  cudaError_t e = launch_p2p_rowpar_finish(p2p_sync(peers, epoch), slot, bias, out, rows, n, dtype,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
   return CAWQ_OK;
 }
 

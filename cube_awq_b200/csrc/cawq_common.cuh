@@ -182,10 +182,24 @@ struct OutMap {
   OT* p1;
   OT* p2;
   uint32_t ld0, ld1, ld2, c1, c2;
+  // replicas of a single-range output (peer buffers): rep[i] + (a - p0)
+  OT* rep[7];
+  uint32_t nrep;
   __device__ __forceinline__ OT* at(uint32_t row, uint32_t col) const {
     if (col < c1) return p0 + (size_t)row * ld0 + col;
     if (col < c2) return p1 + (size_t)row * ld1 + (col - c1);
     return p2 + (size_t)row * ld2 + (col - c2);
+  }
+  // stores v at `a` (an address from at()) and, with REP, at every replica
+  template <bool REP, typename V>
+  __device__ __forceinline__ void put(OT* a, const V& v) const {
+    *reinterpret_cast<V*>(a) = v;
+    if constexpr (REP) {
+      const size_t off = static_cast<size_t>(a - p0);
+#pragma unroll
+      for (int i = 0; i < 7; ++i)
+        if (static_cast<uint32_t>(i) < nrep) *reinterpret_cast<V*>(rep[i] + off) = v;
+    }
   }
 };
 
@@ -206,6 +220,8 @@ inline OutMap<OT> out_map(const GemmProblem& p) {
     m.ld1 = m.ld2 = m.ld0;
     m.c1 = m.c2 = 0xFFFFFFFFu;
   }
+  for (int i = 0; i < 7; ++i) m.rep[i] = static_cast<OT*>(p.rep[i]);
+  m.nrep = static_cast<uint32_t>(p.nrep);
   return m;
 }
 

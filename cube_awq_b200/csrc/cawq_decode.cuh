@@ -956,7 +956,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
             if (col < n) {
               float v = outv[m][e][c];
               if (bias) v += DType<DT>::to_f32(bias[col]);
-              *om.at(row, col) = DType<ODT>::from_f32(v);
+              om.template put<EPI == 2>(om.at(row, col), DType<ODT>::from_f32(v));
             }
           }
         }
@@ -1025,7 +1025,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
       if (col < n) {
         if (bias) v += DType<DT>::to_f32(bias[col]);
-        *om.at(row, col) = DType<ODT>::from_f32(v);
+        om.template put<EPI == 2>(om.at(row, col), DType<ODT>::from_f32(v));
       }
     }
   }
@@ -1048,7 +1048,8 @@ static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 // warp hold fewer CTAs per SM, which costs more than its faster inner loop
 // gains in chains of dependent launches.
 static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
-  return plan.reserved[2] == 1 && p.epi == 0 && p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
+  return plan.reserved[2] == 1 && p.epi == 0 && p.nrep == 0 &&
+         p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
          p.g % kDecStageRows == 0 && plan.warps <= kDecI8MaxStrips;
 }
 
@@ -1080,6 +1081,10 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   // SiLU-gated epilogue: whole 256-column gate / up blocks, AWQ order, output
   // in the input dtype
   if (p.epi == 1 && (p.n % 256 != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype))
+    return false;
+  // replicated output (tensor-parallel push): plain epilogue, one output
+  // range, f16 / bf16 activations, AWQ order
+  if (p.nrep > 0 && (p.epi != 0 || p.out_k || p.dtype == kF32 || p.order != kOrderAwq))
     return false;
   const size_t bands =
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps);
@@ -1161,6 +1166,18 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
 template <int DT, int ODT, int ORDER>
 static cudaError_t launch_decode_m(const GemmProblem& p, const cawq_plan& plan) {
   const bool ga = p.g % kDecStageRows == 0;  // groups end on stage boundaries
+  if (p.nrep > 0) {
+    // EPI 2: the plain epilogue, each element also stored to the replicas
+    if constexpr (DT != kF32 && ORDER == kOrderAwq) {
+      if (decode_mt(p.rows) == 1) {
+        return ga ? launch_decode_t<DT, ODT, ORDER, 1, true, false, 2>(p, plan)
+                  : launch_decode_t<DT, ODT, ORDER, 1, false, false, 2>(p, plan);
+      }
+      return ga ? launch_decode_t<DT, ODT, ORDER, 2, true, false, 2>(p, plan)
+                : launch_decode_t<DT, ODT, ORDER, 2, false, false, 2>(p, plan);
+    }
+    return cudaErrorInvalidValue;
+  }
   if constexpr (DT == ODT && ORDER == kOrderAwq) {
     if (p.epi == 1) {
       if (decode_mt(p.rows) == 1) {

@@ -38,6 +38,12 @@ struct GemmProblem {
   void* out_k = nullptr;
   void* out_v = nullptr;
   size_t ld_k = 0, ld_v = 0, col_k = 0, col_v = 0;
+  // replicas of the (single-range) output: every element is also stored at
+  // the same offset from rep[i] as from `out` — other GPUs' buffers, mapped
+  // into this process (the push of a fused tensor-parallel collective).
+  // Decode and prefill kernels, f16 / bf16 activations, AWQ order only.
+  void* rep[7] = {};
+  int nrep = 0;
 };
 
 // Thread-local error message (cawq_last_error).
@@ -94,6 +100,28 @@ cudaError_t launch_interleave_columns(const void* src, void* dst, size_t rows, s
                                       int world, size_t elem, cudaStream_t stream);
 cudaError_t launch_rowpar_finish(const float* partial, const void* bias, void* out, size_t rows,
                                  size_t n, int dtype, cudaStream_t stream);
+// Fused tensor-parallel push: every rank's peer buffer starts with a flag
+// word per rank. flags[j] is rank j's flag array as mapped in this process
+// (flags[rank] = this rank's own). Rank r publishes `epoch` in word r of
+// every peer's array once its pushed data is complete, then waits until word
+// j of its own array holds `epoch` for every peer j (at most timeout_ns).
+constexpr int kP2PMaxWorld = 8;
+struct P2PSync {
+  uint32_t* flags[kP2PMaxWorld];
+  int world, rank;
+  uint32_t epoch;
+  uint64_t timeout_ns;
+};
+// After the push of a column-parallel GEMM: signal, wait, then copy the
+// gathered [rows, n] result (dense in `slot`) to out (row stride ld_out).
+cudaError_t launch_p2p_colpar_finish(const P2PSync& s, const void* slot, void* out, size_t rows,
+                                     size_t n, size_t ld_out, int dtype, cudaStream_t stream);
+// After the push of a row-parallel GEMM's fp32 partials into slot[world][rows][n]:
+// signal, wait, then out = sum over ranks (in rank order) + bias, cast to dtype.
+cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const void* bias,
+                                     void* out, size_t rows, size_t n, int dtype,
+                                     cudaStream_t stream);
+
 // Device address of the current device's static row-parallel scratch
 // (CAWQ_ROWPAR_SCRATCH_FLOATS floats).
 cudaError_t rowpar_static_scratch(float** ptr);

@@ -452,14 +452,15 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
         for (int i = 0; i < 32; ++i) v[i] += DType<DT>::to_f32(bias[col0 + i]);
       }
       typename DType<ODT>::T* o = om.at(row, col0);  // the chunk lies in one output
+      constexpr bool kRep = EPI == 2;  // also store to the replicas
       if constexpr (ODT == kF32) {
         if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            om.template put<kRep>(o + i, make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = v[i];
+          for (int i = 0; i < 32; ++i) om.template put<kRep>(o + i, v[i]);
         }
       } else {
         using OT = typename DType<ODT>::T;
@@ -470,11 +471,11 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
             OT* hp = reinterpret_cast<OT*>(&pk);
 #pragma unroll
             for (int e = 0; e < 8; ++e) hp[e] = DType<ODT>::from_f32(v[i + e]);
-            *reinterpret_cast<uint4*>(o + i) = pk;
+            om.template put<kRep>(o + i, pk);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = DType<ODT>::from_f32(v[i]);
+          for (int i = 0; i < 32; ++i) om.template put<kRep>(o + i, DType<ODT>::from_f32(v[i]));
         }
       }
     };
@@ -511,7 +512,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
       }
     };
     if (split == 1) {
-      if (ok && EPI == 0) {
+      if (ok && EPI != 1) {
 #pragma unroll 1
         for (int cc = part * kChunks; cc < (part + 1) * kChunks; ++cc) {
           const int h = cc >> 3, c = cc & 7;
@@ -625,7 +626,7 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
               if (col + e < n) {
                 float vv = v4[e];
                 if (bias) vv += DType<DT>::to_f32(bias[col + e]);
-                o[e] = DType<ODT>::from_f32(vv);
+                om.template put<EPI == 2>(o + e, DType<ODT>::from_f32(vv));
               }
             }
           }
@@ -748,6 +749,9 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
   if (p.epi == 1 && (p.n % kPfBN != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype ||
                      (halves == 2 && split > 1)))
     return false;
+  // replicated output (tensor-parallel push): plain epilogue, one output
+  // range, AWQ order
+  if (p.nrep > 0 && (p.epi != 0 || p.out_k || p.order != kOrderAwq)) return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
@@ -804,6 +808,10 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
 
 template <int DT, int ODT>
 static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split) {
+  if (p.nrep > 0) {  // EPI 2: plain epilogue, each store also to the replicas
+    return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 2>(p, split)
+                       : launch_prefill_t<DT, ODT, kOrderAwq, 2, 2>(p, split);
+  }
   if constexpr (DT == ODT) {
     if (p.epi == 1) {
       return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 1>(p, split)

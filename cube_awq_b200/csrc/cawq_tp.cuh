@@ -6,7 +6,9 @@
 //     all-reduce of a row-parallel layer (the bias is added once, after the
 //     full sum, as the single-device layer does);
 //   * interleave_gate_up: the block-interleaved gate / up column order of
-//     the SiLU-gated GEMM, from the plain [gate | up] layout.
+//     the SiLU-gated GEMM, from the plain [gate | up] layout;
+//   * p2p_*_finish: the signal / wait / gather or reduce step that follows a
+//     GEMM whose epilogue pushed its output into the other ranks' buffers.
 #pragma once
 
 #include <mutex>
@@ -118,6 +120,134 @@ cudaError_t launch_interleave_gate_up(const void* src, void* dst, size_t rows, s
   } else {
     interleave_gate_up_kernel<uint16_t><<<(unsigned)blocks, 256, 0, stream>>>(
         static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), rows, width_e, block_e);
+  }
+  return cudaGetLastError();
+}
+
+// ------------------------------------------- fused tensor-parallel push
+// Every block publishes the epoch to each peer (a repeated store of the same
+// value is harmless), then one thread per block waits, bounded, for every
+// peer's epoch in this rank's own flag words. The data the flags cover was
+// written by the previous kernel of the stream (the GEMM's replicated
+// epilogue), which has completed when this kernel starts; the system-scope
+// fence and release store publish it, the acquire load and the block barrier
+// make it visible to the block's readers. On timeout: bit 1 of the device
+// error word, and the block does nothing more.
+// flags[j] by selects, so the kernel parameter is not copied to local memory
+__device__ __forceinline__ uint32_t* p2p_flags(const P2PSync& s, int j) {
+  uint32_t* p = s.flags[0];
+#pragma unroll
+  for (int i = 1; i < kP2PMaxWorld; ++i)
+    if (j == i) p = s.flags[i];
+  return p;
+}
+
+__device__ __forceinline__ bool p2p_signal_and_wait(const P2PSync& s) {
+  __shared__ int ok;
+  if (threadIdx.x < static_cast<unsigned>(s.world) && threadIdx.x != static_cast<unsigned>(s.rank)) {
+    __threadfence_system();
+    uint32_t* f = p2p_flags(s, threadIdx.x) + s.rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(s.epoch) : "memory");
+  }
+  if (threadIdx.x == 0) {
+    int good = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int j = 0; j < s.world && good; ++j) {
+      if (j == s.rank) continue;
+      const uint32_t* f = p2p_flags(s, s.rank) + j;
+      for (uint32_t it = 0;; ++it) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (static_cast<int32_t>(v - s.epoch) >= 0) break;
+        if ((it & 15u) == 15u && globaltimer_ns() - t0 > s.timeout_ns) {
+          atomicOr(&g_cawq_device_error, 2u);
+          good = 0;
+          break;
+        }
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+template <typename V>
+__global__ void __launch_bounds__(256)
+    p2p_colpar_finish_kernel(const P2PSync s, const V* __restrict__ slot, V* __restrict__ out,
+                             size_t rows, size_t nv, size_t ldv) {
+  if (!p2p_signal_and_wait(s)) return;
+  const size_t total = rows * nv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / nv, c = i - r * nv;
+    out[r * ldv + c] = __ldcg(slot + i);  // L2: peers wrote it
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256)
+    p2p_rowpar_finish_kernel(const P2PSync s, const float* __restrict__ slot,
+                             const typename DType<DT>::T* __restrict__ bias,
+                             typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
+  if (!p2p_signal_and_wait(s)) return;
+  const size_t quads = rows * n / 4;  // n % 4 == 0
+  const size_t plane = rows * n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < quads;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < s.world; ++j) {  // rank order: the same sum on every rank
+      const float4 f = __ldcg(reinterpret_cast<const float4*>(slot + j * plane) + i);
+      acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
+    }
+    const size_t e0 = 4 * i, c = e0 % n;
+    const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      out[e0 + e] = DType<DT>::from_f32(v[e] + (bias ? DType<DT>::to_f32(bias[c + e]) : 0.f));
+  }
+}
+
+static unsigned p2p_blocks(size_t work) {
+  size_t b = (work + 255) / 256;
+  if (b > 148 * 4) b = 148 * 4;  // all blocks resident: each one waits
+  return static_cast<unsigned>(b < 1 ? 1 : b);
+}
+
+cudaError_t launch_p2p_colpar_finish(const P2PSync& s, const void* slot, void* out, size_t rows,
+                                     size_t n, size_t ld_out, int dtype, cudaStream_t stream) {
+  const size_t es = dtype == kF32 ? 4 : 2;
+  const bool v16 = (n * es) % 16 == 0 && (ld_out * es) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(slot) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (v16) {
+    const size_t nv = n * es / 16;
+    p2p_colpar_finish_kernel<uint4><<<p2p_blocks(rows * nv), 256, 0, stream>>>(
+        s, static_cast<const uint4*>(slot), static_cast<uint4*>(out), rows, nv, ld_out * es / 16);
+  } else if (es == 4) {
+    p2p_colpar_finish_kernel<uint32_t><<<p2p_blocks(rows * n), 256, 0, stream>>>(
+        s, static_cast<const uint32_t*>(slot), static_cast<uint32_t*>(out), rows, n, ld_out);
+  } else {
+    p2p_colpar_finish_kernel<uint16_t><<<p2p_blocks(rows * n), 256, 0, stream>>>(
+        s, static_cast<const uint16_t*>(slot), static_cast<uint16_t*>(out), rows, n, ld_out);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const void* bias,
+                                     void* out, size_t rows, size_t n, int dtype,
+                                     cudaStream_t stream) {
+  const unsigned b = p2p_blocks(rows * n / 4);
+  if (dtype == kF32) {
+    p2p_rowpar_finish_kernel<kF32><<<b, 256, 0, stream>>>(
+        s, slot, static_cast<const float*>(bias), static_cast<float*>(out), rows, n);
+  } else if (dtype == kF16) {
+    p2p_rowpar_finish_kernel<kF16><<<b, 256, 0, stream>>>(
+        s, slot, static_cast<const __half*>(bias), static_cast<__half*>(out), rows, n);
+  } else {
+    p2p_rowpar_finish_kernel<kBF16><<<b, 256, 0, stream>>>(
+        s, slot, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), rows,
+        n);
   }
   return cudaGetLastError();
 }

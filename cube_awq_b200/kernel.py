@@ -475,7 +475,8 @@ def autotune(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scale
 
 
 def device_error(reset: bool = True) -> int:
-    """Device-side error word (bit 0: a bounded wait timed out). Synchronises."""
+    """Device-side error word (bit 0: a bounded wait timed out; bit 1: a fused
+    tensor-parallel call gave up waiting for a peer). Synchronises."""
     w = ctypes.c_uint32(0)
     check(_lib.lib().cawq_device_error(1 if reset else 0, ctypes.byref(w)))
     return int(w.value)

@@ -22,6 +22,10 @@ Two collective back ends:
 * ``backend="native"``: the library's own NCCL communicator (``TPComm``); one
   C call (cawq_gemm_colpar / cawq_gemm_rowpar) runs the GEMM, the collective
   and the epilogue on the caller's stream — the path a non-Python host uses.
+* ``backend="p2p"``: the collective fused into the GEMM (``TPPeers``; C calls
+  cawq_gemm_colpar_p2p / cawq_gemm_rowpar_p2p): the GEMM's epilogue stores
+  its output into every rank's peer buffer over NVLink, and a small kernel
+  exchanges flags (bounded wait) and finishes the gather or the sum.
 """
 
 from __future__ import annotations
@@ -114,6 +118,56 @@ class TPComm:
             pass
 
 
+class TPPeers:
+    """Peer buffers of the fused tensor-parallel layers (cawq_tp_p2p_create):
+    one buffer of ``nbytes`` per rank, mapped into every rank's process over
+    CUDA IPC, set up collectively over ``comm``. Every fused call takes the
+    next epoch of this object, so all ranks must make the same calls in the
+    same order. ``timeout_ms`` bounds each wait for the peers' flags."""
+
+    def __init__(self, comm: Optional["TPComm"], nbytes: int, timeout_ms: int = 2000,
+                 _table=None):
+        self.epoch = 0
+        self._owned = _table is None
+        if _table is None:
+            p = ctypes.POINTER(_lib.PeersC)()
+            check(_lib.lib().cawq_tp_p2p_create(comm.handle, nbytes, timeout_ms, ctypes.byref(p)))
+            self.table = p
+        else:
+            self.table = _table
+        self.world = self.table.contents.world
+        self.rank = self.table.contents.rank
+        self.slot_bytes = ((nbytes - _lib.CAWQ_TP_P2P_HEADER) // 2) // 256 * 256
+
+    @classmethod
+    def from_pointers(cls, world: int, rank: int, bases, nbytes: int,
+                      timeout_ms: int = 2000) -> "TPPeers":
+        """A table over buffers the caller has mapped itself (any symmetric
+        memory allocator); they must be zero before the first call."""
+        t = _lib.PeersC()
+        t.world, t.rank, t.bytes, t.timeout_ms = world, rank, nbytes, timeout_ms
+        for j, b in enumerate(bases):
+            t.base[j] = b
+        obj = cls(None, nbytes, timeout_ms, _table=ctypes.pointer(t))
+        obj._keep = t
+        return obj
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def close(self) -> None:
+        if self._owned and getattr(self, "table", None):
+            check(_lib.lib().cawq_tp_p2p_destroy(self.table))
+        self.table = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 GemmFn = Callable[..., torch.Tensor]
 
 
@@ -137,20 +191,25 @@ class ColumnParallelAWQLinear:
 
     def __init__(self, qweight, qzeros, scales, bias=None, *, group=None,
                  gather_output: bool = True, backend: str = "torch",
-                 comm: Optional[TPComm] = None, gemm: Optional[GemmFn] = None):
+                 comm: Optional[TPComm] = None, gemm: Optional[GemmFn] = None,
+                 peers: Optional[TPPeers] = None):
         self.group = group
-        self.world, self.rank = _world_rank(group)
+        # the fused layers' ranks are the peer table's
+        self.world, self.rank = ((peers.world, peers.rank) if backend == "p2p" and peers
+                                 else _world_rank(group))
         self.n = scales.shape[1]
         self.k = qweight.shape[0]
         self.group_size = self.k // scales.shape[0]
         self.qweight, self.qzeros, self.scales, self.bias = shard_columns(
             qweight, qzeros, scales, bias, self.world, self.rank)
         self.gather_output = gather_output
-        if backend not in ("torch", "native"):
-            raise ValueError("backend must be 'torch' or 'native'")
+        if backend not in ("torch", "native", "p2p"):
+            raise ValueError("backend must be 'torch', 'native' or 'p2p'")
         if backend == "native" and comm is None:
             raise ValueError("backend='native' needs a TPComm")
-        self.backend, self.comm = backend, comm
+        if backend == "p2p" and peers is None:
+            raise ValueError("backend='p2p' needs TPPeers")
+        self.backend, self.comm, self.peers = backend, comm, peers
         self.gemm = gemm or fused_gemm
         self._gather_ws = None
 
@@ -160,6 +219,13 @@ class ColumnParallelAWQLinear:
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         m = x2.shape[0]
+        if self.backend == "p2p" and self.gather_output:
+            out = torch.empty(m, self.n, dtype=x2.dtype, device=x2.device)
+            check(_lib.lib().cawq_gemm_colpar_p2p(
+                self.peers.table, self.peers.next_epoch(), _ptr(x2), _ptr(self.qweight),
+                _ptr(self.qzeros), _ptr(self.scales), _ptr(self.bias), _ptr(out), m, self.k,
+                self.n, self.group_size, cawq_dtype(x2.dtype), _stream_ptr(x2)))
+            return out.reshape(*lead, self.n)
         if self.backend == "native" and self.gather_output:
             out = torch.empty(m, self.n, dtype=x2.dtype, device=x2.device)
             ws = None
@@ -196,9 +262,12 @@ class RowParallelAWQLinear:
 
     def __init__(self, qweight, qzeros, scales, bias=None, *, group=None,
                  input_is_parallel: bool = True, backend: str = "torch",
-                 comm: Optional[TPComm] = None, gemm: Optional[GemmFn] = None):
+                 comm: Optional[TPComm] = None, gemm: Optional[GemmFn] = None,
+                 peers: Optional[TPPeers] = None):
         self.group = group
-        self.world, self.rank = _world_rank(group)
+        # the fused layers' ranks are the peer table's
+        self.world, self.rank = ((peers.world, peers.rank) if backend == "p2p" and peers
+                                 else _world_rank(group))
         self.k = qweight.shape[0]
         self.n = scales.shape[1]
         self.group_size = self.k // scales.shape[0]
@@ -207,11 +276,13 @@ class RowParallelAWQLinear:
                                                             self.group_size, self.world, self.rank)
         self.bias = bias
         self.input_is_parallel = input_is_parallel
-        if backend not in ("torch", "native"):
-            raise ValueError("backend must be 'torch' or 'native'")
+        if backend not in ("torch", "native", "p2p"):
+            raise ValueError("backend must be 'torch', 'native' or 'p2p'")
         if backend == "native" and comm is None:
             raise ValueError("backend='native' needs a TPComm")
-        self.backend, self.comm = backend, comm
+        if backend == "p2p" and peers is None:
+            raise ValueError("backend='p2p' needs TPPeers")
+        self.backend, self.comm, self.peers = backend, comm, peers
         self.gemm = gemm or fused_gemm
         self._partial = None
 
@@ -223,6 +294,13 @@ class RowParallelAWQLinear:
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         m = x2.shape[0]
+        if self.backend == "p2p":
+            out = torch.empty(m, self.n, dtype=x2.dtype, device=x2.device)
+            check(_lib.lib().cawq_gemm_rowpar_p2p(
+                self.peers.table, self.peers.next_epoch(), _ptr(x2), _ptr(self.qweight),
+                _ptr(self.qzeros), _ptr(self.scales), _ptr(self.bias), _ptr(out), m, self.k,
+                self.n, self.group_size, cawq_dtype(x2.dtype), _stream_ptr(x2)))
+            return out.reshape(*lead, self.n)
         if self.backend == "native":
             if self._partial is None or self._partial.numel() < m * self.n:
                 self._partial = torch.empty(m * self.n, dtype=torch.float32, device=x2.device)

@@ -133,7 +133,8 @@ int cawq_device_supported(int device);
 
 /*
  * Reads (and with reset != 0 clears) the device-side error word of the
- * current device: bit 0 = a bounded wait inside a kernel timed out.
+ * current device: bit 0 = a bounded wait inside a kernel timed out; bit 1 =
+ * a fused tensor-parallel call gave up waiting for a peer's flag.
  * Synchronises the device.
  */
 cawq_status cawq_device_error(int reset, uint32_t* word);
@@ -451,6 +452,84 @@ cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const void* x,
                                      const void* scales, const void* bias, void* out,
                                      size_t rows, size_t k, size_t n, size_t group_size,
                                      cawq_dtype dtype, void* stream);
+
+/* ----------------------------------------------------------------------- */
+/* Fused tensor-parallel layers: the collective in the GEMM's epilogue      */
+/* (no reference counterpart; the reference is single-device)               */
+/* ----------------------------------------------------------------------- */
+/*
+ * Instead of a GEMM followed by an NCCL collective, the GEMM's epilogue
+ * stores its output straight into every rank's peer buffer over NVLink
+ * (plain stores through peer mappings, as each output tile is finished),
+ * then a small kernel publishes a flag to every peer, waits (bounded) for
+ * theirs, and finishes the collective from its own buffer.
+ *
+ * Peer buffers: one per rank, the same size everywhere, each mapped into
+ * every rank's process. A buffer holds CAWQ_TP_P2P_HEADER bytes of flag
+ * words (zero before the first call), then two slots of
+ * ((bytes - CAWQ_TP_P2P_HEADER) / 2) rounded down to 256 bytes; a call uses
+ * slot (epoch & 1), so the slot a peer writes is never the one this rank is
+ * still reading.
+ */
+#define CAWQ_TP_MAX_PEERS 8
+#define CAWQ_TP_P2P_HEADER 256
+typedef struct cawq_tp_peers {
+  int world;                     /* ranks, 1..CAWQ_TP_MAX_PEERS              */
+  int rank;                      /* this rank                                */
+  void* base[CAWQ_TP_MAX_PEERS]; /* every rank's buffer in this process's
+                                    address space (base[rank]: its own);
+                                    256-byte aligned                        */
+  size_t bytes;                  /* size of each buffer                      */
+  int timeout_ms;                /* bound of the wait for peers (<= 0: 2 s);
+                                    on timeout bit 1 of cawq_device_error's
+                                    word is set and the output is not
+                                    written                                 */
+} cawq_tp_peers;
+
+/*
+ * Collective over the communicator's ranks: allocates this rank's buffer of
+ * `bytes` on the current device (once, at set-up), zeroes it, exchanges
+ * CUDA IPC handles over NCCL and maps every peer's buffer. The table is
+ * owned by the library; release it with cawq_tp_p2p_destroy. Callers that
+ * map buffers their own way (any symmetric-memory allocator) fill a
+ * cawq_tp_peers themselves instead.
+ */
+cawq_status cawq_tp_p2p_create(const cawq_tp_comm* comm, size_t bytes, int timeout_ms,
+                               cawq_tp_peers** peers);
+/* Unmaps and frees a table made by cawq_tp_p2p_create, once every rank's
+   last fused call has completed (synchronises this device). */
+cawq_status cawq_tp_p2p_destroy(cawq_tp_peers* peers);
+
+/*
+ * Column-parallel layer with the all-gather in the epilogue: the same
+ * shards and result as cawq_gemm_colpar (out [rows, n] in full on every
+ * rank), f16 / bf16. The local GEMM writes its [rows, n/world] columns into
+ * the slot of every rank's buffer; the finish kernel copies the gathered
+ * slot to `out`. Needs rows * n * sizeof(F) bytes per slot. Every rank makes
+ * the same fused calls in the same order, each with the next `epoch` of
+ * this peer table (1, 2, 3, ...: one counter per table, shared by all
+ * layers that use it).
+ */
+cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,
+                                 const uint32_t* qweight, const uint32_t* qzeros,
+                                 const void* scales, const void* bias, void* out, size_t rows,
+                                 size_t k, size_t n, size_t group_size, cawq_dtype dtype,
+                                 void* stream);
+/*
+ * Row-parallel layer with the all-reduce in the epilogue: the same shards
+ * and result as cawq_gemm_rowpar, f16 / bf16. The local GEMM writes its fp32
+ * partial [rows, n] into plane [rank] of the slot of every rank's buffer
+ * (a one-shot all-reduce: each rank then sums the world planes in rank
+ * order, adds the bias once and casts). Needs world * rows * n * 4 bytes per
+ * slot; the bytes each rank sends grow with world - 1, so for large rows on
+ * more than two ranks cawq_gemm_rowpar's ring all-reduce moves fewer bytes.
+ * Epochs as for cawq_gemm_colpar_p2p.
+ */
+cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,
+                                 const uint32_t* qweight, const uint32_t* qzeros,
+                                 const void* scales, const void* bias, void* out, size_t rows,
+                                 size_t k, size_t n, size_t group_size, cawq_dtype dtype,
+                                 void* stream);
 
 #ifdef __cplusplus
 }

@@ -3,8 +3,10 @@
 Each rank builds the column- and row-parallel layers from the same full
 tensors and checks the full output against the fp64 oracle of the
 unsharded layer, with torch.distributed's NCCL and with the library's own
-communicator (cawq_gemm_colpar / cawq_gemm_rowpar). Rows 1 and 8 run the
-decode kernel (rows = 1 gathers in place), 300 the tensor-core kernel.
+communicator (cawq_gemm_colpar / cawq_gemm_rowpar), and with the collective
+fused into the GEMM's epilogue (cawq_gemm_colpar_p2p / _rowpar_p2p, also
+compared bit for bit with the NCCL path). Rows 1 and 8 run the decode kernel
+(rows = 1 gathers in place), 300 the tensor-core kernel.
 """
 
 import multiprocessing as mp
@@ -26,7 +28,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("backend", ["torch", "native"])
+@pytest.mark.parametrize("backend", ["torch", "native", "p2p"])
 def test_two_gpu_tensor_parallel(backend):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

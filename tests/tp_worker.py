@@ -86,7 +86,8 @@ def cpu_rank(rank, world, port, case, q):
 def gpu_rank(rank, world, port, cases, backend, q):
     import torch
     import torch.distributed as dist
-    comm = None
+    comm = peers = None
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     try:
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
@@ -94,8 +95,10 @@ def gpu_rank(rank, world, port, cases, backend, q):
                                 world_size=world, timeout=timedelta(seconds=60), device_id=dev)
         import oracle
         from cube_awq_b200 import tp
-        if backend == "native":
+        if backend in ("native", "p2p"):
             comm = tp.TPComm(timeout_ms=60000)
+        if backend == "p2p":
+            peers = tp.TPPeers(comm, 16 << 20, timeout_ms=5000)
         msgs = []
         for (k, n, g, rows) in cases:
             x, qw, qz, s, b = problem(k, n, g, rows, seed=k + n + rows)
@@ -105,11 +108,26 @@ def gpu_rank(rank, world, port, cases, backend, q):
                                   dtype="f16", deq_round=False)
             d = lambda t: t.to(dev)
             col = tp.ColumnParallelAWQLinear(d(qw), d(qz), d(sh), d(bh), backend=backend,
-                                             comm=comm)
+                                             comm=comm, peers=peers)
             y = col.forward(d(xh))
             row = tp.RowParallelAWQLinear(d(qw), d(qz), d(sh), d(bh), input_is_parallel=False,
-                                          backend=backend, comm=comm)
+                                          backend=backend, comm=comm, peers=peers)
             y2 = row.forward(d(xh))
+            if backend == "p2p":
+                # again (the other slot), then bit for bit against the NCCL path:
+                # the same local GEMM, and with two ranks the same fp32 sum
+                y_again, y2_again = col.forward(d(xh)), row.forward(d(xh))
+                ncol = tp.ColumnParallelAWQLinear(d(qw), d(qz), d(sh), d(bh), backend="native",
+                                                  comm=comm)
+                nrow = tp.RowParallelAWQLinear(d(qw), d(qz), d(sh), d(bh),
+                                               input_is_parallel=False, backend="native",
+                                               comm=comm)
+                yn, y2n = ncol.forward(d(xh)), nrow.forward(d(xh))
+                torch.cuda.synchronize()
+                for name, a_, b_ in (("colpar", y, yn), ("colpar again", y_again, yn),
+                                     ("rowpar", y2, y2n), ("rowpar again", y2_again, y2n)):
+                    if not torch.equal(a_, b_):
+                        msgs.append(f"p2p {name} k={k} n={n} rows={rows} differs from NCCL")
             torch.cuda.synchronize()
             for name, got in (("colpar", y), ("rowpar", y2)):
                 g64 = got.float().cpu().numpy().astype(np.float64)
@@ -119,6 +137,11 @@ def gpu_rank(rank, world, port, cases, backend, q):
         from cube_awq_b200 import device_error
         if device_error() != 0:
             msgs.append("device error word set")
+        if peers is not None:
+            torch.cuda.synchronize()
+            dist.barrier()  # every rank's last fused call has completed
+            peers.close()
+            peers = None
         if comm is not None:
             comm.close()
             comm = None
