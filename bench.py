@@ -566,66 +566,94 @@ def fused_neighbour_numbers(dev, reps=10):
     return res
 
 
-def tp_fused_numbers(dev, world, max_over_ranks, reps=10):
+def _timed_calls(call, n_it, max_over_ranks):
+    """us per call of `call(i)` issued back to back (direct C calls, so the
+    host stays ahead of the GPU), device-timed, max over ranks."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(n_it):
+        call(i)
+    e1.record()
+    e1.synchronize()
+    return round(max_over_ranks(e0.elapsed_time(e1) / n_it) * 1e3, 2)
+
+
+def tp_fused_numbers(dev, world, max_over_ranks, reps=20):
     """configs[4] layers with the collective fused into the GEMM's epilogue
-    (backend "p2p": pushes over NVLink + flag exchange) against the GEMM
-    followed by NCCL (backend "native"): gate_up column-parallel WITH the
-    all-gather (full [M, 57344] on every rank) and down row-parallel
-    (all-reduce). us per call, back-to-back calls, max over ranks."""
+    (cawq_gemm_colpar_p2p / _rowpar_p2p: pushes over NVLink + flag exchange)
+    against the GEMM followed by NCCL (cawq_gemm_colpar / _rowpar): gate_up
+    column-parallel WITH the all-gather (full [M, 57344] on every rank) and
+    down row-parallel (all-reduce). us per call, max over ranks."""
     import torch
 
-    from cube_awq_b200 import synth, tp
+    from cube_awq_b200 import _lib, synth, tp
+    from cube_awq_b200.errors import check
     k1, n1, k2, n2, g, dt = 8192, 57344, 28672, 8192, GROUP, torch.float16
     comm = tp.TPComm(timeout_ms=120000)
     slot = max(2048 * n1 * 2, world * 2048 * n2 * 4)
     peers = tp.TPPeers(comm, 256 + 2 * slot + 4096, timeout_ms=10000)
     w1 = synth.make_weights(k1, n1, g, dt, dev, seed=4101)
     w2 = synth.make_weights(k2, n2, g, dt, dev, seed=4102)
-    mk_col = lambda be: tp.ColumnParallelAWQLinear(w1.qweight, w1.qzeros, w1.scales, backend=be,
-                                                   comm=comm, peers=peers)
-    mk_row = lambda be: tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend=be,
-                                                comm=comm, peers=peers)
-    layers = {"gate_up_colpar": (mk_col("native"), mk_col("p2p"), k1),
-              "down_rowpar": (mk_row("native"), mk_row("p2p"), k2 // world)}
+    col = tp.ColumnParallelAWQLinear(w1.qweight, w1.qzeros, w1.scales, backend="native",
+                                     comm=comm)
+    row = tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend="native", comm=comm)
     del w1, w2
     torch.cuda.empty_cache()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    res = {"n_gpus": world, "p2p": "GEMM epilogue pushes to peer buffers (CUDA IPC) + flags",
-           "native": "GEMM then NCCL (all-gather + interleave / fp32 all-reduce + epilogue)"}
+    L = _lib.lib()
+    f16 = _lib.CAWQ_F16
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    res = {"n_gpus": world, "fused_p2p": "GEMM epilogue pushes to peer buffers (CUDA IPC) + flags",
+           "nccl": "GEMM, then NCCL all-gather + interleave / fp32 all-reduce + epilogue"}
     for m in (1, 8, 2048):
+        x1 = synth.make_input(m, k1, dt, dev, seed=4103)
+        x2 = synth.make_input(m, k2 // world, dt, dev, seed=4104)
+        out1 = torch.empty(m, n1, dtype=dt, device=dev)
+        out2 = torch.empty(m, n2, dtype=dt, device=dev)
+        ws = torch.empty(m * n1, dtype=dt, device=dev)
+        part = torch.empty(m * n2, dtype=torch.float32, device=dev)
+        cargs = (x1.data_ptr(), col.qweight.data_ptr(), col.qzeros.data_ptr(),
+                 col.scales.data_ptr(), None, out1.data_ptr())
+        rargs = (x2.data_ptr(), row.qweight.data_ptr(), row.qzeros.data_ptr(),
+                 row.scales.data_ptr(), None, out2.data_ptr())
+        calls = {
+            ("gate_up_colpar", "nccl_us"): lambda i: check(L.cawq_gemm_colpar(
+                comm.handle, *cargs, ws.data_ptr(), m, k1, n1, g, f16, stream)),
+            ("gate_up_colpar", "fused_p2p_us"): lambda i: check(L.cawq_gemm_colpar_p2p(
+                peers.table, peers.next_epoch(), *cargs, m, k1, n1, g, f16, stream)),
+            ("down_rowpar", "nccl_us"): lambda i: check(L.cawq_gemm_rowpar(
+                comm.handle, *rargs, part.data_ptr(), m, k2, n2, g, f16, stream)),
+            ("down_rowpar", "fused_p2p_us"): lambda i: check(L.cawq_gemm_rowpar_p2p(
+                peers.table, peers.next_epoch(), *rargs, m, k2, n2, g, f16, stream)),
+        }
         r = {}
-        for name, (ln, lp, kin) in layers.items():
-            x = synth.make_input(m, kin, dt, dev, seed=4103)
-            for lab, layer in (("nccl_us", ln), ("fused_p2p_us", lp)):
-                for _ in range(3):
-                    layer.forward(x)
-                torch.cuda.synchronize()
-                n_it = 3 if m >= 2048 else reps
-                e0.record()
-                for _ in range(n_it):
-                    layer.forward(x)
-                e1.record()
-                e1.synchronize()
-                r.setdefault(name, {})[lab] = round(
-                    max_over_ranks(e0.elapsed_time(e1) / n_it) * 1e3, 2)
+        for (name, lab), call in calls.items():
+            for i in range(3):
+                call(i)
+            r.setdefault(name, {})[lab] = _timed_calls(call, 3 if m >= 2048 else reps,
+                                                       max_over_ranks)
         res[f"M={m}"] = r
+        del x1, x2, out1, out2, ws, part
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()  # every rank's last fused call has completed
     peers.close()
     comm.close()
-    del layers
+    del col, row
     return res
 
 
-def tp_mlp_numbers(dev, world, max_over_ranks, reps=10):
+def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
     """configs[4] over all ranks of the job: us per MLP forward (gate_up
     column-parallel without the gather, then down row-parallel on this rank's
-    half of the gate_up columns, as after the SiLU-and-mul), max over ranks."""
+    share of the gate_up columns, as after the SiLU-and-mul), GEMM + NCCL
+    path, direct C calls, max over ranks."""
     import torch
 
-    from cube_awq_b200 import synth, tp
+    from cube_awq_b200 import _lib, synth, tp
+    from cube_awq_b200.errors import check
     k1, n1, k2, n2, g, dt = 8192, 57344, 28672, 8192, GROUP, torch.float16
     comm = tp.TPComm(timeout_ms=120000)
     w1 = synth.make_weights(k1, n1, g, dt, dev, seed=4001)
@@ -635,29 +663,38 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=10):
     row = tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend="native", comm=comm)
     del w1, w2
     torch.cuda.empty_cache()
+    L = _lib.lib()
+    f16 = _lib.CAWQ_F16
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    nl = n1 // world
     res = {"n_gpus": world, "backend": "native NCCL (cawq_gemm_rowpar)"}
-    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     for m in (1, 8, 2048):
         x = synth.make_input(m, k1, dt, dev, seed=4003)
-        for _ in range(3):
-            h = col.forward(x)
-            row.forward(h[:, :k2 // world].contiguous())
-        torch.cuda.synchronize()
-        t_col = t_row = 0.0
-        for _ in range(reps):
-            e[0].record()
-            h = col.forward(x)
-            hh = h[:, :k2 // world].contiguous()
-            e[1].record()
-            row.forward(hh)
-            e[2].record()
-            e[2].synchronize()
-            t_col += e[0].elapsed_time(e[1])
-            t_row += e[1].elapsed_time(e[2])
-        t_col = max_over_ranks(t_col / reps) * 1e3
-        t_row = max_over_ranks(t_row / reps) * 1e3
-        res[f"M={m}"] = {"us": round(t_col + t_row, 2), "gate_up_colpar_us": round(t_col, 2),
-                         "down_rowpar_allreduce_us": round(t_row, 2)}
+        h = torch.empty(m, nl, dtype=dt, device=dev)
+        hh = h[:, :k2 // world]  # this rank's share of the down input (row stride nl)
+        hh_c = torch.empty(m, k2 // world, dtype=dt, device=dev)
+        out = torch.empty(m, n2, dtype=dt, device=dev)
+        part = torch.empty(m * n2, dtype=torch.float32, device=dev)
+
+        def col_call(i):
+            check(L.cawq_gemm(x.data_ptr(), col.qweight.data_ptr(), col.qzeros.data_ptr(),
+                              col.scales.data_ptr(), None, h.data_ptr(), m, k1, nl, g, f16, f16,
+                              _lib.CAWQ_ORDER_AWQ, nl, stream))
+
+        def row_call(i):
+            hh_c.copy_(hh)
+            check(L.cawq_gemm_rowpar(comm.handle, hh_c.data_ptr(), row.qweight.data_ptr(),
+                                     row.qzeros.data_ptr(), row.scales.data_ptr(), None,
+                                     out.data_ptr(), part.data_ptr(), m, k2, n2, g, f16, stream))
+        for i in range(3):
+            col_call(i)
+            row_call(i)
+        n_it = 3 if m >= 2048 else reps
+        t_col = _timed_calls(col_call, n_it, max_over_ranks)
+        t_row = _timed_calls(row_call, n_it, max_over_ranks)
+        res[f"M={m}"] = {"us": round(t_col + t_row, 2), "gate_up_colpar_us": t_col,
+                         "down_rowpar_allreduce_us": t_row}
+        del x, h, hh_c, out, part
     del col, row
     comm.close()
     return res
