@@ -74,6 +74,13 @@ constexpr int kDecI8MaxStrips = 4;
 //   [X tile: XB rows x 64 k, 128B swizzle][W: strips/2 x 64 rows x 128 B, 128B swizzle]
 //   [S: gps rows x band columns, F][Z: gps rows x band/8 words]
 // gps = quantization groups a 64-row stage can touch.
+// Columns of a band each CTA of a split-K cluster sums: the band's 8-column
+// words dealt out in equal slices, rounded up (the last slice is shorter
+// when split does not divide the words).
+__host__ __device__ constexpr uint32_t dec_ncols(uint32_t bcols, uint32_t split) {
+  return (bcols / 8 + split - 1) / split * 8;
+}
+
 template <int DT, int MT>
 struct DecodeLayout {
   using T = typename DType<DT>::T;
@@ -102,15 +109,16 @@ struct DecodeLayout {
     const size_t raw = z_off(strips, g) + gps(g) * z_row_bytes(strips);
     return (raw + 1023) / 1024 * 1024;
   }
-  // split-K receive buffer: [source rank][XB rows][band columns / split] fp32
-  static __host__ __device__ size_t recv_bytes(int strips) {
-    return (size_t)XB * strips * kDecTileCols * 4;
+  // split-K receive buffer: [source rank][XB rows][dec_ncols] fp32
+  static __host__ __device__ size_t recv_bytes(int strips, uint32_t split) {
+    return (size_t)XB * split * dec_ncols(static_cast<uint32_t>(strips * kDecTileCols), split) * 4;
   }
   // integer path: after the receive buffer, kDecI8BSlots tables of the
   // stage's B fragments (4 steps x 32 lanes x 16 bytes) and, per X row,
   // {1 / scale, sum(x_int) / scale}
-  static size_t smem_bytes(int strips, int stages, uint32_t g, bool i8 = false) {
-    return 1024 /* alignment slack */ + slot_bytes(strips, g) * stages + recv_bytes(strips) +
+  static size_t smem_bytes(int strips, int stages, uint32_t g, uint32_t split, bool i8 = false) {
+    return 1024 /* alignment slack */ + slot_bytes(strips, g) * stages +
+           recv_bytes(strips, split) +
            (i8 ? (size_t)kDecI8BSlots * kDecI8BSlot : 0) +
            (size_t)((i8 ? 3 : 2) * stages + (i8 ? 2 * kDecI8BSlots : 0) + 1) * 8;
   }
@@ -172,7 +180,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 
   const size_t ring_bytes = slot * NS;
   float* recv = reinterpret_cast<float*>(smem + ring_bytes);
-  uint8_t* btabs = smem + ring_bytes + L::recv_bytes(strips);  // integer path: B tables
+  uint8_t* btabs = smem + ring_bytes + L::recv_bytes(strips, split);  // integer path: B tables
   uint64_t* full = reinterpret_cast<uint64_t*>(
       btabs + (I8 ? (size_t)kDecI8BSlots * kDecI8BSlot : 0));
   uint64_t* empty = full + NS;
@@ -182,7 +190,11 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   uint64_t* recv_bar = I8 ? bempty + kDecI8BSlots : empty + NS;  // peers' partial sums landed
   const uint32_t rows_eff = rows < (uint32_t)XB ? rows : (uint32_t)XB;
   const uint32_t bcols = static_cast<uint32_t>(strips * kDecTileCols);
-  const uint32_t ncols = bcols / split;  // columns of the band this CTA sums (multiple of 8)
+  // CTA q of the cluster sums the band's columns [q ncols, q ncols + own):
+  // slices of whole 8-column words, the last one shorter when split does not
+  // divide the band's words
+  const uint32_t ncols = dec_ncols(bcols, split);
+  const uint32_t own = rank * ncols < bcols ? min(ncols, bcols - rank * ncols) : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -197,7 +209,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       }
     }
     mbar_init(recv_bar, 1);
-    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rows_eff * ncols * 4);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * rows_eff * own * 4);
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -1018,8 +1030,8 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       store_pair(row, rank * npair + p, gv, uv);
     }
   } else {
-    for (uint32_t idx = threadIdx.x; idx < rows_eff * ncols; idx += blockDim.x) {
-      const uint32_t row = idx / ncols, c = idx - row * ncols;
+    for (uint32_t idx = threadIdx.x; idx < rows_eff * own; idx += blockDim.x) {
+      const uint32_t row = idx / own, c = idx - row * own;
       const uint32_t col = pband * 8 + rank * ncols + c;
       float v = 0.f;
       for (uint32_t src = 0; src < split; ++src) v += recv[((size_t)src * XB + row) * ncols + c];
@@ -1057,12 +1069,13 @@ static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
   const uint32_t g = static_cast<uint32_t>(p.g);
   const bool mt1 = decode_mt(p.rows) == 1;
   const bool i8 = decode_use_i8(p, plan);
+  const uint32_t sp = plan.split < 1 ? 1u : static_cast<uint32_t>(plan.split);
   if (p.dtype == kF32) {
-    return mt1 ? DecodeLayout<kF32, 1>::smem_bytes(plan.warps, plan.stages, g)
-               : DecodeLayout<kF32, 2>::smem_bytes(plan.warps, plan.stages, g);
+    return mt1 ? DecodeLayout<kF32, 1>::smem_bytes(plan.warps, plan.stages, g, sp)
+               : DecodeLayout<kF32, 2>::smem_bytes(plan.warps, plan.stages, g, sp);
   }
-  return mt1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages, g, i8)
-             : DecodeLayout<kF16, 2>::smem_bytes(plan.warps, plan.stages, g);
+  return mt1 ? DecodeLayout<kF16, 1>::smem_bytes(plan.warps, plan.stages, g, sp, i8)
+             : DecodeLayout<kF16, 2>::smem_bytes(plan.warps, plan.stages, g, sp);
 }
 
 bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
@@ -1072,7 +1085,9 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   if (ax % 16 || aw % 16 || az % 16 || as % 16) return false;
-  if (plan.split < 1 || plan.split > 16 || (plan.split & (plan.split - 1))) return false;
+  if (plan.split < 1 || plan.split > 16) return false;
+  // any cluster size for the plain epilogue; powers of two for the SiLU one
+  if (p.epi == 1 && (plan.split & (plan.split - 1))) return false;
   if (plan.tile_n > 1) return false;
   if (plan.warps < 2 || (plan.warps & 1) || 2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
     return false;

@@ -104,7 +104,7 @@ def test_decode_default_plan_parity(cuda_device, dtype, rows, k, n, g):
     assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
 
 
-@pytest.mark.parametrize("split", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 6, 8, 12, 16])
 @pytest.mark.parametrize("warps", [2, 4, 6, 8])
 @pytest.mark.parametrize("stages", [1, 2, 3, 4])
 @pytest.mark.parametrize("rows,dtype,mma", [(3, "f32", "f16"), (3, "f16", "f16"),
@@ -112,9 +112,11 @@ def test_decode_default_plan_parity(cuda_device, dtype, rows, k, n, g):
                                             (11, "f16", "f16")])
 def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype, mma):
     # warps = 128-column strips per CTA (two consumer warps each), split = CTAs
-    # of a cluster along K; N = 1184 leaves the last band of every strip count
-    # partly out of range. mma "i8" selects the integer tensor path (rows <= 4
-    # with 16-bit X, here g = 128); "f16" is the f16 / bf16 MMA path.
+    # of a cluster along K (any size: the band's 8-column words are dealt out
+    # in rounded-up slices, so 12 CTAs over 2 strips leave the last one none);
+    # N = 1184 leaves the last band of every strip count partly out of range.
+    # mma "i8" selects the integer tensor path (rows <= 4 with 16-bit X, here
+    # g = 128); "f16" is the f16 / bf16 MMA path.
     if rows > 8 and 2 * warps > 8:
         pytest.skip("more warps than a 16-row tile allows")
     plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages, "mma": mma}
