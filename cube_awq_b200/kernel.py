@@ -42,8 +42,19 @@ def cawq_dtype(dtype: torch.dtype) -> int:
                          _lib.CAWQ_ERR_DTYPE) from None
 
 
+# The current stream of a device as a cudaStream_t, without building a
+# torch.cuda.Stream object (about 2 us per call otherwise).
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def current_stream_handle(device_index: int) -> int:
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 def stream_handle(t: torch.Tensor) -> Optional[int]:
-    return torch.cuda.current_stream(t.device).cuda_stream if t.is_cuda else None
+    return current_stream_handle(t.get_device()) if t.is_cuda else None
 
 
 def _desc(t: Optional[torch.Tensor]) -> _lib.TensorDescC:
@@ -370,7 +381,7 @@ class PreparedWeights:
     holds the tensors it was made from (``matches`` compares identity)."""
 
     __slots__ = ("qweight", "qzeros", "scales", "bias", "k", "n", "group_size", "dtype",
-                 "code", "order", "ptrs", "device")
+                 "code", "order", "ptrs", "device", "dev_index", "tail", "call")
 
     def __init__(self, qweight, qzeros, scales, group_size, bias=None, order="awq"):
         _require_cuda(qweight, qzeros, scales, bias)
@@ -399,6 +410,10 @@ class PreparedWeights:
         self.ptrs = (qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
                      bias.data_ptr() if bias is not None else None)
         self.device = scales.device
+        self.dev_index = scales.get_device()
+        # cawq_gemm's arguments after `rows`, and the bound C function
+        self.tail = (k, n, group_size, self.code, self.code, self.order, n)
+        self.call = _lib.lib().cawq_gemm
 
     def matches(self, qweight, qzeros, scales, bias) -> bool:
         return (self.qweight is qweight and self.qzeros is qzeros and self.scales is scales and
@@ -407,19 +422,23 @@ class PreparedWeights:
 
 def gemm_prepared(w: PreparedWeights, x: torch.Tensor) -> torch.Tensor:
     """cawq_gemm with prepared weights: x [rows, K] (contiguous, F) -> [rows, N]."""
+    # the per-call host work is kept to the checks, one allocation and one C
+    # call: at decode sizes it is of the order of the kernel's own time
     if x.dtype != w.dtype:
         raise DTypeError("scales and bias must have the input's float dtype (F)",
                          _lib.CAWQ_ERR_DTYPE)
-    if not x.is_cuda:
+    if x.get_device() != w.dev_index:
         _require_cuda(x)
+        raise CubeAwqError(f"x is on {x.device}, the weights on {w.device}",
+                           _lib.CAWQ_ERR_INVALID_ARGUMENT)
     rows, k = x.shape
     if k != w.k:
         raise ShapeError("input last dim (K) must match qweight rows", _lib.CAWQ_ERR_INVALID_SHAPE)
-    out = torch.empty((rows, w.n), dtype=w.dtype, device=x.device)
-    qw, qz, sc, b = w.ptrs
-    check(_lib.lib().cawq_gemm(x.data_ptr(), qw, qz, sc, b, out.data_ptr(), rows, k, w.n,
-                               w.group_size, w.code, w.code, w.order, w.n,
-                               torch.cuda.current_stream(x.device).cuda_stream))
+    out = x.new_empty((rows, w.n))
+    st = w.call(x.data_ptr(), *w.ptrs, out.data_ptr(), rows, *w.tail,
+                current_stream_handle(w.dev_index))
+    if st:
+        check(st)
     return out
 
 

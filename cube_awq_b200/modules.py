@@ -80,6 +80,11 @@ class AWQGEMMLinear:
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         """awq_gemm.rs:146-232: [..., K] -> [..., N]; bias fused after the K sum."""
+        w = self._prep
+        if (w is not None and input.dim() == 2 and input.shape[1] == w.k and
+                w.matches(self.qweight, self.qzeros, self.scales, self.bias) and
+                input.is_contiguous()):
+            return gemm_prepared(w, input)  # the common decode / prefill call
         _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
         k = input.shape[-1]
         _shape_assert(k > 0, "input last dim (K) must be > 0")
