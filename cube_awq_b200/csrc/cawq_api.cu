@@ -1177,8 +1177,7 @@ CAWQ_API cawq_status cawq_tp_p2p_destroy(cawq_tp_peers* peers) {
 
 // Checks a peer table for one fused call and returns this call's slot
 // offset (the slot alternates with the epoch's parity).
-static cawq_status p2p_check(const cawq_tp_peers* peers, uint32_t epoch, size_t need,
-                             size_t* slot_off) {
+static cawq_status p2p_table_check(const cawq_tp_peers* peers, uint32_t epoch) {
   if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
   if (peers->world < 1 || peers->world > CAWQ_TP_MAX_PEERS || peers->rank < 0 ||
       peers->rank >= peers->world)
@@ -1187,6 +1186,13 @@ static cawq_status p2p_check(const cawq_tp_peers* peers, uint32_t epoch, size_t 
     if (!peers->base[j] || reinterpret_cast<uintptr_t>(peers->base[j]) % 256 != 0)
       return fail(CAWQ_ERR_ALIGNMENT, "peers: every base must be non-null and 256-byte aligned");
   if (epoch == 0) return fail(CAWQ_ERR_INVALID_ARGUMENT, "epoch must start at 1");
+  return CAWQ_OK;
+}
+
+static cawq_status p2p_check(const cawq_tp_peers* peers, uint32_t epoch, size_t need,
+                             size_t* slot_off) {
+  cawq_status st = p2p_table_check(peers, epoch);
+  if (st != CAWQ_OK) return st;
   const size_t slot = peers->bytes > CAWQ_TP_P2P_HEADER
                           ? ((peers->bytes - CAWQ_TP_P2P_HEADER) / 2) & ~static_cast<size_t>(255)
                           : 0;
@@ -1216,9 +1222,10 @@ CAWQ_API cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t e
                                           void* stream) {
   if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
     return fail(CAWQ_ERR_DTYPE, "the fused tensor-parallel layers take CAWQ_F16 or CAWQ_BF16");
-  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  cawq_status st = p2p_table_check(peers, epoch);
+  if (st != CAWQ_OK) return st;
   size_t n0 = 0, nl = 0;
-  cawq_status st = cawq_tp_column_shard(n, peers->world, peers->rank, &n0, &nl);
+  st = cawq_tp_column_shard(n, peers->world, peers->rank, &n0, &nl);
   if (st != CAWQ_OK) return st;
   const size_t es = dtype_size(dtype);
   size_t off = 0;
@@ -1252,9 +1259,10 @@ CAWQ_API cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t e
                                           void* stream) {
   if (dtype != CAWQ_F16 && dtype != CAWQ_BF16)
     return fail(CAWQ_ERR_DTYPE, "the fused tensor-parallel layers take CAWQ_F16 or CAWQ_BF16");
-  if (!peers) return fail(CAWQ_ERR_NULL_POINTER, "peers must be non-null");
+  cawq_status st = p2p_table_check(peers, epoch);
+  if (st != CAWQ_OK) return st;
   size_t k0 = 0, kl = 0;
-  cawq_status st = cawq_tp_row_shard(k, group_size, peers->world, peers->rank, &k0, &kl);
+  st = cawq_tp_row_shard(k, group_size, peers->world, peers->rank, &k0, &kl);
   if (st != CAWQ_OK) return st;
   if (n % 32 != 0) return fail(CAWQ_ERR_INVALID_SHAPE, "n must be a multiple of 32");
   size_t off = 0;

@@ -106,3 +106,45 @@ def test_qkv_entry_checks_split_before_the_device():
     a = list(args(512, 128, 0))
     a[8] = 0  # no rows: nothing to do, no device needed
     assert lib.cawq_gemm_qkv(*a) == 0
+
+
+def test_p2p_entries_check_the_peer_table_before_the_device():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(16)
+
+    def table(world=2, rank=0, bases=(256, 512), nbytes=1 << 20):
+        t = _lib.PeersC()
+        t.world, t.rank, t.bytes, t.timeout_ms = world, rank, nbytes, 0
+        for j, b in enumerate(bases):
+            t.base[j] = b
+        return t
+
+    def call(t, epoch=1, rows=1, n=1024, dtype=_lib.CAWQ_F16, fn="cawq_gemm_colpar_p2p"):
+        return getattr(lib, fn)(ctypes.byref(t), epoch, p, p, p, p, None, p, rows, 512, n, 128,
+                                dtype, None)
+
+    assert call(table(), dtype=_lib.CAWQ_F32) == _lib.CAWQ_ERR_DTYPE
+    assert call(table(world=9, bases=[256] * 8)) == _lib.CAWQ_ERR_INVALID_ARGUMENT
+    assert call(table(bases=(256, 0))) == _lib.CAWQ_ERR_ALIGNMENT
+    assert call(table(bases=(256, 300))) == _lib.CAWQ_ERR_ALIGNMENT  # not 256-byte aligned
+    assert call(table(), epoch=0) == _lib.CAWQ_ERR_INVALID_ARGUMENT
+    assert call(table(nbytes=4096), rows=8) == _lib.CAWQ_ERR_INVALID_SHAPE
+    assert "per slot" in _lib.last_error()
+    # row-parallel needs world planes of fp32 partial sums per slot
+    # (4 KB slots: enough for one f16 row of the gather, not for 2 fp32 planes)
+    assert call(table(nbytes=256 + 2 * 4096), rows=1,
+                fn="cawq_gemm_rowpar_p2p") == _lib.CAWQ_ERR_INVALID_SHAPE
+    assert call(table(), n=1000) == _lib.CAWQ_ERR_INVALID_SHAPE  # not whole 32-column shards
+    assert call(table(), rows=0) == 0  # nothing to do, no device needed
+
+
+def test_p2p_layers_need_a_peer_table():
+    import torch
+    from cube_awq_b200 import tp
+    qw = torch.zeros(128, 8, dtype=torch.int32)
+    qz = torch.zeros(1, 8, dtype=torch.int32)
+    s = torch.ones(1, 64, dtype=torch.float16)
+    with pytest.raises(ValueError):
+        tp.ColumnParallelAWQLinear(qw, qz, s, backend="p2p")
+    with pytest.raises(ValueError):
+        tp.RowParallelAWQLinear(qw, qz, s, backend="p2p")
