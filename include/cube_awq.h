@@ -469,7 +469,8 @@ cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const void* x,
  * words (zero before the first call), then two slots of
  * ((bytes - CAWQ_TP_P2P_HEADER) / 2) rounded down to 256 bytes; a call uses
  * slot (epoch & 1), so the slot a peer writes is never the one this rank is
- * still reading.
+ * still reading. That holds when each rank's fused calls on one table run in
+ * order on the GPU (one stream, or streams the caller orders).
  */
 #define CAWQ_TP_MAX_PEERS 8
 #define CAWQ_TP_P2P_HEADER 256
