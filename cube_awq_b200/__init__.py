@@ -24,7 +24,7 @@ from .kernel import (DECODE_M_THRESHOLD, DECODE_TILE_M, ShapeConfig, autotune, a
 from .modules import (AWQGateUpSiluMul, AWQGEMMLinear, AWQGEMMLinearConfig, AWQLinear,
                       AWQLinearConfig, AWQQKVLinear)
 from .tp import ColumnParallelAWQLinear, RowParallelAWQLinear, TPComm, TPPeers
-from .loader import load_awq_linears
+from .loader import fuse_decoder_layers, load_awq_linears
 
 import os as _os
 
@@ -40,6 +40,7 @@ __all__ = [
     "AWQGateUpSiluMul", "AWQGEMMLinear", "AWQGEMMLinearConfig", "AWQLinear", "AWQLinearConfig",
     "AWQQKVLinear",
     "ColumnParallelAWQLinear", "RowParallelAWQLinear", "TPComm", "TPPeers", "load_awq_linears",
+    "fuse_decoder_layers",
     "CubeAwqError", "DeviceTimeoutError", "DTypeError", "ShapeError", "UnsupportedDeviceError",
     "DECODE_M_THRESHOLD", "DECODE_TILE_M", "ShapeConfig", "autotune", "awq_gemm_linear",
     "dequantize_awq", "dequantize_native", "device_error", "gemm", "gemm_qkv", "gemm_silu_mul",

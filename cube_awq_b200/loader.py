@@ -115,3 +115,50 @@ def load_awq_linears(path: Union[str, Iterable[str]], device: Union[str, torch.d
     if wanted is not None and wanted - set(layers):
         raise KeyError(f"layers not in the checkpoint: {sorted(wanted - set(layers))}")
     return layers
+
+
+# ----------------------------------------------------- fused neighbours
+_GATE_UP = ("gate_proj", "up_proj")
+_QKV = ("q_proj", "k_proj", "v_proj")
+
+
+def plan_fusions(names: Iterable[str]) -> Dict[str, tuple]:
+    """Groups of sibling layers that the fused modules can replace, by the
+    usual decoder-layer names: ``<p>.gate_proj`` + ``<p>.up_proj`` ->
+    ``<p>.gate_up_proj`` ("gate_up"), ``<p>.q_proj`` + ``<p>.k_proj`` +
+    ``<p>.v_proj`` -> ``<p>.qkv_proj`` ("qkv"). Returns {fused name: (kind,
+    member names in order)}; host-only, no tensors involved."""
+    names = set(names)
+    out: Dict[str, tuple] = {}
+    for name in sorted(names):
+        parent, _, leaf = name.rpartition(".")
+        base = parent + "." if parent else ""
+        if leaf == _GATE_UP[0] and base + _GATE_UP[1] in names:
+            out[base + "gate_up_proj"] = ("gate_up", tuple(base + m for m in _GATE_UP))
+        elif leaf == _QKV[0] and all(base + m in names for m in _QKV[1:]):
+            out[base + "qkv_proj"] = ("qkv", tuple(base + m for m in _QKV))
+    return out
+
+
+def fuse_decoder_layers(layers: Dict[str, AWQGEMMLinear]) -> Dict[str, object]:
+    """The loaded layers with each gate / up pair replaced by one
+    ``AWQGateUpSiluMul`` (``<p>.gate_up_proj``: forward gives silu(gate) *
+    up) and each q / k / v triple by one ``AWQQKVLinear`` (``<p>.qkv_proj``:
+    forward gives (q, k, v)). Groups the fused kernels cannot take (an
+    intermediate size that is not a multiple of 128, f32 scales, q / k / v
+    sizes that are not multiples of 32, mismatched shapes) stay as they are.
+    The fused modules hold their own copies of the weights (interleaved or
+    concatenated); the members are dropped from the returned dict."""
+    from .errors import CubeAwqError
+    from .modules import AWQGateUpSiluMul, AWQQKVLinear
+    out: Dict[str, object] = dict(layers)
+    for fused, (kind, members) in plan_fusions(layers).items():
+        parts = [layers[m] for m in members]
+        try:
+            mod = AWQGateUpSiluMul(*parts) if kind == "gate_up" else AWQQKVLinear(*parts)
+        except CubeAwqError:
+            continue
+        for m in members:
+            del out[m]
+        out[fused] = mod
+    return out

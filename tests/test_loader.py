@@ -96,3 +96,50 @@ def test_loaded_layers_run_on_the_gpu(checkpoint, cuda_device):
                           src["qzeros"].numpy().view(np.uint32), src["scales"].numpy(), 128,
                           bias=src["bias"].numpy(), dtype="f16", deq_round=False)
     assert max_rel_err(y.float().cpu().numpy().astype(np.float64), ref) <= GEMM_TOL["f16"]
+
+
+def test_plan_fusions_groups_decoder_siblings():
+    from cube_awq_b200.loader import plan_fusions
+    names = ["model.layers.0.mlp.gate_proj", "model.layers.0.mlp.up_proj",
+             "model.layers.0.mlp.down_proj", "model.layers.0.self_attn.q_proj",
+             "model.layers.0.self_attn.k_proj", "model.layers.0.self_attn.v_proj",
+             "model.layers.0.self_attn.o_proj", "model.layers.1.mlp.gate_proj",  # no up: alone
+             "model.layers.1.self_attn.q_proj", "model.layers.1.self_attn.k_proj"]  # no v
+    got = plan_fusions(names)
+    assert got == {
+        "model.layers.0.mlp.gate_up_proj": ("gate_up", ("model.layers.0.mlp.gate_proj",
+                                                        "model.layers.0.mlp.up_proj")),
+        "model.layers.0.self_attn.qkv_proj": ("qkv", ("model.layers.0.self_attn.q_proj",
+                                                      "model.layers.0.self_attn.k_proj",
+                                                      "model.layers.0.self_attn.v_proj")),
+    }
+
+
+@pytest.mark.gpu
+def test_fused_decoder_layers_match_the_separate_ones(tmp_path, cuda_device):
+    from safetensors.torch import save_file
+    from cube_awq_b200 import fuse_decoder_layers
+    rng = np.random.default_rng(11)
+    k = 256
+    src = {"m.0.mlp.gate_proj": _layer(rng, k, 256, 64), "m.0.mlp.up_proj": _layer(rng, k, 256, 64),
+           "m.0.attn.q_proj": _layer(rng, k, 256, 64, bias=True),
+           "m.0.attn.k_proj": _layer(rng, k, 64, 64, bias=True),
+           "m.0.attn.v_proj": _layer(rng, k, 64, 64, bias=True),
+           # an intermediate size of 192 is not whole 128-column blocks: stays unfused
+           "m.1.mlp.gate_proj": _layer(rng, k, 192, 64), "m.1.mlp.up_proj": _layer(rng, k, 192, 64)}
+    save_file({f"{p}.{n}": t for p, ts in src.items() for n, t in ts.items()},
+              str(tmp_path / "m.safetensors"))
+    layers = load_awq_linears(str(tmp_path), device=cuda_device)
+    fused = fuse_decoder_layers(layers)
+    assert set(fused) == {"m.0.mlp.gate_up_proj", "m.0.attn.qkv_proj", "m.1.mlp.gate_proj",
+                          "m.1.mlp.up_proj"}
+    x = torch.from_numpy(rng.standard_normal((5, k)).astype(np.float16)).to(cuda_device)
+    h = fused["m.0.mlp.gate_up_proj"](x)
+    g, u = layers["m.0.mlp.gate_proj"](x).float(), layers["m.0.mlp.up_proj"](x).float()
+    ref = torch.nn.functional.silu(g) * u
+    bound = 2.1 * GEMM_TOL["f16"] * g.abs().max() * u.abs().max()
+    assert (h.float() - ref).abs().max() <= bound + 2 ** -11 * ref.abs().max()
+    q, kk, v = fused["m.0.attn.qkv_proj"](x)
+    for got, name in ((q, "q_proj"), (kk, "k_proj"), (v, "v_proj")):
+        want = layers[f"m.0.attn.{name}"](x).float()
+        assert (got.float() - want).abs().max() <= 2 * GEMM_TOL["f16"] * want.abs().max()
