@@ -907,6 +907,45 @@ cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
     }
     return split;
   };
+  if (p.rows > 128) {
+    // 256-row tiles (two MMA halves sharing each dequantized stage) or
+    // 128-row tiles with more split K, whichever a cost model measured on
+    // B200 puts first (Qwen2-7B and Llama-2-7B linears at M = 192-512, every
+    // tile height and split): a launch takes waves x (fixed + 0.53 us per
+    // 64-row stage of the CTA's K share), the fixed part ~26 us for 256-row
+    // tiles (8 dequant / epilogue warps for twice the rows) and ~14 us for
+    // 128-row tiles, plus ~4 us for the 256-row tile's split-K hand-off. The
+    // model picked the measured best, or one within a few percent, in every
+    // case swept; at large M the 256-row tiles always win (the fixed part is
+    // paid by half as many tiles).
+    const size_t ntiles = (p.n + kPfBN - 1) / kPfBN;
+    double best = 1e300;
+    int best_w = 2, best_s = 1;
+    for (int warps : {2, 1}) {
+      for (int sp : {1, 2, 4, 8}) {
+        if (warps == 2 && sp > 4) continue;
+        if (sp > 1 && kt < (size_t)sp * 8) continue;
+        if (p.epi == 1 && warps == 2 && sp > 1) continue;
+        const size_t tiles = ntiles * ((p.rows + 128 * (size_t)warps - 1) / (128 * (size_t)warps));
+        const int act = sp == 1 ? static_cast<int>(sms)
+                                : (warps == 1 ? pf_max_active_clusters<1>(dev.device, sp)
+                                              : pf_max_active_clusters<2>(dev.device, sp));
+        if (act <= 0) continue;
+        const size_t waves = (tiles + act - 1) / act;
+        const size_t stages = (kt + sp - 1) / sp;
+        const double t = waves * ((warps == 2 ? 26.0 : 14.0) + 0.53 * stages) +
+                         (warps == 2 && sp > 1 ? 4.0 : 0.0);
+        if (t < best) {
+          best = t;
+          best_w = warps;
+          best_s = sp;
+        }
+      }
+    }
+    pl.warps = best_w;
+    pl.split = best_s;
+    return pl;
+  }
   int split = split_for(pl.warps);
   if (p.epi == 1 && pl.warps == 2 && split > 1) {
     // the 256-row tile's split-K hand-off has no SiLU epilogue: 128-row

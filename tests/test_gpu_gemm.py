@@ -351,3 +351,17 @@ def test_planner_splits_k_for_mid_m(cuda_device):
     assert p["path"] == PATH_PREFILL and p["warps"] == 1 and p["split"] == 4
     p = cawq.plan_get(2048, 4096, 4096, 128, torch.float16)
     assert p["path"] == PATH_PREFILL and p["warps"] == 2 and p["split"] == 1
+
+
+def test_planner_cost_model_for_rows_above_128(cuda_device):
+    # 128-row tiles with split K where 256-row tiles would leave most SMs
+    # idle (Qwen2 o_proj / down at M = 256: 14 column tiles), 256-row tiles
+    # where the columns alone fill the GPU (Qwen2 gate_up: 148 column tiles)
+    for n, k in ((3584, 3584), (3584, 18944)):
+        p = cawq.plan_get(256, k, n, 64, torch.float16)
+        assert p["path"] == PATH_PREFILL and p["warps"] == 1 and p["split"] >= 2, p
+    p = cawq.plan_get(256, 3584, 37888, 64, torch.float16)
+    assert p["path"] == PATH_PREFILL and p["warps"] == 2 and p["split"] == 1, p
+    for m in (1024, 2048, 4096):
+        p = cawq.plan_get(m, 4096, 22016, 128, torch.float16)
+        assert p["warps"] == 2, (m, p)
