@@ -279,12 +279,21 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The next kernel of the stream may launch now and set itself up while
+  // this one runs; it reads this kernel's output only after its own
+  // griddepcontrol.wait, which waits for this whole grid.
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------- X ring producer
     if (lane == 0) {
       bool ok = true;
       int issued = 0;
+      // X may be the previous kernel's output: wait for that grid (the
+      // weights, scales and zeros are loaded by warp 2 without waiting). The
+      // epilogue's stores come after every X stage, so they also follow the
+      // previous grid, which may still have been reading this output.
+      pdl_wait();
       for (int i = 0; i < KTL && ok; ++i) {
         const int s = i % L::kXSt, u = i / L::kXSt;
         if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
@@ -758,7 +767,7 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
 }
 
 template <int DT, int ODT, int ORDER, int HALVES, int EPI = 0>
-static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
+static cudaError_t launch_prefill_t(const GemmProblem& p, int split, bool pdl) {
   using T = typename DType<DT>::T;
   using OT = typename DType<ODT>::T;
   using L = PrefillLayout<HALVES>;
@@ -789,13 +798,20 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
   cfg.blockDim = dim3(pf_threads(L::kBM / 128));
   cfg.dynamicSmemBytes = L::kSmem;
   cfg.stream = p.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
   if (split > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
     attr[na].val.clusterDim.y = 1;
     attr[na].val.clusterDim.z = static_cast<unsigned>(split);
+    ++na;
+  }
+  // programmatic dependent launch (plan.reserved[0] = 1 turns it off): the
+  // prologue and the weight loads overlap the previous kernel's tail
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
   cfg.attrs = attr;
@@ -807,35 +823,43 @@ static cudaError_t launch_prefill_t(const GemmProblem& p, int split) {
 }
 
 template <int DT, int ODT>
-static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split) {
+static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split, bool pdl) {
   if (p.nrep > 0) {  // EPI 2: plain epilogue, each store also to the replicas
-    return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 2>(p, split)
-                       : launch_prefill_t<DT, ODT, kOrderAwq, 2, 2>(p, split);
+    return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 2>(p, split, pdl)
+                       : launch_prefill_t<DT, ODT, kOrderAwq, 2, 2>(p, split, pdl);
   }
   if constexpr (DT == ODT) {
     if (p.epi == 1) {
-      return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 1>(p, split)
-                         : launch_prefill_t<DT, ODT, kOrderAwq, 2, 1>(p, split);
+      return halves == 1 ? launch_prefill_t<DT, ODT, kOrderAwq, 1, 1>(p, split, pdl)
+                         : launch_prefill_t<DT, ODT, kOrderAwq, 2, 1>(p, split, pdl);
     }
   }
   if (halves == 1) {
-    return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 1>(p, split)
-                                    : launch_prefill_t<DT, ODT, kOrderAwq, 1>(p, split);
+    return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 1>(p, split, pdl)
+                                    : launch_prefill_t<DT, ODT, kOrderAwq, 1>(p, split, pdl);
   }
-  return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 2>(p, split)
-                                  : launch_prefill_t<DT, ODT, kOrderAwq, 2>(p, split);
+  return p.order == kOrderNatural ? launch_prefill_t<DT, ODT, kOrderNatural, 2>(p, split, pdl)
+                                  : launch_prefill_t<DT, ODT, kOrderAwq, 2>(p, split, pdl);
 }
 
-cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo&) {
+cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
   const int halves = pf_halves(plan);
   const int split = plan.split < 1 ? 1 : plan.split;
+  // Programmatic dependent launch for grids of one wave, whose ~14-26 us of
+  // fixed cost per tile it partly hides (Qwen2-7B layer: M = 64 105 -> 98 us,
+  // M = 256 164 -> 156 us); with several waves it hides little and measured
+  // within noise, so those launch plainly.
+  const size_t ctas = ((p.n + kPfBN - 1) / kPfBN) *
+                      ((p.rows + 128 * (size_t)halves - 1) / (128 * (size_t)halves)) * split;
+  const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
+  const bool pdl = plan.reserved[0] == 0 && ctas <= sms;
   if (p.dtype == kF16) {
-    return p.out_dtype == kF32 ? launch_prefill_o<kF16, kF32>(p, halves, split)
-                               : launch_prefill_o<kF16, kF16>(p, halves, split);
+    return p.out_dtype == kF32 ? launch_prefill_o<kF16, kF32>(p, halves, split, pdl)
+                               : launch_prefill_o<kF16, kF16>(p, halves, split, pdl);
   }
   if (p.dtype == kBF16) {
-    return p.out_dtype == kF32 ? launch_prefill_o<kBF16, kF32>(p, halves, split)
-                               : launch_prefill_o<kBF16, kBF16>(p, halves, split);
+    return p.out_dtype == kF32 ? launch_prefill_o<kBF16, kF32>(p, halves, split, pdl)
+                               : launch_prefill_o<kBF16, kBF16>(p, halves, split, pdl);
   }
   return cudaErrorNotSupported;
 }

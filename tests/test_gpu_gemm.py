@@ -171,6 +171,35 @@ def test_decode_chain_with_and_without_programmatic_launch(cuda_device, pdl, row
     assert max_rel_err(y2.float().cpu().numpy(), ref2) <= GEMM_TOL["f16"]
 
 
+@pytest.mark.parametrize("pdl", [True, False])
+@pytest.mark.parametrize("rows,halves,split", [(64, 1, 4), (200, 2, 1), (300, 1, 2)])
+def test_prefill_chain_with_and_without_programmatic_launch(cuda_device, pdl, rows, halves,
+                                                             split):
+    # Three dependent prefill GEMMs back to back, each reading the previous
+    # output as X and writing a buffer the one before it read: the kernel's
+    # X loads must wait for the previous grid, and so must its stores.
+    k, g = 1024, 128
+    x, qw, qz, s, _ = random_awq(k, k, g, "f16", rows, seed=31)
+    _, qw2, qz2, s2, _ = random_awq(k, k, g, "f16", rows, seed=32)
+    plan = {"path": PATH_PREFILL, "warps": halves, "split": split, "pdl": pdl}
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    w1 = (t(qw, "u32"), t(qz, "u32"), t(s, "f16"))
+    w2 = (t(qw2, "u32"), t(qz2, "u32"), t(s2, "f16"))
+    a = t(x, "f16")
+    b = torch.empty_like(a)
+    for _ in range(2):
+        a = t(x, "f16")
+        cawq.gemm(a, *w1, g, out=b, plan=plan)   # b = x W1
+        cawq.gemm(b, *w2, g, out=a, plan=plan)   # a = b W2 (a was read by the first)
+        cawq.gemm(a, *w1, g, out=b, plan=plan)   # b = a W1 (b was read by the second)
+    torch.cuda.synchronize()
+    h1 = oracle.gemm_f64(x, qw, qz, s, g, dtype="f16", deq_round=True).astype(np.float16)
+    h2 = oracle.gemm_f64(h1, qw2, qz2, s2, g, dtype="f16", deq_round=True)
+    assert max_rel_err(a.float().cpu().numpy(), h2) <= 2 * GEMM_TOL["f16"]
+    h3 = oracle.gemm_f64(a.cpu().numpy(), qw, qz, s, g, dtype="f16", deq_round=True)
+    assert max_rel_err(b.float().cpu().numpy(), h3) <= GEMM_TOL["f16"]
+
+
 @pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("rows,k,n,g", [(1, 64, 32, 32), (7, 256, 96, 32), (33, 512, 256, 64),
                                         (130, 256, 4096, 128)])
