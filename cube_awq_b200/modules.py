@@ -18,8 +18,9 @@ import torch
 
 from . import _lib
 from .errors import CubeAwqError, DTypeError, ShapeError
-from .kernel import (PreparedWeights, dequantize_awq, gemm, gemm_prepared, gemm_qkv,
-                     gemm_silu_mul, interleave_gate_up)
+from .errors import check
+from .kernel import (PreparedWeights, cawq_dtype, current_stream_handle, dequantize_awq, gemm,
+                     gemm_prepared, gemm_qkv, gemm_silu_mul, interleave_gate_up)
 
 AWQ_PACK_FACTOR = 8  # awq_gemm.rs:12
 TILE_N_BASE = 32     # awq_gemm.rs:13
@@ -203,11 +204,29 @@ class AWQGateUpSiluMul:
         self.qzeros = cat(gate.qzeros, up.qzeros)
         self.scales = cat(gate.scales, up.scales)
         self.bias = cat(gate.bias, up.bias) if gate.bias is not None else None
+        # the constant part of the C call, for the 2-D fast path of forward
+        self._dev = self.scales.get_device()
+        self._ptrs = (self.qweight.data_ptr(), self.qzeros.data_ptr(), self.scales.data_ptr(),
+                      self.bias.data_ptr() if self.bias is not None else None)
+        self._tail = (self.d_input, 2 * inter, self._group_size, cawq_dtype(self.scales.dtype),
+                      inter)
+        self._call = _lib.lib().cawq_gemm_silu_mul
 
     def group_size(self) -> int:
         return self._group_size
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:
+        if (input.dim() == 2 and input.shape[1] == self.d_input and
+                input.dtype == self.scales.dtype and input.get_device() == self._dev and
+                input.is_contiguous()):
+            # the common call: checks, one allocation, one C call
+            rows = input.shape[0]
+            out = input.new_empty((rows, self.d_output))
+            st = self._call(input.data_ptr(), *self._ptrs, out.data_ptr(), rows, *self._tail,
+                            current_stream_handle(self._dev))
+            if st:
+                check(st)
+            return out
         _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
         k = input.shape[-1]
         _shape_assert(k == self.d_input, "input last dim (K) must match qweight rows")
@@ -256,6 +275,13 @@ class AWQQKVLinear:
         self.qzeros = cat("qzeros")
         self.scales = cat("scales")
         self.bias = cat("bias") if q.bias is not None else None
+        # the constant part of the C call, for the fast path of forward
+        self._dev = self.scales.get_device()
+        self._ptrs = (self.qweight.data_ptr(), self.qzeros.data_ptr(), self.scales.data_ptr(),
+                      self.bias.data_ptr() if self.bias is not None else None)
+        code = cawq_dtype(self.scales.dtype) if self._dev >= 0 else 0
+        self._tail = (self.d_input, self.n_q, self.n_kv, self._group_size, code, code)
+        self._call = _lib.lib().cawq_gemm_qkv
 
     def group_size(self) -> int:
         return self._group_size
@@ -267,6 +293,20 @@ class AWQQKVLinear:
         x = input.reshape(-1, k)
         if not x.is_contiguous():
             x = x.contiguous()
+        if (out is None and x.dtype == self.scales.dtype and x.get_device() == self._dev and
+                self._dev >= 0):
+            # the common call: checks, three allocations, one C call
+            rows = x.shape[0]
+            q, kk, v = (x.new_empty((rows, self.n_q)), x.new_empty((rows, self.n_kv)),
+                        x.new_empty((rows, self.n_kv)))
+            st = self._call(x.data_ptr(), *self._ptrs, q.data_ptr(), kk.data_ptr(), v.data_ptr(),
+                            rows, *self._tail, self.n_q, self.n_kv, self.n_kv,
+                            current_stream_handle(self._dev))
+            if st:
+                check(st)
+            lead = input.shape[:-1]
+            return (q.reshape(*lead, self.n_q), kk.reshape(*lead, self.n_kv),
+                    v.reshape(*lead, self.n_kv))
         q, kk, v = gemm_qkv(x, self.qweight, self.qzeros, self.scales, self._group_size,
                             self.n_q, self.n_kv, bias=self.bias, out=out)
         if out is not None:
