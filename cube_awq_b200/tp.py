@@ -38,7 +38,7 @@ import torch.distributed as dist
 
 from . import _lib
 from .errors import check
-from .kernel import cawq_dtype, gemm as fused_gemm
+from .kernel import cawq_dtype, current_stream_handle, gemm as fused_gemm
 
 
 # ------------------------------------------------------------ shard math
@@ -171,12 +171,12 @@ class TPPeers:
 GemmFn = Callable[..., torch.Tensor]
 
 
-def _stream_ptr(t: torch.Tensor):
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+def _stream_ptr(t: torch.Tensor) -> int:
+    return current_stream_handle(t.get_device())
 
 
-def _ptr(t: Optional[torch.Tensor]):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return t.data_ptr() if t is not None else None
 
 
 # ------------------------------------------------------------- layers
