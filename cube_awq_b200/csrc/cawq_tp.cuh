@@ -261,7 +261,9 @@ static __device__ __align__(256) float g_rowpar_scratch[CAWQ_ROWPAR_SCRATCH_FLOA
 cudaError_t rowpar_static_scratch(float** ptr) {
   // Set-up on the first call per device: cudaGetSymbolAddress with that
   // device current (the caller's current device, the communicator's), its
-  // status checked, the address kept for every later call on that device.
+  // status checked, the address kept for every later call on that device
+  // for the life of the process (a device reset, which would move the
+  // array, is not supported with this entry point).
   constexpr int kMaxDevices = 64;
   static std::mutex mu;
   static float* cached[kMaxDevices] = {};

@@ -204,18 +204,32 @@ class AWQGateUpSiluMul:
         self.qzeros = cat(gate.qzeros, up.qzeros)
         self.scales = cat(gate.scales, up.scales)
         self.bias = cat(gate.bias, up.bias) if gate.bias is not None else None
-        # the constant part of the C call, for the 2-D fast path of forward
+        self._inter = inter
+        self._call = _lib.lib().cawq_gemm_silu_mul
+        self._prepare()
+
+    def _prepare(self) -> None:
+        """The constant part of the C call for the 2-D fast path of forward,
+        made from the tensors held now; forward re-makes it when one of them
+        has been replaced (identity check), so it never reads freed memory."""
+        self._held = (self.qweight, self.qzeros, self.scales, self.bias)
         self._dev = self.scales.get_device()
         self._ptrs = (self.qweight.data_ptr(), self.qzeros.data_ptr(), self.scales.data_ptr(),
                       self.bias.data_ptr() if self.bias is not None else None)
-        self._tail = (self.d_input, 2 * inter, self._group_size, cawq_dtype(self.scales.dtype),
-                      inter)
-        self._call = _lib.lib().cawq_gemm_silu_mul
+        self._tail = (self.d_input, 2 * self._inter, self._group_size,
+                      cawq_dtype(self.scales.dtype), self._inter)
+
+    def _current(self) -> bool:
+        h = self._held
+        return (self.qweight is h[0] and self.qzeros is h[1] and self.scales is h[2] and
+                self.bias is h[3])
 
     def group_size(self) -> int:
         return self._group_size
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:
+        if not self._current():
+            self._prepare()
         if (input.dim() == 2 and input.shape[1] == self.d_input and
                 input.dtype == self.scales.dtype and input.get_device() == self._dev and
                 input.is_contiguous()):
@@ -275,18 +289,31 @@ class AWQQKVLinear:
         self.qzeros = cat("qzeros")
         self.scales = cat("scales")
         self.bias = cat("bias") if q.bias is not None else None
-        # the constant part of the C call, for the fast path of forward
+        self._call = _lib.lib().cawq_gemm_qkv
+        self._prepare()
+
+    def _prepare(self) -> None:
+        """The constant part of the C call for the fast path of forward, made
+        from the tensors held now; forward re-makes it when one of them has
+        been replaced (identity check), so it never reads freed memory."""
+        self._held = (self.qweight, self.qzeros, self.scales, self.bias)
         self._dev = self.scales.get_device()
         self._ptrs = (self.qweight.data_ptr(), self.qzeros.data_ptr(), self.scales.data_ptr(),
                       self.bias.data_ptr() if self.bias is not None else None)
         code = cawq_dtype(self.scales.dtype) if self._dev >= 0 else 0
         self._tail = (self.d_input, self.n_q, self.n_kv, self._group_size, code, code)
-        self._call = _lib.lib().cawq_gemm_qkv
+
+    def _current(self) -> bool:
+        h = self._held
+        return (self.qweight is h[0] and self.qzeros is h[1] and self.scales is h[2] and
+                self.bias is h[3])
 
     def group_size(self) -> int:
         return self._group_size
 
     def forward(self, input: torch.Tensor, out: Optional[tuple] = None) -> tuple:
+        if not self._current():
+            self._prepare()
         _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
         k = input.shape[-1]
         _shape_assert(k == self.d_input, "input last dim (K) must match qweight rows")

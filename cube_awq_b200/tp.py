@@ -37,7 +37,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .errors import check
+from .errors import CubeAwqError, DTypeError, ShapeError, check
 from .kernel import cawq_dtype, current_stream_handle, gemm as fused_gemm
 
 
@@ -179,6 +179,21 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return t.data_ptr() if t is not None else None
 
 
+def _check_native_input(x2: torch.Tensor, scales: torch.Tensor, k: int) -> None:
+    """The C calls take raw pointers: before one, the input must be a device
+    tensor on the weights' GPU, in the scales' dtype (the kernels read x and
+    scales with one element size) and with the shard's K columns."""
+    if x2.dtype != scales.dtype:
+        raise DTypeError(f"input dtype {x2.dtype} must equal the scales dtype {scales.dtype}",
+                         _lib.CAWQ_ERR_DTYPE)
+    if x2.shape[-1] != k:
+        raise ShapeError(f"input last dim ({x2.shape[-1]}) must be {k}",
+                         _lib.CAWQ_ERR_INVALID_SHAPE)
+    if not x2.is_cuda or not scales.is_cuda or x2.get_device() != scales.get_device():
+        raise CubeAwqError(f"the input must be on the weights' GPU ({scales.device}), "
+                           f"got {x2.device}", _lib.CAWQ_ERR_INVALID_ARGUMENT)
+
+
 # ------------------------------------------------------------- layers
 class ColumnParallelAWQLinear:
     """Column-parallel AWQGEMMLinear: this rank's N/P output columns.
@@ -219,6 +234,8 @@ class ColumnParallelAWQLinear:
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         m = x2.shape[0]
+        if self.backend in ("p2p", "native") and self.gather_output:
+            _check_native_input(x2, self.scales, self.k)
         if self.backend == "p2p" and self.gather_output:
             out = torch.empty(m, self.n, dtype=x2.dtype, device=x2.device)
             check(_lib.lib().cawq_gemm_colpar_p2p(
@@ -294,6 +311,8 @@ class RowParallelAWQLinear:
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         m = x2.shape[0]
+        if self.backend in ("p2p", "native"):
+            _check_native_input(x2, self.scales, self.kl)
         if self.backend == "p2p":
             out = torch.empty(m, self.n, dtype=x2.dtype, device=x2.device)
             check(_lib.lib().cawq_gemm_rowpar_p2p(

@@ -430,8 +430,10 @@ cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint
  *   - rows * n above CAWQ_ROWPAR_SCRATCH_FLOATS is refused with
  *     CAWQ_ERR_INVALID_SHAPE (use cawq_gemm_rowpar with a workspace instead);
  *   - the first call on a device looks the array's device address up once
- *     (cudaGetSymbolAddress, on the current device) and keeps it; make that
- *     first call before any stream capture;
+ *     (cudaGetSymbolAddress, on the current device) and keeps it for the
+ *     life of the process; make that first call before any stream capture.
+ *     Resetting the device (cudaDeviceReset) while the library is loaded is
+ *     not supported with this entry point: the kept address would be stale;
  *   - this library allocates nothing in the call, on the device or through
  *     any allocating library routine; NCCL's own connection buffers are
  *     NCCL's, and with its default lazy connection a communicator may set
@@ -470,7 +472,11 @@ cawq_status cawq_gemm_rowpar_noalloc(const cawq_tp_comm* comm, const void* x,
  * ((bytes - CAWQ_TP_P2P_HEADER) / 2) rounded down to 256 bytes; a call uses
  * slot (epoch & 1), so the slot a peer writes is never the one this rank is
  * still reading. That holds when each rank's fused calls on one table run in
- * order on the GPU (one stream, or streams the caller orders).
+ * order on the GPU (one stream, or streams the caller orders), and only while
+ * every wait has succeeded: once a finish kernel's wait has timed out (bit 1
+ * of cawq_device_error's word), a peer may already be writing the slot of a
+ * later epoch that this rank still reads, so the table is unusable. Every
+ * rank then destroys it and the ranks create a new one.
  */
 #define CAWQ_TP_MAX_PEERS 8
 #define CAWQ_TP_P2P_HEADER 256
