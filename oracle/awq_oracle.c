@@ -162,43 +162,85 @@ void awqo_dequant(const uint32_t* qw, const uint32_t* qz, const void* sc,
 
 /* -------------------------------------------------------------------- GEMM */
 
-/* Reference numerics, f32: float operations, contraction disabled. */
+/* Reference numerics, f32: float operations, contraction disabled. Per
+ * output: w = (q - z) * s rounded once, acc = acc + x * w (product and sum
+ * each rounded), k ascending from acc = 0 -- the reference's F = f32 path.
+ * Laid out for the host's vector units: one task owns 128 columns (16 packed
+ * words) of one row; the 8 columns of a word are one 8-lane vector, unpacked
+ * with the nibble order's shift table. Lanes are independent outputs, so the
+ * operations and their order per output are those of a plain scalar loop. */
+static const int kShiftAwq[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+static const int kShiftNat[8] = {0, 4, 8, 12, 16, 20, 24, 28};
+
+typedef uint32_t v8u __attribute__((vector_size(32)));
+typedef float v8f __attribute__((vector_size(32)));
+
+static inline void f32_block(const float* x, const uint32_t* qw,
+                             const uint32_t* qz, const float* sc,
+                             const float* bias, float* out, size_t m, size_t K,
+                             size_t N, size_t g, size_t j0, size_t nw,
+                             const int* sh) {
+  const size_t npk = N / 8;
+  const v8u shv = {(uint32_t)sh[0], (uint32_t)sh[1], (uint32_t)sh[2], (uint32_t)sh[3],
+                   (uint32_t)sh[4], (uint32_t)sh[5], (uint32_t)sh[6], (uint32_t)sh[7]};
+  const v8u mask = {15u, 15u, 15u, 15u, 15u, 15u, 15u, 15u};
+  v8f acc[16];
+  for (size_t j = 0; j < 16; ++j) acc[j] = (v8f){0, 0, 0, 0, 0, 0, 0, 0};
+  for (size_t k0 = 0; k0 < K; k0 += g) {
+    const size_t grp = k0 / g;
+    const size_t k1 = k0 + g < K ? k0 + g : K;
+    v8f zf[16], sf[16];
+    for (size_t j = 0; j < nw; ++j) {
+      const uint32_t b = qz[grp * npk + j0 + j];
+      const v8u bz = {b, b, b, b, b, b, b, b};
+      zf[j] = __builtin_convertvector((bz >> shv) & mask, v8f);
+      memcpy(&sf[j], sc + grp * N + 8 * (j0 + j), sizeof(v8f));
+    }
+    for (size_t k = k0; k < k1; ++k) {
+      const float xs = x[m * K + k];
+      const v8f xv = {xs, xs, xs, xs, xs, xs, xs, xs};
+      const uint32_t* wq = qw + k * npk + j0;
+      for (size_t j = 0; j < nw; ++j) {
+        const uint32_t a = wq[j];
+        const v8u av = {a, a, a, a, a, a, a, a};
+        const v8f q = __builtin_convertvector((av >> shv) & mask, v8f);
+        const v8f w = (q - zf[j]) * sf[j];   /* (q - z) exact, one rounding of * s */
+        acc[j] = acc[j] + xv * w;            /* product and sum rounded separately */
+      }
+    }
+  }
+  for (size_t j = 0; j < nw; ++j) {
+    float v[8];
+    memcpy(v, &acc[j], sizeof(v));
+    for (int c = 0; c < 8; ++c) {
+      float r = v[c];
+      if (bias) r = r + bias[8 * (j0 + j) + (size_t)c];
+      out[m * N + 8 * (j0 + j) + (size_t)c] = r;
+    }
+  }
+}
+
 static void gemm_ref_f32(const float* x, const uint32_t* qw, const uint32_t* qz,
                          const float* sc, const float* bias, float* out,
                          size_t M, size_t K, size_t N, size_t g, int order,
                          int nthreads) {
-  size_t npk = N / 8;
-  const size_t NB = 256; /* column block per task */
-  long long nblocks = (long long)((N + NB - 1) / NB);
+  const size_t npk = N / 8;
+  const size_t WB = 16; /* packed words (128 columns) per task */
+  const long long nblocks = (long long)((npk + WB - 1) / WB);
+  const int* sh = order == 0 ? kShiftAwq : kShiftNat;
   long long task;
-  (void)nthreads;
 #pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads > 0 ? nthreads : awqo_max_threads())
   for (task = 0; task < nblocks * (long long)M; ++task) {
-    size_t m = (size_t)(task / nblocks);
-    size_t n0 = (size_t)(task % nblocks) * NB;
-    size_t n1 = n0 + NB < N ? n0 + NB : N;
-    float acc[256];
-    float w[256];
-    for (size_t n = n0; n < n1; ++n) acc[n - n0] = 0.0f;
-    for (size_t k = 0; k < K; ++k) {
-      size_t grp = k / g;
-      float xv = x[m * K + k];
-      for (size_t n = n0; n < n1; ++n) {
-        float q = (float)awqo_nibble(qw[k * npk + n / 8], (int)(n % 8), order);
-        float z = (float)awqo_nibble(qz[grp * npk + n / 8], (int)(n % 8), order);
-        w[n - n0] = (q - z) * sc[grp * N + n];
-      }
-      for (size_t n = n0; n < n1; ++n) {
-        float prod = xv * w[n - n0];
-        acc[n - n0] = acc[n - n0] + prod;
-      }
-    }
-    for (size_t n = n0; n < n1; ++n) {
-      float v = acc[n - n0];
-      if (bias) v = v + bias[n];
-      out[m * N + n] = v;
+    const size_t m = (size_t)(task / nblocks);
+    const size_t j0 = (size_t)(task % nblocks) * WB;
+    const size_t nw = j0 + WB < npk ? WB : npk - j0;
+    if (order == 0) {
+      f32_block(x, qw, qz, sc, bias, out, m, K, N, g, j0, nw, kShiftAwq);
+    } else {
+      f32_block(x, qw, qz, sc, bias, out, m, K, N, g, j0, nw, kShiftNat);
     }
   }
+  (void)sh;
 }
 
 /* Reference numerics in a 16-bit F: each operation computed exactly in
