@@ -90,3 +90,22 @@ def test_dequant_cfg5_full_size_sampled_rows(cuda_device):
         got = out[rows].cpu().numpy()
         assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
     assert cawq.device_error() == 0
+
+
+@pytest.mark.parametrize("offset_floats", [4, 8])
+def test_dequant_f32_output_16_byte_aligned(cuda_device, offset_floats):
+    # offset 4: 16-byte aligned only (two 128-bit stores per word); offset 8:
+    # 32-byte aligned (one 256-bit store per word)
+    k, n, g = 200, 256, 40
+    rng = np.random.default_rng(6 + offset_floats)
+    qw = rng.integers(0, 2**32, (k, n // 8), dtype=np.uint64).astype(np.uint32)
+    qz = rng.integers(0, 2**32, (k // g, n // 8), dtype=np.uint64).astype(np.uint32)
+    s = rng.uniform(0.001, 0.02, (k // g, n)).astype(np.float32)
+    buf = torch.full((k * n + offset_floats,), float("nan"), dtype=torch.float32,
+                     device=cuda_device)
+    out = buf[offset_floats:].view(k, n)
+    cawq.dequantize_native(to_torch(qw, "u32", cuda_device), to_torch(qz, "u32", cuda_device),
+                           to_torch(s, "f32", cuda_device), out, g)
+    exp = oracle.dequant(qw, qz, s, g, "f32", "natural")
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), exp.view(np.uint32))
+    assert torch.isnan(buf[:offset_floats]).all()
