@@ -85,6 +85,11 @@ void decode_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* o
 cawq_plan decode_default_plan(const GemmProblem& p, const DeviceInfo& dev);
 
 bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+// f32 activations and scales on the tensor cores (cawq_prefill_f32.cuh);
+// prefill_supports / launch_prefill hand f32 problems to these
+bool prefill_f32_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+cudaError_t launch_prefill_f32(const GemmProblem& p, const cawq_plan& plan,
+                               const DeviceInfo& dev);
 cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
 void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
                         int max_count);

@@ -740,6 +740,9 @@ static size_t pf_smem(int halves) {
 }
 
 bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
+  if (p.dtype == kF32) {  // 128 x 128 tiles of the f32 kernel, no split
+    return (plan.warps == 0 || plan.warps == 1) && prefill_f32_supports(p, plan, dev);
+  }
   const int halves = pf_halves(plan);
   if (plan.warps != 0 && plan.warps != 1 && plan.warps != 2) return false;
   const int split = plan.split < 1 ? 1 : plan.split;
@@ -843,6 +846,7 @@ static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split,
 }
 
 cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
+  if (p.dtype == kF32) return launch_prefill_f32(p, plan, dev);
   const int halves = pf_halves(plan);
   const int split = plan.split < 1 ? 1 : plan.split;
   // Programmatic dependent launch for grids of one wave, whose ~14-26 us of
@@ -911,6 +915,11 @@ cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   pl.tile_n = kPfBN;
   pl.stages = kPfBStages;
   pl.warps = p.rows <= 128 ? 1 : 2;
+  if (p.dtype == kF32) {  // the f32 kernel: 128 x 128 tiles, no split
+    pl.warps = 1;
+    pl.split = 1;
+    return pl;
+  }
   const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
   const size_t kt = p.k / kPfBK;
   auto split_for = [&](int warps) {

@@ -1,0 +1,497 @@
+// cawq_prefill_f32.cuh — large-M fused AWQ GEMM with f32 activations and
+// scales on tcgen05 tensor cores (sm_100a).
+//
+// Y[M, N] = X[M, K] · ((Q - Z) · S)[K, N], F = f32: the reference's gemm_awq
+// with F = f32 (src/kernel/awq_kernel_gemm.rs:181-439), the precision its own
+// tests use. The tensor cores take 16-bit operands, so the f32 arithmetic is
+// arranged so that nothing is lost where it matters:
+//
+//   * B = (q - z), a small integer, is exact in bf16: the weights enter the
+//     MMA without rounding and the scale is not applied there;
+//   * X = hi + lo with hi = x truncated to bf16 and lo = bf16(x - hi), so
+//     |x - hi - lo| <= 2^-16 |x|; two MMAs (hi·B + lo·B) per k step;
+//   * each quantization group accumulates in its own fp32 TMEM buffer (two,
+//     used in turn), and the epilogue warps add s[g, n] · D_g into a running
+//     fp32 sum kept in TMEM while the tensor core fills the other buffer:
+//     Y = sum_g s_g · (sum_{k in g} x (q - z)).
+//
+// The result differs from the reference's sequential f32 sum by rounding
+// only: every product is exact but for the 2^-16 split of x, and the sums are
+// fp32 (the parity tests bound it against the exact fp64 oracle at the north
+// star's 1e-3 · ||ref||_inf).
+//
+// CTA tile 128 x 128, 64-row k stages; 19 warps:
+//   warp 0      TMA producer of the f32 X ring (two 32-column boxes a stage);
+//   warp 1      allocates 512 TMEM columns (D0, D1, running sum) and issues
+//               tcgen05.mma.cta_group::1.kind::f16 (bf16, M=128, N=128, K=16);
+//   warp 2      TMA producer of the packed weights + zero row (W ring) and,
+//               at each group's first stage, of the group's scale row;
+//   warps 3-6   split each X stage into the hi / lo bf16 A tiles (K-major,
+//               128-byte swizzle);
+//   warps 7-10  turn the packed stage into the exact (q - z) bf16 B tile
+//               (MN-major, 128-byte swizzle);
+//   warps 11-18 per group: running += s · D_g (tcgen05.ld / st), two per
+//               TMEM lane quarter, 64 columns each; after the last group,
+//               add the bias and store the rows.
+#pragma once
+
+#include "cawq_common.cuh"
+#include "cawq_prefill.cuh"
+
+namespace cawq {
+
+constexpr int kP32BM = 128;
+constexpr int kP32BN = 128;
+constexpr int kP32BK = 64;
+constexpr int kP32Threads = 19 * 32;
+
+struct P32Layout {
+  static constexpr int kXSt = 2, kASt = 2, kWSt = 4, kBSt = 2;
+  static constexpr int kX = kP32BM * kP32BK * 4;      // 32768: f32 X, two 128-B boxes
+  static constexpr int kA = kP32BM * kP32BK * 2;      // 16384: one bf16 A tile (hi or lo)
+  static constexpr int kB = kP32BK * kP32BN * 2;      // 16384: bf16 B tile
+  static constexpr int kW = kP32BK * kP32BN / 8 * 4;  // 4096: packed words, 64-B rows
+  static constexpr int kZ = kP32BN / 8 * 4;           // 64: the stage's zero row
+  static constexpr int kWSlot = 4352;                 // kW + kZ, rounded up
+  static constexpr int kS = kP32BN * 4;               // 512: a group's scale row
+  static constexpr size_t kOffA = (size_t)kX * kXSt;
+  static constexpr size_t kOffB = kOffA + (size_t)2 * kA * kASt;
+  static constexpr size_t kOffW = kOffB + (size_t)kB * kBSt;
+  static constexpr size_t kOffS = kOffW + (size_t)kWSlot * kWSt;
+  static constexpr size_t kOffBars = kOffS + (size_t)kS * 2;
+  static constexpr size_t kSmem = 1024 + kOffBars + 512;
+};
+
+// 32 lanes x 32 fp32 columns -> registers, without the wait (the caller
+// issues tcgen05.wait::ld before using them).
+__device__ __forceinline__ void tmem_ld_32x32b_x32_nowait(uint32_t taddr, float (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+        "=f"(v[7]), "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]),
+        "=f"(v[14]), "=f"(v[15]), "=f"(v[16]), "=f"(v[17]), "=f"(v[18]), "=f"(v[19]),
+        "=f"(v[20]), "=f"(v[21]), "=f"(v[22]), "=f"(v[23]), "=f"(v[24]), "=f"(v[25]),
+        "=f"(v[26]), "=f"(v[27]), "=f"(v[28]), "=f"(v[29]), "=f"(v[30]), "=f"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+      "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]),
+      "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]),
+      "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]),
+      "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// x (f32 pair) -> (hi, lo) bf16 pairs: hi = x with its low 16 bits cleared
+// (exact), lo = x - hi (exact in f32) rounded to bf16.
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const uint32_t u0 = __float_as_uint(x0), u1 = __float_as_uint(x1);
+  hi = prmt(u0, u1, 0x7632u);
+  const float r0 = x0 - __uint_as_float(u0 & 0xFFFF0000u);
+  const float r1 = x1 - __uint_as_float(u1 & 0xFFFF0000u);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int ORDER>
+__global__ void __launch_bounds__(kP32Threads, 1)
+    prefill_f32_kernel(const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_s,
+                       const __grid_constant__ CUtensorMap tm_z, const float* __restrict__ bias,
+                       const OutMap<float> om, uint32_t rows, uint32_t k, uint32_t n, uint32_t g) {
+  using L = P32Layout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
+  uint64_t* xempty = xfull + L::kXSt;
+  uint64_t* afull = xempty + L::kXSt;
+  uint64_t* aempty = afull + L::kASt;
+  uint64_t* wfull = aempty + L::kASt;
+  uint64_t* wempty = wfull + L::kWSt;
+  uint64_t* bfull = wempty + L::kWSt;
+  uint64_t* bempty = bfull + L::kBSt;
+  uint64_t* dfull = bempty + L::kBSt;  // [2] a group's sum is in D[b]
+  uint64_t* dempty = dfull + 2;        // [2] the epilogue has read D[b]
+  uint64_t* sfull = dempty + 2;        // [2] the group's scale row landed
+  uint64_t* sempty = sfull + 2;        // [2] the epilogue is done with it
+  uint64_t* drain_bar = sempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  __shared__ int s_x_issued, s_w_issued;
+  bool role_ok = true;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t n0 = blockIdx.x * kP32BN;
+  const uint32_t m0 = blockIdx.y * kP32BM;
+  const int KT = static_cast<int>(k / kP32BK);
+  const int spg = static_cast<int>(g / kP32BK);  // stages per group (g % 64 == 0)
+  const int NG = KT / spg;
+
+  auto x_slot = [&](int s) { return smem + (size_t)s * L::kX; };
+  auto a_slot = [&](int s) { return smem + L::kOffA + (size_t)s * 2 * L::kA; };
+  auto b_slot = [&](int s) { return smem + L::kOffB + (size_t)s * L::kB; };
+  auto w_slot = [&](int s) { return smem + L::kOffW + (size_t)s * L::kWSlot; };
+  auto s_slot = [&](int b) { return reinterpret_cast<const float*>(smem + L::kOffS + (size_t)b * L::kS); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::kXSt; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 128);
+    }
+    for (int s = 0; s < L::kASt; ++s) {
+      mbar_init(&afull[s], 128);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < L::kWSt; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 128);
+    }
+    for (int s = 0; s < L::kBSt; ++s) {
+      mbar_init(&bfull[s], 128);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dfull[b], 1);
+      mbar_init(&dempty[b], 256);
+      mbar_init(&sfull[b], 1);
+      mbar_init(&sempty[b], 256);
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------- X ring producer
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      pdl_wait();  // X may be the previous kernel's output
+      for (int i = 0; i < KT && ok; ++i) {
+        const int s = i % L::kXSt, u = i / L::kXSt;
+        if (u > 0) ok = mbar_wait_bounded(&xempty[s], (uint32_t)((u - 1) & 1));
+        if (!ok) break;
+        mbar_arrive_expect_tx(&xfull[s], L::kX);
+        tma_load_2d(x_slot(s), &tm_x, i * kP32BK, static_cast<int>(m0), &xfull[s]);
+        tma_load_2d(x_slot(s) + L::kX / 2, &tm_x, i * kP32BK + 32, static_cast<int>(m0),
+                    &xfull[s]);
+        issued = i + 1;
+      }
+      s_x_issued = issued;
+      role_ok = ok;
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ---------------------------------- W ring + group scale producer
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int i = 0; i < KT && ok; ++i) {
+        const int s = i % L::kWSt, u = i / L::kWSt;
+        const int grp = i / spg;
+        if (i % spg == 0) {
+          const int b = grp & 1;
+          if (grp >= 2) ok = mbar_wait_bounded(&sempty[b], (uint32_t)(((grp >> 1) - 1) & 1));
+          if (!ok) break;
+          mbar_arrive_expect_tx(&sfull[b], L::kS);
+          tma_load_2d(smem + L::kOffS + (size_t)b * L::kS, &tm_s, static_cast<int>(n0), grp,
+                      &sfull[b]);
+        }
+        if (u > 0) ok = mbar_wait_bounded(&wempty[s], (uint32_t)((u - 1) & 1));
+        if (!ok) break;
+        mbar_arrive_expect_tx(&wfull[s], L::kW + L::kZ);
+        tma_load_2d(w_slot(s), &tm_w, static_cast<int>(n0 / 8), i * kP32BK, &wfull[s]);
+        tma_load_2d(w_slot(s) + L::kW, &tm_z, static_cast<int>(n0 / 8), grp, &wfull[s]);
+        issued = i + 1;
+      }
+      s_w_issued = issued;
+      role_ok = ok;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(true, kP32BM, kP32BN);
+      bool ok = true;
+      for (int kt = 0; kt < KT && ok; ++kt) {
+        const int grp = kt / spg, b = grp & 1;
+        const bool first = kt % spg == 0, last = kt % spg == spg - 1;
+        if (first && grp >= 2) ok = mbar_wait_bounded(&dempty[b], (uint32_t)(((grp >> 1) - 1) & 1));
+        const int sa = kt % L::kASt, ua = kt / L::kASt;
+        const int sb = kt % L::kBSt, ub = kt / L::kBSt;
+        ok = ok && mbar_wait_bounded(&afull[sa], (uint32_t)(ua & 1)) &&
+             mbar_wait_bounded(&bfull[sb], (uint32_t)(ub & 1));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t ahi = smem_u32(a_slot(sa)), alo = ahi + L::kA;
+        const uint32_t ba = smem_u32(b_slot(sb));
+        const uint32_t d = tmem + (uint32_t)b * kP32BN;
+#pragma unroll
+        for (int j = 0; j < kP32BK / 16; ++j) {
+          const uint64_t bd = umma_desc_sw128(ba + 2048 * j, 8192, 1024);
+          umma_f16(d, umma_desc_sw128(ahi + 32 * j, 16, 1024), bd, idesc,
+                   (first && j == 0) ? 0u : 1u);
+          umma_f16(d, umma_desc_sw128(alo + 32 * j, 16, 1024), bd, idesc, 1u);
+        }
+        umma_commit(&aempty[sa]);
+        umma_commit(&bempty[sb]);
+        if (last) umma_commit(&dfull[b]);
+      }
+      if (!ok) {
+        umma_commit(drain_bar);  // wait (bounded) for the MMAs already issued
+        mbar_wait_bounded(drain_bar, 0u);
+      }
+      role_ok = ok;
+    }
+    __syncwarp();
+  } else if (warp >= 3 && warp <= 6) {
+    // ------------------------------------------ X split into hi / lo
+    const int t = threadIdx.x - 96;  // 0..127
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int sx = kt % L::kXSt, ux = kt / L::kXSt;
+      const int sa = kt % L::kASt, ua = kt / L::kASt;
+      if (ok) ok = mbar_wait_bounded(&xfull[sx], (uint32_t)(ux & 1));
+      if (ok && ua > 0) ok = mbar_wait_bounded(&aempty[sa], (uint32_t)((ua - 1) & 1));
+      if (ok) {
+        const uint8_t* xs = x_slot(sx);
+        uint8_t* ah = a_slot(sa);
+        uint8_t* al = ah + L::kA;
+        // 128 rows x 8 chunks of 8 k; item i: row i >> 3, chunk i & 7
+#pragma unroll 2
+        for (int it = 0; it < 8; ++it) {
+          const int i = t + 128 * it;
+          const int r = i >> 3, c8 = i & 7, r7 = r & 7;
+          // f32 source: box c8 >> 2 (k 0-31 / 32-63), 16-byte chunks 2 (c8 & 3)
+          // and + 1 of row r, 128-byte swizzled
+          const uint8_t* srow = xs + (c8 >> 2) * (L::kX / 2) + r * 128;
+          const int cc = (c8 & 3) * 2;
+          const float4 a = *reinterpret_cast<const float4*>(srow + ((cc ^ r7) << 4));
+          const float4 b = *reinterpret_cast<const float4*>(srow + (((cc + 1) ^ r7) << 4));
+          uint4 hi, lo;
+          split_bf16x2(a.x, a.y, hi.x, lo.x);
+          split_bf16x2(a.z, a.w, hi.y, lo.y);
+          split_bf16x2(b.x, b.y, hi.z, lo.z);
+          split_bf16x2(b.z, b.w, hi.w, lo.w);
+          const int off = r * 128 + ((c8 ^ r7) << 4);
+          *reinterpret_cast<uint4*>(ah + off) = hi;
+          *reinterpret_cast<uint4*>(al + off) = lo;
+        }
+      }
+      mbar_arrive(&xempty[sx]);  // after the reads above
+      fence_proxy_async_smem();
+      mbar_arrive(&afull[sa]);
+    }
+    role_ok = ok;
+  } else if (warp >= 7 && warp <= 10) {
+    // ------------------------------------------- dequantize: B = q - z
+    const int t = threadIdx.x - 224;  // 0..127
+    const int w = t & 15;             // packed word of the row (8 columns)
+    const int r0 = t >> 4;            // rows r0 + 8 i
+    const int a = w >> 3, l = w & 7;  // 64-column block, 16-byte chunk in it
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int sw = kt % L::kWSt, uw = kt / L::kWSt;
+      const int sb = kt % L::kBSt, ub = kt / L::kBSt;
+      if (ok) ok = mbar_wait_bounded(&wfull[sw], (uint32_t)(uw & 1));
+      if (ok && ub > 0) ok = mbar_wait_bounded(&bempty[sb], (uint32_t)((ub - 1) & 1));
+      if (ok) {
+        const uint8_t* ws = w_slot(sw);
+        uint8_t* bs = b_slot(sb);
+        uint32_t zp[4];
+        pf_pairs<kBF16, ORDER>(reinterpret_cast<const uint32_t*>(ws + L::kW)[w], zp);
+        uint32_t qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          qv[i] = reinterpret_cast<const uint32_t*>(ws)[(r0 + 8 * i) * 16 + w];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + 8 * i, r7 = r & 7;
+          uint32_t tq[4];
+          pf_pairs<kBF16, ORDER>(qv[i], tq);
+          uint4 v;  // (128 + q) - (128 + z) = q - z, exact
+          v.x = PfHalf2<kBF16>::sub(tq[0], zp[0]);
+          v.y = PfHalf2<kBF16>::sub(tq[1], zp[1]);
+          v.z = PfHalf2<kBF16>::sub(tq[2], zp[2]);
+          v.w = PfHalf2<kBF16>::sub(tq[3], zp[3]);
+          *reinterpret_cast<uint4*>(bs + a * 8192 + (r >> 3) * 1024 + r7 * 128 +
+                                    ((l ^ r7) << 4)) = v;
+        }
+      }
+      mbar_arrive(&wempty[sw]);  // after the values above were consumed
+      fence_proxy_async_smem();
+      mbar_arrive(&bfull[sb]);
+    }
+    role_ok = ok;
+  } else {
+    // ------------------------------------------------ group epilogue
+    const int lq = warp & 3;  // TMEM lane quarter this warp may access
+    const int ch = (warp - 11) >> 2;  // column half (64 columns)
+    const uint32_t row_t = (uint32_t)(32 * lq);
+    const uint32_t run = tmem + 2 * kP32BN + (row_t << 16);
+    bool ok = true;
+    for (int grp = 0; grp < NG; ++grp) {
+      const int b = grp & 1, u = grp >> 1;
+      if (ok) ok = mbar_wait_bounded(&dfull[b], (uint32_t)(u & 1));
+      if (ok) ok = mbar_wait_bounded(&sfull[b], (uint32_t)(u & 1));
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld / st are warp-collective
+      if (ok) {
+        tc_fence_after();
+        const float* sc = s_slot(b);
+        const uint32_t dbuf = tmem + (uint32_t)b * kP32BN + (row_t << 16);
+        const bool last = grp == NG - 1;
+#pragma unroll 1
+        for (int c = 2 * ch; c < 2 * ch + 2; ++c) {
+          float d[32], acc[32];
+          // both loads in flight before the one wait
+          tmem_ld_32x32b_x32_nowait(dbuf + 32 * c, d);
+          if (grp > 0) tmem_ld_32x32b_x32_nowait(run + 32 * c, acc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (grp == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 s4 = *reinterpret_cast<const float4*>(sc + 32 * c + i);
+            acc[i] = fmaf(s4.x, d[i], acc[i]);
+            acc[i + 1] = fmaf(s4.y, d[i + 1], acc[i + 1]);
+            acc[i + 2] = fmaf(s4.z, d[i + 2], acc[i + 2]);
+            acc[i + 3] = fmaf(s4.w, d[i + 3], acc[i + 3]);
+          }
+          if (!last) {
+            tmem_st_32x32b_x32(run + 32 * c, acc);
+          } else {
+            const uint32_t row = m0 + row_t + lane, col0 = n0 + 32 * c;
+            if (row < rows && col0 < n) {
+              if (bias) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] += bias[col0 + i];
+              }
+              float* o = om.at(row, col0);  // a 32-column chunk lies in one output
+              if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  *reinterpret_cast<float4*>(o + i) =
+                      make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] = acc[i];
+              }
+            }
+          }
+        }
+        tc_fence_before();
+      }
+      mbar_arrive(&dempty[b]);
+      mbar_arrive(&sempty[b]);
+    }
+    role_ok = ok;
+  }
+
+  // No copy this CTA issued may still be writing its shared memory when it
+  // exits: after a failed (timed-out) run, wait (bounded) for the last
+  // stage issued into each ring slot.
+  if (__syncthreads_or(role_ok ? 0 : 1) && threadIdx.x == 0) {
+    const int xi = s_x_issued, wi = s_w_issued;
+    for (int j = xi > L::kXSt ? xi - L::kXSt : 0; j < xi; ++j)
+      mbar_wait_bounded(&xfull[j % L::kXSt], (uint32_t)((j / L::kXSt) & 1));
+    for (int j = wi > L::kWSt ? wi - L::kWSt : 0; j < wi; ++j)
+      mbar_wait_bounded(&wfull[j % L::kWSt], (uint32_t)((j / L::kWSt) & 1));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host
+bool prefill_f32_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
+  if (plan.split > 1 || p.epi != 0 || p.nrep > 0) return false;
+  if (p.dtype != kF32 || p.out_dtype != kF32) return false;
+  if (dev.cc_major != 10 || dev.smem_optin < P32Layout::kSmem) return false;
+  if (p.rows == 0 || p.k % kP32BK != 0 || p.g % kP32BK != 0 || p.k % p.g != 0 || p.n % 32 != 0)
+    return false;
+  if (p.k >= (1ull << 31) || p.n >= (1ull << 31) || p.rows >= (1ull << 31) ||
+      p.ld_out >= (1ull << 31))
+    return false;
+  if ((p.rows + kP32BM - 1) / kP32BM > 65535) return false;
+  const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
+  const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
+  return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
+}
+
+template <int ORDER>
+static cudaError_t launch_prefill_f32_t(const GemmProblem& p, bool pdl) {
+  using L = P32Layout;
+  CUtensorMap tx, tw, ts, tz;
+  const uint64_t npk = p.n / 8, groups = p.k / p.g;
+  if (!pf_encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.x, p.k, p.rows, p.k * 4, 32, kP32BM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !pf_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kP32BN / 8, kP32BK,
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !pf_encode(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.sc, p.n, groups, p.n * 4, kP32BN, 1,
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !pf_encode(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qz, npk, groups, npk * 4, kP32BN / 8, 1,
+                 CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    return cudaErrorInvalidValue;
+  }
+  auto kern = prefill_f32_kernel<ORDER>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(L::kSmem));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<uint32_t>((p.n + kP32BN - 1) / kP32BN),
+                     static_cast<uint32_t>((p.rows + kP32BM - 1) / kP32BM), 1);
+  cfg.blockDim = dim3(kP32Threads);
+  cfg.dynamicSmemBytes = L::kSmem;
+  cfg.stream = p.stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, tz, static_cast<const float*>(p.bias),
+                            out_map<float>(p), static_cast<uint32_t>(p.rows),
+                            static_cast<uint32_t>(p.k), static_cast<uint32_t>(p.n),
+                            static_cast<uint32_t>(p.g));
+}
+
+cudaError_t launch_prefill_f32(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
+  const size_t ctas = ((p.n + kP32BN - 1) / kP32BN) * ((p.rows + kP32BM - 1) / kP32BM);
+  const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
+  const bool pdl = plan.reserved[0] == 0 && ctas <= sms;
+  return p.order == kOrderNatural ? launch_prefill_f32_t<kOrderNatural>(p, pdl)
+                                  : launch_prefill_f32_t<kOrderAwq>(p, pdl);
+}
+
+}  // namespace cawq

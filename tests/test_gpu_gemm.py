@@ -124,6 +124,30 @@ def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype, mma):
     assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
 
 
+@pytest.mark.parametrize("kslices", [2, 4])
+@pytest.mark.parametrize("split", [1, 3, 8])
+@pytest.mark.parametrize("warps,stages", [(2, 4), (2, 8), (4, 4)])
+@pytest.mark.parametrize("rows,dtype,g", [(1, "f16", 128), (3, "f32", 64), (11, "bf16", 128),
+                                          (2, "f16", 256)])
+def test_decode_k_slices(cuda_device, kslices, split, warps, stages, rows, dtype, g):
+    # tile_n = K slices: the CTA's stages are dealt out to kslices sets of
+    # consumer warps (stage j to slice j mod kslices), each folding its own
+    # groups, and the sums are added in the CTA (ring depths are multiples of
+    # the slice count, so each slot serves one slice). Odd stage counts, so
+    # slices get unequal counts and a group can be split between slices
+    # (K = 2112 / 2176 / 2304 for g = 64 / 128 / 256); N = 1184 leaves the
+    # last band partly out of range.
+    if rows > 8 and 2 * warps * kslices > 8:
+        pytest.skip("more warps than a 16-row tile allows")
+    if 2 * warps * kslices > 16:
+        pytest.skip("more than 16 consumer warps")
+    plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages,
+            "tile_n": kslices}
+    got, ref, _ = _run(cuda_device, dtype, rows, {64: 2112, 128: 2176, 256: 2304}[g], 1184, g,
+                       plan=plan)
+    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
+
+
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("rows", [1, 2, 4])
 @pytest.mark.parametrize("g", [64, 128, 256])
@@ -287,7 +311,68 @@ def test_prefill_bias_natural_order_fp32_out_and_ld(cuda_device, dtype):
 def test_planner_picks_prefill_for_large_m(cuda_device):
     assert cawq.plan_get(2048, 4096, 4096, 128, torch.float16)["path"] == PATH_PREFILL
     assert cawq.plan_get(1, 4096, 4096, 128, torch.float16)["path"] == PATH_DECODE
-    assert cawq.plan_get(2048, 4096, 4096, 128, torch.float32)["path"] == PATH_GENERIC
+    # f32 activations: the tcgen05 kernel with x split into bf16 hi + lo
+    assert cawq.plan_get(2048, 4096, 4096, 128, torch.float32)["path"] == PATH_PREFILL
+    # ... which needs whole 64-row groups; the CUDA-core kernel takes the rest
+    assert cawq.plan_get(2048, 4096, 4096, 32, torch.float32)["path"] == PATH_GENERIC
+
+
+PREFILL_F32_SHAPES = [(17, 128, 256, 64), (128, 512, 512, 128), (200, 512, 800, 128),
+                      (37, 1024, 4160, 64), (513, 2048, 1024, 256), (129, 4096, 4096, 128)]
+
+
+@pytest.mark.parametrize("rows,k,n,g", PREFILL_F32_SHAPES)
+def test_prefill_f32_tcgen05_parity(cuda_device, rows, k, n, g):
+    # f32 x and scales on the tensor cores: exact (q - z) weights, x as bf16
+    # hi + lo, each group's sum scaled in fp32; N = 800 / 4160 end in a
+    # partial 128-column tile. The north star's bound against the exact sum,
+    # and against the reference's own f32 numerics.
+    x, qw, qz, s, _ = random_awq(k, n, g, "f32", rows, seed=rows + n + 1)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    y = cawq.gemm(t(x, "f32"), t(qw, "u32"), t(qz, "u32"), t(s, "f32"), g,
+                  plan={"path": PATH_PREFILL})
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().astype(np.float64)
+    ref = oracle.gemm_f64(x, qw, qz, s, g, dtype="f32", deq_round=False)
+    assert max_rel_err(got, ref) <= 1e-4
+    ref_numerics = oracle.gemm_ref(x, qw, qz, s, g, dtype="f32").astype(np.float64)
+    assert max_rel_err(got, ref_numerics) <= GEMM_TOL["f32"]
+
+
+def test_prefill_f32_bias_natural_order_ld_and_determinism(cuda_device):
+    rows, k, n, g = 300, 1024, 512, 128
+    x, qw, qz, s, b = random_awq(k, n, g, "f32", rows, seed=19)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    full = torch.zeros(rows, 2 * n, dtype=torch.float32, device=cuda_device)
+    args = (t(x, "f32"), t(qw, "u32"), t(qz, "u32"), t(s, "f32"), g)
+    cawq.gemm(*args, bias=t(b, "f32"), out=full[:, n:], order="natural",
+              plan={"path": PATH_PREFILL})
+    y2 = cawq.gemm(*args, bias=t(b, "f32"), order="natural", plan={"path": PATH_PREFILL})
+    torch.cuda.synchronize()
+    ref = oracle.gemm_f64(x, qw, qz, s, g, bias=b, dtype="f32", order="natural",
+                          deq_round=False)
+    got = full.cpu().numpy()
+    assert max_rel_err(got[:, n:], ref) <= 1e-4
+    assert float(np.abs(got[:, :n]).max()) == 0.0
+    assert torch.equal(full[:, n:], y2)
+
+
+def test_prefill_f32_full_size_sampled_rows(cuda_device):
+    # configs[2] with f32 activations: M = 2048 on the 4096 x 4096 layer
+    from cube_awq_b200 import synth
+    k, n, g, m = 4096, 4096, 128, 2048
+    w = synth.make_weights(k, n, g, torch.float32, cuda_device, seed=87)
+    xt = synth.make_input(m, k, torch.float32, cuda_device, seed=88)
+    y = cawq.gemm(xt, w.qweight, w.qzeros, w.scales, g)
+    y2 = cawq.gemm(xt, w.qweight, w.qzeros, w.scales, g)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    rows = np.arange(0, m, 32)
+    x = xt.cpu().numpy()[rows]
+    ref = oracle.gemm_f64(x, w.qweight.cpu().numpy(), w.qzeros.cpu().numpy(),
+                          w.scales.cpu().numpy(), g, dtype="f32", deq_round=False)
+    assert max_rel_err(y.cpu().numpy()[rows].astype(np.float64), ref) <= 1e-4
+    assert cawq.device_error() == 0
 
 
 def test_prefill_full_size_sampled_rows(cuda_device):
