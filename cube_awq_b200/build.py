@@ -2,6 +2,9 @@
 
     python -m cube_awq_b200.build [--force] [--verbose]
 
+It also builds _cawq_torch.so (csrc/cawq_torch.cpp, against torch's headers
+with the host compiler), the compiled host path of the module forward.
+
 Each translation unit under csrc/ is compiled to an object in csrc/_build/
 (in parallel), then linked with the static CUDA runtime into
 cube_awq_b200/libcube_awq.so. Only the extern "C" symbols of include/cube_awq.h
@@ -105,6 +108,40 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     return LIB_PATH
 
 
+EXT_SRC = os.path.join(CSRC, "cawq_torch.cpp")
+EXT_PATH = os.path.join(PKG_DIR, "_cawq_torch.so")
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> str:
+    """Compile _cawq_torch.so, the compiled host path of the module forward
+    (a torch binding over libcube_awq.so; see csrc/cawq_torch.cpp)."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+    deps = [EXT_SRC, os.path.join(INCLUDE, "cube_awq.h")]
+    if not force and not _stale(EXT_PATH, deps):
+        return EXT_PATH
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    inc = ce.include_paths(device_type="cuda") + [sysconfig.get_paths()["include"], INCLUDE]
+    cxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
+    tmp = EXT_PATH + ".tmp"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_cawq_torch",
+           "-DTORCH_API_INCLUDE_EXTENSION_H"] + [f"-I{d}" for d in inc] + [
+           EXT_SRC, "-o", tmp, f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_python", f"-L{PKG_DIR}", "-lcube_awq", "-Wl,-rpath,$ORIGIN",
+           f"-Wl,-rpath,{torch_lib}"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch extension build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, EXT_PATH)
+    return EXT_PATH
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
@@ -112,6 +149,7 @@ def main(argv=None) -> int:
     ap.add_argument("--ptxas-info", action="store_true", help="print registers / spills / smem")
     a = ap.parse_args(argv)
     print(build(force=a.force, verbose=a.verbose, ptxas_info=a.ptxas_info))
+    print(build_torch_ext(force=a.force, verbose=a.verbose))
     return 0
 
 

@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
                   const typename DType<DT>::T* __restrict__ bias,
                   const OutMap<typename DType<ODT>::T> om, uint32_t rows, uint32_t k, uint32_t n,
                   uint32_t g, uint32_t split, uint32_t nstage_ring,
-                  uint32_t strips_u, uint32_t pf_stages, uint32_t kslices) {
+                  uint32_t strips_u, uint32_t pf_stages) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
   constexpr bool kF16Mma = (DT == kF16);
@@ -156,17 +156,9 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
   const int strips = static_cast<int>(strips_u);
-  // Consumer warps: `consumers` column warps (one per 64-column half of each
-  // strip) times `kw_n` K slices: slice kw takes the CTA's stages kw, kw +
-  // kw_n, ... and the slices' sums are added inside the CTA at the end (the
-  // stages of one CTA run in parallel instead of one after another). The ring
-  // depth is a multiple of kw_n, so every slot serves one slice and a
-  // slice's parity waits never skip a phase of its slots. Warps
-  // 0..all_consumers-1; then the producer; on the integer path (one slice)
-  // the X preparation warp last.
+  // warps 0..consumers-1; then the producer; on the integer path the X
+  // preparation warp last
   const int consumers = 2 * strips;
-  const int kw_n = static_cast<int>(kslices);
-  const int all_consumers = consumers * kw_n;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gq = lane >> 2;
@@ -231,7 +223,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   __shared__ int s_issued;  // stages whose copies the producer issued
 
   bool ok = true;
-  if (warp == all_consumers) {
+  if (warp == consumers) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       // valid columns of the band (the bulk copies must stay inside a row)
@@ -310,7 +302,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   }
 
   if constexpr (I8) {
-    if (warp == all_consumers + 1) {
+    if (warp == consumers + 1) {
       // --------------------------------------------------- X preparation
       // Per stage, each X row (rows <= 4) becomes 16-bit fixed point with a
       // power-of-two scale: |x| < 2^(e+1) over the row's 64 values, so
@@ -397,17 +389,15 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   // this warp's strip and 64-column half; the lane's two packed words inside
   // the strip (element gq of the warp's 16-byte chunks A and B) and which four
   // nibbles of them it holds (npar 0: nibbles 0-3, npar 1: nibbles 4-7)
-  const int cw = warp % consumers;  // column warp
-  const int kw = warp / consumers;  // K slice
-  const int strip = cw % strips;
-  const int half = (cw / strips) & 1;
+  const int strip = warp % strips;
+  const int half = (warp / strips) & 1;
   const int wA = 8 * half + (gq >> 1);
   const int wB = wA + 4;
   const int npar = gq & 1;
   int oword = 0;               // the word whose 8 columns this lane writes
   float outv[MT][2][8] = {};   // its sums, rows 8m + 2t + e, column order
 
-  if (warp < all_consumers) {
+  if (warp < consumers) {
     // -------------------------------------------------------- consumers
     // Weights: one ldmatrix.x4.trans per 16-row step. Lane L supplies row
     // L & 7 of matrix L >> 3 (matrices 0 / 1: k rows 0-7 of chunks A / B,
@@ -803,40 +793,28 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     if constexpr (GA) {
       // g is a multiple of 64: groups end on stage boundaries, so the four
       // steps of a stage run without any branch and the fold (if any) follows.
-      // This slice's stages are kw, kw + kw_n, ...; it folds when its next
-      // stage lies in another group (or it has none left), and the stage
-      // after a fold restarts the accumulators (D = A B).
-      // Counters advance without division: the ring slot and its phase
-      // (the depth is a multiple of kw_n) and the stage's index in its group.
       const uint32_t spgs = g / kDecStageRows;  // stages per group
-      uint32_t in_grp = (c_beg + (uint32_t)kw) % spgs;
-      sl = kw;
-      bool fresh = false;                       // D holds nothing to keep
-      for (int j = kw; j < nst; j += kw_n) {
+      uint32_t in_grp = c_beg % spgs;           // stage index inside its group
+      for (int j = 0; j < nst; ++j) {
         if (ok) ok = mbar_wait_bounded(&full[sl], par);
         ok = __all_sync(0xffffffffu, ok);  // keep the warp convergent
         if (!ok) break;
         const uint8_t* sbase = smem + sl * slot;
-        if (fresh) {
+        // a group's first stage (not the CTA's first: D starts at 0 there)
+        if (in_grp == 0 && j > 0) {
           stage_mma(sbase, std::integral_constant<bool, true>{});
         } else {
           stage_mma(sbase, std::integral_constant<bool, false>{});
         }
-        fresh = false;
-        // this slice's next stage, j + kw_n, lies in another group (or there
-        // is none): fold now
-        in_grp += static_cast<uint32_t>(kw_n);
-        if (j + kw_n >= nst || in_grp >= spgs) {
+        if (++in_grp == spgs || j + 1 == nst) {
           fold(sbase + L::s_off(strips), sbase + L::z_off(strips, g),
                std::integral_constant<bool, false>{});
-          fresh = true;
-          while (in_grp >= spgs) in_grp -= spgs;
+          in_grp = 0;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[sl]);
-        sl += kw_n;
-        if (sl >= NS) {
-          sl -= NS;
+        if (++sl == NS) {
+          sl = 0;
           par ^= 1u;
         }
       }
@@ -891,39 +869,6 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       }
     }
 
-    // K slices: slices 1.. leave their sums in shared memory (the ring, free
-    // once every consumer has passed its last stage), slice 0 adds them in
-    // slice order. Only slice 0's warps go on to the output.
-    if (kw_n > 1) {
-      named_bar_sync(2, 32 * all_consumers);  // every stage consumed
-      float* red = reinterpret_cast<float*>(smem);
-      constexpr int kPer = MT * 16;  // floats per lane
-      if (kw > 0) {
-        float* dst = red + ((size_t)((kw - 1) * consumers + cw) * 32 + lane) * kPer;
-#pragma unroll
-        for (int m = 0; m < MT; ++m)
-#pragma unroll
-          for (int n4 = 0; n4 < 4; ++n4)
-            reinterpret_cast<float4*>(dst)[m * 4 + n4] =
-                make_float4(tot[m][n4][0], tot[m][n4][1], tot[m][n4][2], tot[m][n4][3]);
-      }
-      named_bar_sync(2, 32 * all_consumers);
-      if (kw == 0) {
-        for (int src = 1; src < kw_n; ++src) {
-          const float* sp = red + ((size_t)((src - 1) * consumers + cw) * 32 + lane) * kPer;
-#pragma unroll
-          for (int m = 0; m < MT; ++m)
-#pragma unroll
-            for (int n4 = 0; n4 < 4; ++n4) {
-              const float4 f = reinterpret_cast<const float4*>(sp)[m * 4 + n4];
-              tot[m][n4][0] += f.x;
-              tot[m][n4][1] += f.y;
-              tot[m][n4][2] += f.z;
-              tot[m][n4][3] += f.w;
-            }
-        }
-      }
-    }
     // Lanes gq and gq ^ 1 hold the two nibble halves of words wA and wB: swap
     // one slot so that each lane has all 8 columns of one word.
     oword = npar ? wB : wA;
@@ -1120,20 +1065,6 @@ static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
          p.g % kDecStageRows == 0 && plan.warps <= kDecI8MaxStrips;
 }
 
-static int decode_kslices(const cawq_plan& plan) { return plan.tile_n > 1 ? plan.tile_n : 1; }
-
-// bytes of the stage ring (the K slices' sums reuse it at the end)
-static size_t decode_ring_bytes(const GemmProblem& p, const cawq_plan& plan) {
-  const uint32_t g = static_cast<uint32_t>(p.g);
-  const bool mt1 = decode_mt(p.rows) == 1;
-  const size_t slot = p.dtype == kF32
-                          ? (mt1 ? DecodeLayout<kF32, 1>::slot_bytes(plan.warps, g)
-                                 : DecodeLayout<kF32, 2>::slot_bytes(plan.warps, g))
-                          : (mt1 ? DecodeLayout<kF16, 1>::slot_bytes(plan.warps, g)
-                                 : DecodeLayout<kF16, 2>::slot_bytes(plan.warps, g));
-  return slot * static_cast<size_t>(plan.stages);
-}
-
 static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
   const uint32_t g = static_cast<uint32_t>(p.g);
   const bool mt1 = decode_mt(p.rows) == 1;
@@ -1157,23 +1088,9 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   if (plan.split < 1 || plan.split > 16) return false;
   // any cluster size for the plain epilogue; powers of two for the SiLU one
   if (p.epi == 1 && (plan.split & (plan.split - 1))) return false;
-  // tile_n = K slices per CTA (0 or 1: one); more than one needs groups of
-  // whole stages, the tensor path, and a ring that can hold the slices' sums
-  const int kw = decode_kslices(plan);
-  if (plan.tile_n < 0 || (kw != 1 && kw != 2 && kw != 4)) return false;
-  if (plan.warps < 2 || (plan.warps & 1) ||
-      2 * plan.warps * kw > dec_max_consumers(decode_mt(p.rows)))
+  if (plan.tile_n > 1) return false;
+  if (plan.warps < 2 || (plan.warps & 1) || 2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
     return false;
-  if (kw > 1) {
-    // a ring slot must always serve the same slice (stage j lives in slot
-    // j % stages and belongs to slice j % kw), so that a slice never skips a
-    // phase of the slots it waits on
-    if (plan.stages % kw != 0) return false;
-    if (p.g % kDecStageRows != 0 || decode_use_i8(p, plan)) return false;
-    const size_t ring = decode_ring_bytes(p, plan);
-    const size_t red = (size_t)(kw - 1) * 2 * plan.warps * 32 * decode_mt(p.rows) * 16 * 4;
-    if (ring < red) return false;
-  }
   if (plan.stages < 1 || plan.stages > kDecMaxStages) return false;
   if (plan.reserved[2] < 0 || plan.reserved[2] > 1) return false;
   // SiLU-gated epilogue: whole 256-column gate / up blocks, AWQ order, output
@@ -1230,8 +1147,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(bands * plan.split);
-  const int kw = decode_kslices(plan);
-  cfg.blockDim = dim3((2 * plan.warps * kw + (I8 ? 2 : 1)) * 32);
+  cfg.blockDim = dim3((2 * plan.warps + (I8 ? 2 : 1)) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = p.stream;
   cudaLaunchAttribute attr[2];
@@ -1259,8 +1175,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                             static_cast<uint32_t>(p.n), static_cast<uint32_t>(p.g),
                             static_cast<uint32_t>(plan.split),
                             static_cast<uint32_t>(plan.stages), static_cast<uint32_t>(plan.warps),
-                            static_cast<uint32_t>(plan.reserved[1] > 0 ? plan.reserved[1] : 0),
-                            static_cast<uint32_t>(kw));
+                            static_cast<uint32_t>(plan.reserved[1] > 0 ? plan.reserved[1] : 0));
 }
 
 template <int DT, int ODT, int ORDER>

@@ -26,13 +26,14 @@
 //               tcgen05.mma.cta_group::1.kind::f16 (bf16, M=128, N=128, K=16);
 //   warp 2      TMA producer of the packed weights + zero row (W ring) and,
 //               at each group's first stage, of the group's scale row;
-//   warps 3-6   split each X stage into the hi / lo bf16 A tiles (K-major,
-//               128-byte swizzle);
-//   warps 7-10  turn the packed stage into the exact (q - z) bf16 B tile
+//   warps 3-10  split each X stage into the hi / lo bf16 A tiles (K-major,
+//               128-byte swizzle): this is the most work per stage, since
+//               every column tile converts its own rows of X;
+//   warps 11-14 turn the packed stage into the exact (q - z) bf16 B tile
 //               (MN-major, 128-byte swizzle);
-//   warps 11-18 per group: running += s · D_g (tcgen05.ld / st), two per
-//               TMEM lane quarter, 64 columns each; after the last group,
-//               add the bias and store the rows.
+//   warps 15-18 per group: running += s · D_g (tcgen05.ld / st), one per
+//               TMEM lane quarter; after the last group, add the bias and
+//               store the rows.
 #pragma once
 
 #include "cawq_common.cuh"
@@ -97,9 +98,13 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float (
 __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
   const uint32_t u0 = __float_as_uint(x0), u1 = __float_as_uint(x1);
   hi = prmt(u0, u1, 0x7632u);
-  const float r0 = x0 - __uint_as_float(u0 & 0xFFFF0000u);
-  const float r1 = x1 - __uint_as_float(u1 & 0xFFFF0000u);
-  const __nv_bfloat162 l = __floats2bfloat162_rn(r0, r1);
+  // (x0, x1) - (hi0, hi1) as one packed f32x2 subtraction
+  const uint64_t xv = (uint64_t)u0 | ((uint64_t)u1 << 32);
+  const uint64_t hv = xv & 0xFFFF0000FFFF0000ull;
+  uint64_t rv;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(rv) : "l"(xv), "l"(hv));
+  const __nv_bfloat162 l = __floats2bfloat162_rn(__uint_as_float((uint32_t)rv),
+                                                 __uint_as_float((uint32_t)(rv >> 32)));
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
@@ -147,10 +152,10 @@ __global__ void __launch_bounds__(kP32Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::kXSt; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], 128);
+      mbar_init(&xempty[s], 256);
     }
     for (int s = 0; s < L::kASt; ++s) {
-      mbar_init(&afull[s], 128);
+      mbar_init(&afull[s], 256);
       mbar_init(&aempty[s], 1);
     }
     for (int s = 0; s < L::kWSt; ++s) {
@@ -163,9 +168,9 @@ __global__ void __launch_bounds__(kP32Threads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&dfull[b], 1);
-      mbar_init(&dempty[b], 256);
+      mbar_init(&dempty[b], 128);
       mbar_init(&sfull[b], 1);
-      mbar_init(&sempty[b], 256);
+      mbar_init(&sempty[b], 128);
     }
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
@@ -263,9 +268,9 @@ __global__ void __launch_bounds__(kP32Threads, 1)
       role_ok = ok;
     }
     __syncwarp();
-  } else if (warp >= 3 && warp <= 6) {
+  } else if (warp >= 3 && warp <= 10) {
     // ------------------------------------------ X split into hi / lo
-    const int t = threadIdx.x - 96;  // 0..127
+    const int t = threadIdx.x - 96;  // 0..255
     bool ok = true;
     for (int kt = 0; kt < KT; ++kt) {
       const int sx = kt % L::kXSt, ux = kt / L::kXSt;
@@ -278,8 +283,8 @@ __global__ void __launch_bounds__(kP32Threads, 1)
         uint8_t* al = ah + L::kA;
         // 128 rows x 8 chunks of 8 k; item i: row i >> 3, chunk i & 7
 #pragma unroll 2
-        for (int it = 0; it < 8; ++it) {
-          const int i = t + 128 * it;
+        for (int it = 0; it < 4; ++it) {
+          const int i = t + 256 * it;
           const int r = i >> 3, c8 = i & 7, r7 = r & 7;
           // f32 source: box c8 >> 2 (k 0-31 / 32-63), 16-byte chunks 2 (c8 & 3)
           // and + 1 of row r, 128-byte swizzled
@@ -302,9 +307,9 @@ __global__ void __launch_bounds__(kP32Threads, 1)
       mbar_arrive(&afull[sa]);
     }
     role_ok = ok;
-  } else if (warp >= 7 && warp <= 10) {
+  } else if (warp >= 11 && warp <= 14) {
     // ------------------------------------------- dequantize: B = q - z
-    const int t = threadIdx.x - 224;  // 0..127
+    const int t = threadIdx.x - 352;  // 0..127
     const int w = t & 15;             // packed word of the row (8 columns)
     const int r0 = t >> 4;            // rows r0 + 8 i
     const int a = w >> 3, l = w & 7;  // 64-column block, 16-byte chunk in it
@@ -345,7 +350,6 @@ __global__ void __launch_bounds__(kP32Threads, 1)
   } else {
     // ------------------------------------------------ group epilogue
     const int lq = warp & 3;  // TMEM lane quarter this warp may access
-    const int ch = (warp - 11) >> 2;  // column half (64 columns)
     const uint32_t row_t = (uint32_t)(32 * lq);
     const uint32_t run = tmem + 2 * kP32BN + (row_t << 16);
     bool ok = true;
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(kP32Threads, 1)
         const uint32_t dbuf = tmem + (uint32_t)b * kP32BN + (row_t << 16);
         const bool last = grp == NG - 1;
 #pragma unroll 1
-        for (int c = 2 * ch; c < 2 * ch + 2; ++c) {
+        for (int c = 0; c < kP32BN / 32; ++c) {
           float d[32], acc[32];
           // both loads in flight before the one wait
           tmem_ld_32x32b_x32_nowait(dbuf + 32 * c, d);

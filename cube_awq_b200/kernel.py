@@ -381,7 +381,7 @@ class PreparedWeights:
     holds the tensors it was made from (``matches`` compares identity)."""
 
     __slots__ = ("qweight", "qzeros", "scales", "bias", "k", "n", "group_size", "dtype",
-                 "code", "order", "ptrs", "device", "dev_index", "tail", "call")
+                 "code", "order", "ptrs", "device", "dev_index", "tail", "call", "fast")
 
     def __init__(self, qweight, qzeros, scales, group_size, bias=None, order="awq"):
         _require_cuda(qweight, qzeros, scales, bias)
@@ -414,10 +414,30 @@ class PreparedWeights:
         # cawq_gemm's arguments after `rows`, and the bound C function
         self.tail = (k, n, group_size, self.code, self.code, self.order, n)
         self.call = _lib.lib().cawq_gemm
+        # the compiled forward (checks, allocation and C call in C++), if built
+        ext = _torch_ext()
+        self.fast = ext.Layer(qweight, qzeros, scales, bias, group_size,
+                              self.order) if ext is not None else None
 
     def matches(self, qweight, qzeros, scales, bias) -> bool:
         return (self.qweight is qweight and self.qzeros is qzeros and self.scales is scales and
                 self.bias is bias)
+
+
+_EXT = False  # not looked up yet
+
+
+def _torch_ext():
+    """_cawq_torch (csrc/cawq_torch.cpp), the compiled host path of the
+    module forward over libcube_awq.so, or None if it was not built."""
+    global _EXT
+    if _EXT is False:
+        try:
+            from . import _cawq_torch as ext
+        except ImportError:
+            ext = None
+        _EXT = ext
+    return _EXT
 
 
 def gemm_prepared(w: PreparedWeights, x: torch.Tensor) -> torch.Tensor:

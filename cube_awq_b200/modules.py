@@ -82,10 +82,17 @@ class AWQGEMMLinear:
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         """awq_gemm.rs:146-232: [..., K] -> [..., N]; bias fused after the K sum."""
         w = self._prep
-        if (w is not None and input.dim() == 2 and input.shape[1] == w.k and
-                w.matches(self.qweight, self.qzeros, self.scales, self.bias) and
-                input.is_contiguous()):
-            return gemm_prepared(w, input)  # the common decode / prefill call
+        if w is not None and w.matches(self.qweight, self.qzeros, self.scales, self.bias):
+            # the common decode / prefill call: checks, allocation and the C
+            # call in compiled code; an input it does not take goes on below
+            if w.fast is not None:
+                r = w.fast.forward(input)
+                if r.__class__ is torch.Tensor:
+                    return r
+                if r is not None:
+                    check(r)
+            elif input.dim() == 2 and input.shape[1] == w.k and input.is_contiguous():
+                return gemm_prepared(w, input)
         _shape_assert(input.dim() >= 2, "input tensor must have at least 2 dims: [..., K]")
         k = input.shape[-1]
         _shape_assert(k > 0, "input last dim (K) must be > 0")
@@ -164,6 +171,12 @@ class AWQLinear:
         if w is None or not w.matches(self.qweight, self.qzeros, self.scales, None):
             w = self._prep = PreparedWeights(self.qweight, self.qzeros, self.scales,
                                              self.group_size(), order="natural")
+        if w.fast is not None:
+            r = w.fast.forward(x)
+            if r.__class__ is torch.Tensor:
+                return r
+            if r is not None:
+                check(r)
         return gemm_prepared(w, x)
 
     __call__ = forward

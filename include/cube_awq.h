@@ -104,10 +104,7 @@ typedef struct cawq_plan {
   int path;      /* cawq_path                                            */
   int split;     /* decode: CTAs per cluster splitting K (1..16)         */
   int warps;     /* decode: 128-column strips per CTA (even, 2..8)      */
-  int tile_n;    /* prefill: CTA tile N; decode: K slices per CTA (0 or
-                    1: one; 2 or 4: the CTA's stages are dealt out to that
-                    many sets of consumer warps, whose sums are added in
-                    the CTA; needs group_size % 64 == 0)                   */
+  int tile_n;    /* prefill: CTA tile N; decode: 0                       */
   int stages;    /* pipeline stages                                      */
   int reserved[3]; /* reserved[0] = 1: launch without programmatic
                       dependent launch (no overlap with the previous

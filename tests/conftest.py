@@ -22,6 +22,7 @@ def pytest_configure(config):
 def _ensure_built():
     from cube_awq_b200 import build as b
     b.build()
+    b.build_torch_ext()
     import oracle
     oracle.build()
 

@@ -124,30 +124,6 @@ def test_decode_every_plan(cuda_device, split, warps, stages, rows, dtype, mma):
     assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
 
 
-@pytest.mark.parametrize("kslices", [2, 4])
-@pytest.mark.parametrize("split", [1, 3, 8])
-@pytest.mark.parametrize("warps,stages", [(2, 4), (2, 8), (4, 4)])
-@pytest.mark.parametrize("rows,dtype,g", [(1, "f16", 128), (3, "f32", 64), (11, "bf16", 128),
-                                          (2, "f16", 256)])
-def test_decode_k_slices(cuda_device, kslices, split, warps, stages, rows, dtype, g):
-    # tile_n = K slices: the CTA's stages are dealt out to kslices sets of
-    # consumer warps (stage j to slice j mod kslices), each folding its own
-    # groups, and the sums are added in the CTA (ring depths are multiples of
-    # the slice count, so each slot serves one slice). Odd stage counts, so
-    # slices get unequal counts and a group can be split between slices
-    # (K = 2112 / 2176 / 2304 for g = 64 / 128 / 256); N = 1184 leaves the
-    # last band partly out of range.
-    if rows > 8 and 2 * warps * kslices > 8:
-        pytest.skip("more warps than a 16-row tile allows")
-    if 2 * warps * kslices > 16:
-        pytest.skip("more than 16 consumer warps")
-    plan = {"path": PATH_DECODE, "split": split, "warps": warps, "stages": stages,
-            "tile_n": kslices}
-    got, ref, _ = _run(cuda_device, dtype, rows, {64: 2112, 128: 2176, 256: 2304}[g], 1184, g,
-                       plan=plan)
-    assert max_rel_err(got, ref) <= GEMM_TOL[dtype]
-
-
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("rows", [1, 2, 4])
 @pytest.mark.parametrize("g", [64, 128, 256])
