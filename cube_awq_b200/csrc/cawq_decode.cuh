@@ -59,8 +59,6 @@ namespace cawq {
 constexpr int kDecTileCols = 128;  // output columns per strip (consumer warp)
 constexpr int kDecTileWords = 16;  // packed words per k row in a strip
 constexpr int kDecBoxWords = 32;   // packed words per k row in a weight box (2 strips)
-// A CTA of one strip loads one 16-word (64-byte) box per stage, 64-byte
-// swizzled: 16-byte chunk c of box row r lands at c ^ ((r >> 1) & 3).
 constexpr int kDecStageRows = 64;  // k rows per TMA stage (4 MMA steps)
 constexpr int kDecMaxWarps = 8;
 constexpr int kDecMaxStages = 8;
@@ -241,9 +239,6 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
         uint8_t* dst = smem + sl * slot;
         const int kr = static_cast<int>((c_beg + j) * kDecStageRows);
         mbar_arrive_expect_tx(&full[sl], tx);
-        if (strips == 1) {
-          tma_load_2d(dst + L::kXBytes, &tm_w, static_cast<int>(pband), kr, &full[sl]);
-        }
         for (int b = 0; b < strips / 2; ++b) {
           tma_load_2d(dst + L::kXBytes + 2 * b * L::kWBytes, &tm_w,
                       static_cast<int>(pband + b * kDecBoxWords), kr, &full[sl]);
@@ -277,7 +272,6 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       // stages past the ring: weights, scales and zeros prefetched into L2 only
       auto prefetch_weights = [&](int j) {
         const int kr = static_cast<int>((c_beg + j) * kDecStageRows);
-        if (strips == 1) tma_prefetch_l2_2d(&tm_w, static_cast<int>(pband), kr);
         for (int b = 0; b < strips / 2; ++b)
           tma_prefetch_l2_2d(&tm_w, static_cast<int>(pband + b * kDecBoxWords), kr);
         const uint32_t g0 = (uint32_t)kr / g;
@@ -408,22 +402,13 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     // Weights: one ldmatrix.x4.trans per 16-row step. Lane L supplies row
     // L & 7 of matrix L >> 3 (matrices 0 / 1: k rows 0-7 of chunks A / B,
     // 2 / 3: rows 8-15); the 128-byte swizzle moves chunk c of box row r to
-    // c ^ (r & 7), which spreads each matrix over all banks. A one-strip CTA's
-    // 64-byte box rows hold chunk c of row r at c ^ ((r >> 1) & 3): the 8 rows
-    // of a matrix again fall on 8 different bank groups.
-    uint32_t wld, wstep;  // this lane's row address in step 0; bytes per step
+    // c ^ (r & 7), which spreads each matrix over all banks.
+    uint32_t wld;
     {
       const int mi = lane >> 3, r8 = lane & 7;
-      if (strips == 1) {
-        const int chunk = 2 * half + (mi & 1);
-        wld = L::kXBytes + (8 * (mi >> 1) + r8) * 64 + ((chunk ^ ((r8 >> 1) & 3)) << 4);
-        wstep = 1024;
-      } else {
-        const int chunk = 4 * (strip & 1) + 2 * half + (mi & 1);  // 16-byte chunk in the box row
-        wld = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + (8 * (mi >> 1) + r8) * 128 +
-              ((chunk ^ r8) << 4);
-        wstep = 2048;
-      }
+      const int chunk = 4 * (strip & 1) + 2 * half + (mi & 1);  // 16-byte chunk in the box row
+      wld = L::kXBytes + (strip >> 1) * 2 * L::kWBytes + (8 * (mi >> 1) + r8) * 128 +
+            ((chunk ^ r8) << 4);
     }
     // scales of words wA / wB and their zero words inside the stage rows
     const uint32_t s_off[2] = {(uint32_t)(strip * kDecTileCols + 8 * wA) * (uint32_t)sizeof(T),
@@ -538,7 +523,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
           uint32_t R[4];
-          ldmatrix_x4_trans(smem_u32(sbase) + wld + st * wstep, R[0], R[1], R[2], R[3]);
+          ldmatrix_x4_trans(smem_u32(sbase) + wld + st * 2048, R[0], R[1], R[2], R[3]);
           const uint4 bt = *reinterpret_cast<const uint4*>(tbase + st * 512 + lane * 16);
 #pragma unroll
           for (int mk = 0; mk < 2; ++mk) {
@@ -740,7 +725,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     auto step_mma = [&](const uint8_t* sbase, int s, const uint32_t (&bh)[MT][2],
                         const uint32_t (&bl)[MT][2], auto zero_tag) {
       uint32_t R[4];
-      ldmatrix_x4_trans(smem_u32(sbase) + wld + s * wstep, R[0], R[1], R[2], R[3]);
+      ldmatrix_x4_trans(smem_u32(sbase) + wld + s * 2048, R[0], R[1], R[2], R[3]);
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         mma(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1], zero_tag);
@@ -1077,7 +1062,7 @@ static int decode_mt(size_t rows) { return rows <= 8 ? 1 : 2; }
 static bool decode_use_i8(const GemmProblem& p, const cawq_plan& plan) {
   return plan.reserved[2] == 1 && p.epi == 0 && p.nrep == 0 &&
          p.rows <= (size_t)kDecI8MaxRows && p.dtype != kF32 &&
-         p.g % kDecStageRows == 0 && plan.warps >= 2 && plan.warps <= kDecI8MaxStrips;
+         p.g % kDecStageRows == 0 && plan.warps <= kDecI8MaxStrips;
 }
 
 static size_t decode_smem(const GemmProblem& p, const cawq_plan& plan) {
@@ -1104,16 +1089,13 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   // any cluster size for the plain epilogue; powers of two for the SiLU one
   if (p.epi == 1 && (plan.split & (plan.split - 1))) return false;
   if (plan.tile_n > 1) return false;
-  // strips per CTA: 1, or an even count (pairs share a 128-byte box)
-  if (plan.warps < 1 || (plan.warps > 1 && (plan.warps & 1)) ||
-      2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
+  if (plan.warps < 2 || (plan.warps & 1) || 2 * plan.warps > dec_max_consumers(decode_mt(p.rows)))
     return false;
   if (plan.stages < 1 || plan.stages > kDecMaxStages) return false;
   if (plan.reserved[2] < 0 || plan.reserved[2] > 1) return false;
   // SiLU-gated epilogue: whole 256-column gate / up blocks, AWQ order, output
   // in the input dtype
-  if (p.epi == 1 && (p.n % 256 != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype ||
-                     plan.warps < 2))
+  if (p.epi == 1 && (p.n % 256 != 0 || p.order != kOrderAwq || p.out_dtype != p.dtype))
     return false;
   // replicated output (tensor-parallel push): plain epilogue, one output
   // range, f16 / bf16 activations, AWQ order
@@ -1132,10 +1114,8 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
   using OT = typename DType<ODT>::T;
   CUtensorMap tm_w, tm_x;
   const uint64_t npk = p.n / 8;
-  const bool box64 = plan.warps == 1;  // one strip: a 64-byte box, 64-byte swizzle
-  if (!encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4,
-                 box64 ? kDecTileWords : kDecBoxWords, kDecStageRows,
-                 box64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)) {
+  if (!encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kDecBoxWords,
+                 kDecStageRows, CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
   const CUtensorMapDataType xdt = DT == kF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -1279,7 +1259,7 @@ void decode_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* o
   const size_t nst_total = (p.k / 16 + 3) / 4;
   for (int split = 2; split <= 16; split *= 2) {
     if (nst_total < (size_t)split) break;
-    for (int warps : {1, 2, 4, 6, 8}) {
+    for (int warps : {2, 4, 6, 8}) {
       for (int stages : {2, 3, 4, 6}) {
         cawq_plan pl = {};
         pl.path = CAWQ_PATH_DECODE;

@@ -103,7 +103,7 @@ typedef struct cawq_gemm_args {
 typedef struct cawq_plan {
   int path;      /* cawq_path                                            */
   int split;     /* decode: CTAs per cluster splitting K (1..16)         */
-  int warps;     /* decode: 128-column strips per CTA (1, or even 2..8) */
+  int warps;     /* decode: 128-column strips per CTA (even, 2..8)      */
   int tile_n;    /* prefill: CTA tile N; decode: 0                       */
   int stages;    /* pipeline stages                                      */
   int reserved[3]; /* reserved[0] = 1: launch without programmatic
