@@ -271,7 +271,8 @@ static bool plan_supports(const GemmProblem& p, const cawq_plan& plan, const Dev
   switch (plan.path) {
     case CAWQ_PATH_DECODE: return decode_supports(p, plan, dev);
     case CAWQ_PATH_PREFILL: return prefill_supports(p, plan, dev);
-    case CAWQ_PATH_GENERIC: return p.epi == 0 && p.nrep == 0 && generic_supports(p);
+    case CAWQ_PATH_GENERIC:
+      return p.epi == 0 && p.nrep == 0 && !(p.scw && p.out_k) && generic_supports(p);
     default: return false;
   }
 }
@@ -351,7 +352,8 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
                                cawq_dtype out_dtype, cawq_order order, size_t ld_out,
                                const cawq_plan* plan, void* stream, bool module_rules,
                                int epi = 0, const QkvOut* qkv = nullptr,
-                               void* const* reps = nullptr, int nrep = 0) {
+                               void* const* reps = nullptr, int nrep = 0,
+                               void* const* scat = nullptr, size_t scw = 0) {
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype))
     return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
   if (out_dtype != dtype && out_dtype != CAWQ_F32)
@@ -398,6 +400,10 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
   }
   for (int i = 0; i < nrep; ++i) p.rep[i] = reps[i];
   p.nrep = nrep;
+  if (scat && scw) {
+    for (int i = 0; i < 8; ++i) p.scat[i] = scat[i];
+    p.scw = scw;
+  }
   cawq_plan pl = plan ? *plan : choose_plan(p, dev);
   if (plan && !plan_supports(p, pl, dev))
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "the plan cannot run this problem");
@@ -1267,6 +1273,37 @@ CAWQ_API cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t e
   if (n % 32 != 0) return fail(CAWQ_ERR_INVALID_SHAPE, "n must be a multiple of 32");
   size_t off = 0;
   const size_t plane = rows * n * sizeof(float);
+  const int world = peers->world;
+  // Reduce-scatter + all-gather once the one-shot push would send more than
+  // 4 MiB per rank (each rank then sends (world-1)/world of a partial plane
+  // and of the result, instead of world-1 whole planes); the same choice on
+  // every rank, from the shapes alone.
+  const bool rs = world > 1 && n % (32 * (size_t)world) == 0 &&
+                  plane * (size_t)(world - 1) > (4u << 20);
+  if (rs) {
+    const size_t es = dtype == CAWQ_F32 ? 4 : 2;
+    const size_t gath = (plane + 255) / 256 * 256;  // gather region after the partials
+    if ((st = p2p_check(peers, epoch, gath + rows * n * es, &off)) != CAWQ_OK) return st;
+    if (rows == 0) return CAWQ_OK;
+    if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+    // column chunk o of this rank's partial -> rank o's region part[rank]
+    const size_t cw = n / world;
+    void* scat[8] = {};
+    for (int o = 0; o < world; ++o)
+      scat[o] = static_cast<uint8_t*>(peers->base[o]) + off + peers->rank * rows * cw * 4;
+    st = gemm_common(x, qweight, qzeros, scales, nullptr, scat[peers->rank], rows, kl, n,
+                     group_size, dtype, CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0,
+                     nullptr, nullptr, 0, scat, cw);
+    if (st != CAWQ_OK) return st;
+    P2PSync sa = p2p_sync(peers, epoch), sb = p2p_sync(peers, epoch);
+    sb.fofs = 8;  // the gather's own flag words
+    const float* part = reinterpret_cast<const float*>(
+        static_cast<uint8_t*>(peers->base[peers->rank]) + off);
+    cudaError_t e = launch_p2p_rowpar_rs(sa, sb, part, off + gath, bias, out, rows, n, dtype,
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "reduce-scatter launch");
+    return CAWQ_OK;
+  }
   if ((st = p2p_check(peers, epoch, plane * peers->world, &off)) != CAWQ_OK) return st;
   if (rows == 0) return CAWQ_OK;
   if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");

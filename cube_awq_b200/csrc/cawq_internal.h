@@ -44,6 +44,11 @@ struct GemmProblem {
   // Decode and prefill kernels, f16 / bf16 activations, AWQ order only.
   void* rep[7] = {};
   int nrep = 0;
+  // scatter of a single-range output to the owners of its column chunks (the
+  // reduce-scatter push of a row-parallel layer): columns [o scw, (o+1) scw)
+  // go to scat[o] + row * scw + (col - o scw); scw = 0: off.
+  void* scat[8] = {};
+  size_t scw = 0;
 };
 
 // Thread-local error message (cawq_last_error).
@@ -116,11 +121,21 @@ struct P2PSync {
   int world, rank;
   uint32_t epoch;
   uint64_t timeout_ns;
+  int fofs = 0;  // first flag word of the set this exchange uses (0 or 8)
 };
 // After the push of a column-parallel GEMM: signal, wait, then copy the
 // gathered [rows, n] result (dense in `slot`) to out (row stride ld_out).
 cudaError_t launch_p2p_colpar_finish(const P2PSync& s, const void* slot, void* out, size_t rows,
                                      size_t n, size_t ld_out, int dtype, cudaStream_t stream);
+// Reduce-scatter + all-gather finish of a row-parallel GEMM whose epilogue
+// scattered its fp32 partial to the owners of the column chunks (part =
+// this rank's region [world][rows][n/world]): flag set A, sum the own chunk,
+// push it (cast, + bias) into every gather region (at gath_off of each
+// buffer) and out; flag set B, copy the other chunks from the own gather
+// region to out. dtype f16 / bf16.
+cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, const float* part,
+                                 size_t gath_off, const void* bias, void* out, size_t rows,
+                                 size_t n, int dtype, cudaStream_t stream);
 // After the push of a row-parallel GEMM's fp32 partials into slot[world][rows][n]:
 // signal, wait, then out = sum over ranks (in rank order) + bias, cast to dtype.
 cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const void* bias,

@@ -764,6 +764,7 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
   // replicated output (tensor-parallel push): plain epilogue, one output
   // range, AWQ order
   if (p.nrep > 0 && (p.epi != 0 || p.out_k || p.order != kOrderAwq)) return false;
+  if (p.scw && (p.epi != 0 || p.out_k || p.nrep > 0)) return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;

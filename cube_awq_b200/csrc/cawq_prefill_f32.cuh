@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kP32Threads, 1)
 
 // ------------------------------------------------------------------ host
 bool prefill_f32_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
-  if (plan.split > 1 || p.epi != 0 || p.nrep > 0) return false;
+  if (plan.split > 1 || p.epi != 0 || p.nrep > 0 || (p.scw && p.out_k)) return false;
   if (p.dtype != kF32 || p.out_dtype != kF32) return false;
   if (dev.cc_major != 10 || dev.smem_optin < P32Layout::kSmem) return false;
   if (p.rows == 0 || p.k % kP32BK != 0 || p.g % kP32BK != 0 || p.k % p.g != 0 || p.n % 32 != 0)

@@ -146,7 +146,7 @@ __device__ __forceinline__ bool p2p_signal_and_wait(const P2PSync& s) {
   __shared__ int ok;
   if (threadIdx.x < static_cast<unsigned>(s.world) && threadIdx.x != static_cast<unsigned>(s.rank)) {
     __threadfence_system();
-    uint32_t* f = p2p_flags(s, threadIdx.x) + s.rank;
+    uint32_t* f = p2p_flags(s, threadIdx.x) + s.fofs + s.rank;
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(s.epoch) : "memory");
   }
   if (threadIdx.x == 0) {
@@ -154,7 +154,7 @@ __device__ __forceinline__ bool p2p_signal_and_wait(const P2PSync& s) {
     const uint64_t t0 = globaltimer_ns();
     for (int j = 0; j < s.world && good; ++j) {
       if (j == s.rank) continue;
-      const uint32_t* f = p2p_flags(s, s.rank) + j;
+      const uint32_t* f = p2p_flags(s, s.rank) + s.fofs + j;
       for (uint32_t it = 0;; ++it) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
@@ -208,6 +208,68 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Reduce-scatter half of the row-parallel exchange. Each rank's GEMM pushed
+// the fp32 partial of column chunk o (cw = n / world columns) into rank o's
+// buffer, region part[src][rows][cw]. After the flag exchange (set A) this
+// rank owns chunk `rank`: it sums the world partials in rank order, adds the
+// bias once, casts, and writes the result to its own output and to the same
+// place of every peer's gather region gath[rows][n] (the all-gather push).
+template <int DT>
+__global__ void __launch_bounds__(256)
+    p2p_rowpar_rs_kernel(const P2PSync s, const float* __restrict__ part,
+                         const typename DType<DT>::T* __restrict__ bias,
+                         typename DType<DT>::T* __restrict__ out, size_t gath_off, size_t rows,
+                         size_t n) {
+  using T = typename DType<DT>::T;
+  if (!p2p_signal_and_wait(s)) return;
+  const size_t cw = n / s.world, c0 = (size_t)s.rank * cw;
+  const size_t oct = rows * (cw / 8);  // 8 columns per item (cw % 32 == 0)
+  const size_t plane = rows * cw;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < oct;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / (cw / 8), c = (i - r * (cw / 8)) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < s.world; ++j) {  // rank order: the same sum on every rank
+      const float4* src = reinterpret_cast<const float4*>(part + j * plane + r * cw + c);
+      const float4 a = __ldcg(src), b = __ldcg(src + 1);  // L2: peers wrote them
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    uint4 v;
+    T* h = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c0 + c + e]) : 0.f));
+    const size_t at = r * n + c0 + c;
+    *reinterpret_cast<uint4*>(out + at) = v;
+    for (int j = 0; j < s.world; ++j) {
+      if (j == s.rank) continue;
+      T* g = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(p2p_flags(s, j)) + gath_off);
+      *reinterpret_cast<uint4*>(g + at) = v;  // over NVLink
+    }
+  }
+}
+
+// All-gather half: after the flag exchange (set B) every peer's chunk is in
+// this rank's gather region; copy them (not this rank's own) to the output.
+template <int DT>
+__global__ void __launch_bounds__(256)
+    p2p_rowpar_ag_kernel(const P2PSync s, const typename DType<DT>::T* __restrict__ gath,
+                         typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
+  if (!p2p_signal_and_wait(s)) return;
+  const size_t cw = n / s.world;
+  const size_t per_row = (n - cw) / 8;  // 8-element vectors outside the own chunk
+  const size_t total = rows * per_row;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / per_row;
+    size_t c = (i - r * per_row) * 8;
+    if (c >= (size_t)s.rank * cw) c += cw;  // skip the own chunk
+    const size_t at = r * n + c;
+    *reinterpret_cast<uint4*>(out + at) = __ldcg(reinterpret_cast<const uint4*>(gath + at));
+  }
+}
+
 static unsigned p2p_blocks(size_t work) {
   size_t b = (work + 255) / 256;
   if (b > 148 * 4) b = 148 * 4;  // all blocks resident: each one waits
@@ -248,6 +310,28 @@ cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const 
     p2p_rowpar_finish_kernel<kBF16><<<b, 256, 0, stream>>>(
         s, slot, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), rows,
         n);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, const float* part,
+                                 size_t gath_off, const void* bias, void* out, size_t rows,
+                                 size_t n, int dtype, cudaStream_t stream) {
+  const size_t cw = n / sa.world;
+  const unsigned b1 = p2p_blocks(rows * cw / 8);
+  const unsigned b2 = p2p_blocks(rows * (n - cw) / 8);
+  const void* gath = reinterpret_cast<const uint8_t*>(sa.flags[sa.rank]) + gath_off;
+  if (dtype == kF16) {
+    p2p_rowpar_rs_kernel<kF16><<<b1, 256, 0, stream>>>(
+        sa, part, static_cast<const __half*>(bias), static_cast<__half*>(out), gath_off, rows, n);
+    p2p_rowpar_ag_kernel<kF16><<<b2, 256, 0, stream>>>(
+        sb, static_cast<const __half*>(gath), static_cast<__half*>(out), rows, n);
+  } else {
+    p2p_rowpar_rs_kernel<kBF16><<<b1, 256, 0, stream>>>(
+        sa, part, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out),
+        gath_off, rows, n);
+    p2p_rowpar_ag_kernel<kBF16><<<b2, 256, 0, stream>>>(
+        sb, static_cast<const __nv_bfloat16*>(gath), static_cast<__nv_bfloat16*>(out), rows, n);
   }
   return cudaGetLastError();
 }

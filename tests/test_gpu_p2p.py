@@ -123,3 +123,46 @@ def test_rejects_small_buffers_and_epoch_zero(cuda_device):
     assert "per slot" in _lib.last_error()
     assert _lib.lib().cawq_gemm_rowpar_p2p(peers.table, 0, *args) == \
         _lib.CAWQ_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_rowpar_reduce_scatter_push_on_one_gpu(cuda_device, dtype):
+    # Rank 0 of a two-rank table whose "peer" buffer is a second local buffer;
+    # both of its flag sets for rank 1 (words 1 and 8 + 1) are preset far
+    # ahead, so the waits pass at once. rows * n * 4 bytes above 4 MiB take the
+    # reduce-scatter path: the GEMM scatters its fp32 partial by column chunk
+    # (the peer's chunk to the peer's region part[0]), this rank sums its own
+    # chunk over the planes (the peer's plane here is empty), adds the bias,
+    # writes it to the output and pushes it into the peer's gather region;
+    # the other chunk of the output comes from this rank's own gather region,
+    # which no peer wrote (zeros).
+    rows, k, n, g = 600, 1024, 2048, 128
+    plane = rows * n * 4
+    gath = (plane + 255) // 256 * 256
+    es = 2
+    slot = gath + rows * n * es
+    nbytes = 256 + 2 * (slot + 4096)
+    own, other = _buffer(cuda_device, nbytes), _buffer(cuda_device, nbytes)
+    own.view(torch.int32)[1] = 1 << 20
+    own.view(torch.int32)[9] = 1 << 20
+    peers = tp.TPPeers.from_pointers(2, 0, [own.data_ptr(), other.data_ptr()], nbytes)
+    x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed=31)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    x, qw, qz, s, b = t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), t(b, dtype)
+    row = tp.RowParallelAWQLinear(qw, qz, s, b, backend="p2p", peers=peers,
+                                  input_is_parallel=False)
+    y = row(x)                                     # epoch 1: slot 1
+    torch.cuda.synchronize()
+    assert cawq.device_error() == 0
+    part = cawq.gemm(x[:, :k // 2].contiguous(), row.qweight, row.qzeros, row.scales, g,
+                     out_dtype=torch.float32)
+    cw = n // 2
+    off = 256 + peers.slot_bytes                   # slot 1
+    want0 = (part[:, :cw] + b[:cw].float()).to(x.dtype)
+    assert torch.equal(y[:, :cw], want0)
+    assert float(y[:, cw:].float().abs().max()) == 0.0
+    peer_part = other[off:off + rows * cw * 4].view(torch.float32).view(rows, cw)
+    assert torch.equal(peer_part, part[:, cw:])
+    peer_gath = other[off + gath:off + gath + rows * n * es].view(x.dtype).view(rows, n)
+    assert torch.equal(peer_gath[:, :cw], want0)
+    assert float(peer_gath[:, cw:].float().abs().max()) == 0.0
