@@ -715,14 +715,43 @@ def tp_fused_numbers(dev, world, max_over_ranks, reps=20):
     return res
 
 
+def _graph_calls_us(fn, n_rep, max_over_ranks):
+    """us per fn() replayed from a CUDA graph (captured once, so the host
+    stays out of the timed region), device-timed, max over ranks. fn(stream)
+    issues its work on the given raw stream handle."""
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        fn(s.cuda_stream)  # warm-up outside the graph (lazy set-up)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn(s.cuda_stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(n_rep):
+            g.replay()
+        e1.record(s)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n_rep
+    del g  # a graph holding NCCL calls goes before the communicator
+    torch.cuda.synchronize()
+    return round(max_over_ranks(us), 2)
+
+
 def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
     """configs[4] over all ranks of the job: us per MLP forward (gate_up
     column-parallel without the gather, then down row-parallel on this rank's
     share of the gate_up columns, as after the SiLU-and-mul), GEMM + NCCL
-    path, direct C calls, max over ranks. `one_gpu_us` is the same MLP
-    unsharded on one GPU (each rank times it on its own GPU alone, max over
-    ranks), and `efficiency` = one_gpu_us / (n_gpus * us), the strong-scaling
-    efficiency of the sharded layer."""
+    path (the library's own communicator), each part captured in a CUDA
+    graph so that the host stays out of the timed region, max over ranks.
+    `one_gpu_us` is the same MLP unsharded on one GPU (each rank times it on
+    its own GPU alone, max over ranks), and `efficiency` = one_gpu_us / (n_gpus
+    * us), the strong-scaling efficiency of the sharded layer."""
     import torch
 
     from cube_awq_b200 import _lib, synth, tp
@@ -736,9 +765,9 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
     row = tp.RowParallelAWQLinear(w2.qweight, w2.qzeros, w2.scales, backend="native", comm=comm)
     L = _lib.lib()
     f16 = _lib.CAWQ_F16
-    stream = torch.cuda.current_stream(dev).cuda_stream
     nl = n1 // world
     res = {"n_gpus": world, "backend": "native NCCL (cawq_gemm_colpar shard / cawq_gemm_rowpar)",
+           "timing": "CUDA graph per part (NCCL calls captured), device time, max over ranks",
            "limit": "the down all-reduce (fp32 [M, 8192]) and per-call latency at small M"}
     for m in (1, 8, 2048):
         x = synth.make_input(m, k1, dt, dev, seed=4003)
@@ -750,38 +779,35 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
         h1 = torch.empty(m, n1, dtype=dt, device=dev)
         x2f = synth.make_input(m, k2, dt, dev, seed=4004)
 
-        def col_call(i):
+        def col_call(stream):
             check(L.cawq_gemm(x.data_ptr(), col.qweight.data_ptr(), col.qzeros.data_ptr(),
                               col.scales.data_ptr(), None, h.data_ptr(), m, k1, nl, g, f16, f16,
                               _lib.CAWQ_ORDER_AWQ, nl, stream))
 
-        def row_call(i):
+        def row_call(stream):
             hh_c.copy_(hh)
             check(L.cawq_gemm_rowpar(comm.handle, hh_c.data_ptr(), row.qweight.data_ptr(),
                                      row.qzeros.data_ptr(), row.scales.data_ptr(), None,
                                      out.data_ptr(), part.data_ptr(), m, k2, n2, g, f16, stream))
 
-        def one_gpu_call(i):  # the unsharded MLP on this GPU alone
+        def one_gpu_call(stream):  # the unsharded MLP on this GPU alone
             check(L.cawq_gemm(x.data_ptr(), w1.qweight.data_ptr(), w1.qzeros.data_ptr(),
                               w1.scales.data_ptr(), None, h1.data_ptr(), m, k1, n1, g, f16, f16,
                               _lib.CAWQ_ORDER_AWQ, n1, stream))
             check(L.cawq_gemm(x2f.data_ptr(), w2.qweight.data_ptr(), w2.qzeros.data_ptr(),
                               w2.scales.data_ptr(), None, out.data_ptr(), m, k2, n2, g, f16, f16,
                               _lib.CAWQ_ORDER_AWQ, n2, stream))
-        for i in range(3):
-            col_call(i)
-            row_call(i)
-            one_gpu_call(i)
-        n_it = 3 if m >= 2048 else reps
-        t_col = _timed_calls(col_call, n_it, max_over_ranks)
-        t_row = _timed_calls(row_call, n_it, max_over_ranks)
-        t_one = _timed_calls(one_gpu_call, n_it, max_over_ranks)
+        n_rep = 3 if m >= 2048 else reps
+        t_col = _graph_calls_us(col_call, n_rep, max_over_ranks)
+        t_row = _graph_calls_us(row_call, n_rep, max_over_ranks)
+        t_one = _graph_calls_us(one_gpu_call, n_rep, max_over_ranks)
         t = t_col + t_row
         res[f"M={m}"] = {"us": round(t, 2), "gate_up_colpar_us": t_col,
                          "down_rowpar_allreduce_us": t_row, "one_gpu_us": t_one,
                          "efficiency": round(t_one / (world * t), 3)}
         del x, h, hh_c, out, part, h1, x2f
     del col, row, w1, w2
+    torch.cuda.synchronize()
     comm.close()
     torch.cuda.empty_cache()
     return res

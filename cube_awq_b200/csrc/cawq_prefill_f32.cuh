@@ -47,7 +47,7 @@ constexpr int kP32BK = 64;
 constexpr int kP32Threads = 19 * 32;
 
 struct P32Layout {
-  static constexpr int kXSt = 2, kASt = 2, kWSt = 4, kBSt = 2;
+  static constexpr int kXSt = 2, kASt = 3, kWSt = 4, kBSt = 2;
   static constexpr int kX = kP32BM * kP32BK * 4;      // 32768: f32 X, two 128-B boxes
   static constexpr int kA = kP32BM * kP32BK * 2;      // 16384: one bf16 A tile (hi or lo)
   static constexpr int kB = kP32BK * kP32BN * 2;      // 16384: bf16 B tile

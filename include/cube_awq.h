@@ -524,12 +524,21 @@ cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, con
                                  void* stream);
 /*
  * Row-parallel layer with the all-reduce in the epilogue: the same shards
- * and result as cawq_gemm_rowpar, f16 / bf16. The local GEMM writes its fp32
- * partial [rows, n] into plane [rank] of the slot of every rank's buffer
- * (a one-shot all-reduce: each rank then sums the world planes in rank
- * order, adds the bias once and casts). Needs world * rows * n * 4 bytes per
- * slot; the bytes each rank sends grow with world - 1, so for large rows on
- * more than two ranks cawq_gemm_rowpar's ring all-reduce moves fewer bytes.
+ * and result as cawq_gemm_rowpar, f16 / bf16. Two exchanges, chosen from the
+ * shapes alone (the same on every rank):
+ *   - one-shot (when world * rows * n * 4 bytes per rank is at most 4 MiB,
+ *     or n is not a multiple of 32 * world): the local GEMM writes its fp32
+ *     partial [rows, n] into plane [rank] of the slot of every rank's buffer;
+ *     each rank then sums the world planes in rank order, adds the bias once
+ *     and casts. Needs world * rows * n * 4 bytes per slot;
+ *   - reduce-scatter + all-gather (larger exchanges): the local GEMM writes
+ *     column chunk o (n / world columns) of its fp32 partial into rank o's
+ *     slot only; rank o sums its chunk over the world partials in rank
+ *     order, adds the bias, casts, and writes the chunk into every rank's
+ *     gather region; after a second flag exchange (flag words 8..15 of the
+ *     header) each rank copies the other chunks to `out`. Each rank sends
+ *     (world - 1) / world of a plane in fp32 and of the result in F. Needs
+ *     rows * n * 4 (rounded up to 256) + rows * n * sizeof(F) bytes per slot.
  * Epochs as for cawq_gemm_colpar_p2p.
  */
 cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,

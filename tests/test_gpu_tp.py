@@ -6,7 +6,9 @@ unsharded layer, with torch.distributed's NCCL and with the library's own
 communicator (cawq_gemm_colpar / cawq_gemm_rowpar), and with the collective
 fused into the GEMM's epilogue (cawq_gemm_colpar_p2p / _rowpar_p2p, also
 compared bit for bit with the NCCL path). Rows 1 and 8 run the decode kernel
-(rows = 1 gathers in place), 300 the tensor-core kernel.
+(rows = 1 gathers in place), 300 and 600 the tensor-core kernel; at 600 rows
+the fused row-parallel layer reduce-scatters and all-gathers instead of
+pushing whole partials.
 """
 
 import multiprocessing as mp
@@ -19,7 +21,10 @@ import tp_worker
 
 pytestmark = pytest.mark.gpu
 
-CASES = [(1024, 2048, 128, 1), (1024, 2048, 128, 8), (2048, 1024, 64, 300)]
+# the last case exchanges more than 4 MiB per rank, so the fused row-parallel
+# layer takes its reduce-scatter + all-gather path
+CASES = [(1024, 2048, 128, 1), (1024, 2048, 128, 8), (2048, 1024, 64, 300),
+         (2048, 2048, 128, 600)]
 
 
 def _free_port() -> int:
