@@ -374,6 +374,61 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t& r0, 
 }
 
 // ------------------------------------------------------- global access
+// ------------------------------------------------- packed 16-bit dequant
+// Magic-number unpack shared by the prefill and dequantize kernels: a nibble
+// q masked into the mantissa of the magic value m gives m + q exactly (f16:
+// m = 1024, bf16: m = 128), so (m + q) - (m + z) = q - z exactly and one
+// multiply by s rounds once, as the reference's (q - z) * s in F does.
+template <int DT>
+struct PfHalf2;
+template <>
+struct PfHalf2<kF16> {
+  static constexpr uint32_t kMagic = 0x64006400u;  // f16 1024
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+};
+template <>
+struct PfHalf2<kBF16> {
+  static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128
+  static __device__ __forceinline__ uint32_t sub(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  static __device__ __forceinline__ uint32_t mul(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+};
+
+// Four (1024 + nibble) pairs of adjacent logical columns of one packed word.
+template <int DT, int ORDER>
+__device__ __forceinline__ void pf_pairs(uint32_t q, uint32_t (&t)[4]) {
+  constexpr uint32_t M = PfHalf2<DT>::kMagic;
+  if constexpr (ORDER == kOrderAwq) {
+    // logical (2i, 2i+1) live in nibbles (i, i+4)
+    t[0] = lop3_and_or(q, 0x000F000Fu, M);
+    t[1] = lop3_and_or(q >> 4, 0x000F000Fu, M);
+    t[2] = lop3_and_or(q >> 8, 0x000F000Fu, M);
+    t[3] = lop3_and_or(q >> 12, 0x000F000Fu, M);
+  } else {
+    // logical (2i, 2i+1) live in nibbles (2i, 2i+1) = both halves of byte i
+    const uint32_t q4 = q >> 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t sel = (uint32_t)(i | (i << 4) | ((4 + i) << 8) | ((4 + i) << 12));
+      t[i] = lop3_and_or(prmt(q, q4, sel), 0x000F000Fu, M);
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t ldg_nc_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));

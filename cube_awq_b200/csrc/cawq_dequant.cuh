@@ -7,9 +7,10 @@
 // row) so that a warp's loads and stores of a row are each one contiguous
 // span, and the group's zero and scales are reused across the tile's rows.
 //
-// Bit exactness: q - z is an exact small integer in every F; its product with
-// s is exact in f32 when s is f16/bf16 (at most 4 + 11 significant bits), so
-// one conversion to F rounds once, like the reference's multiply in F.
+// Bit exactness: q - z is an exact small integer in every F. For f16 / bf16
+// it is formed as (m + q) - (m + z) on packed pairs (magic-number unpack, exact)
+// and multiplied by s in F, one rounding; for f32, (float)(q - z) * s, one
+// rounding: in both cases the reference's multiply in F.
 #pragma once
 
 #include "cawq_common.cuh"
@@ -56,6 +57,7 @@ __global__ void __launch_bounds__(kDqThreads)
   uint32_t cur = 0xFFFFFFFFu;  // group whose zero word and scales are loaded
   uint32_t z = 0;
   float s[8];
+  [[maybe_unused]] uint32_t zp[4], sp[4];  // 16-bit F: (m + z) and s as packed pairs
   for (uint32_t r0 = row0; r0 < row1; r0 += kDqInflight) {
     uint32_t qv[kDqInflight];
 #pragma unroll
@@ -72,46 +74,70 @@ __global__ void __launch_bounds__(kDqThreads)
         cur = grp;
         z = __ldg(qz + (size_t)grp * npk + p);
         const T* srow = sc + (size_t)grp * n + (size_t)p * 8;
-        if constexpr (VEC && DT == kF32) {
+        if constexpr (DT != kF32) {
+          pf_pairs<DT, ORDER>(z, zp);
+          if constexpr (VEC) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(srow));
+            sp[0] = raw.x; sp[1] = raw.y; sp[2] = raw.z; sp[3] = raw.w;
+          } else {
+            const uint16_t* h = reinterpret_cast<const uint16_t*>(srow);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              sp[c] = (uint32_t)__ldg(h + 2 * c) | ((uint32_t)__ldg(h + 2 * c + 1) << 16);
+          }
+        } else if constexpr (VEC) {
           const float4 s0 = __ldg(reinterpret_cast<const float4*>(srow));
           const float4 s1 = __ldg(reinterpret_cast<const float4*>(srow) + 1);
           s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w;
           s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
-        } else if constexpr (VEC) {
-          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(srow));
-          const T* h = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) s[c] = DType<DT>::to_f32(h[c]);
         } else {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) s[c] = DType<DT>::to_f32(srow[c]);
+          for (int c = 0; c < 8; ++c) s[c] = srow[c];
         }
       }
       const uint32_t q = qv[i];
-      float v[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int sh = 4 * nibble_of_col(c, ORDER);
-        const int d = static_cast<int>((q >> sh) & 15u) - static_cast<int>((z >> sh) & 15u);
-        v[c] = __fmul_rn(static_cast<float>(d), s[c]);  // (q - z) exact, one rounding of * s
-      }
       T* orow = out + (size_t)row * n + (size_t)p * 8;
-      if constexpr (VEC && DT == kF32 && W8) {
-        stg_cs_v8(orow, v);
-      } else if constexpr (VEC && DT == kF32) {
-        stg_cs_v4(orow, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
-                                   __float_as_uint(v[2]), __float_as_uint(v[3])));
-        stg_cs_v4(orow + 4, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]),
-                                       __float_as_uint(v[6]), __float_as_uint(v[7])));
-      } else if constexpr (VEC) {
-        uint4 a;
-        T* h = reinterpret_cast<T*>(&a);
+      if constexpr (DT != kF32) {
+        // 16-bit F: (m + q) - (m + z) = q - z exactly, then one rounding of
+        // the product with s, two columns per instruction
+        using H = PfHalf2<DT>;
+        uint32_t t[4];
+        pf_pairs<DT, ORDER>(q, t);
+        uint4 v;
+        v.x = H::mul(H::sub(t[0], zp[0]), sp[0]);
+        v.y = H::mul(H::sub(t[1], zp[1]), sp[1]);
+        v.z = H::mul(H::sub(t[2], zp[2]), sp[2]);
+        v.w = H::mul(H::sub(t[3], zp[3]), sp[3]);
+        if constexpr (VEC) {
+          stg_cs_v4(orow, v);
+        } else {
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+          uint16_t* o16 = reinterpret_cast<uint16_t*>(orow);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) h[c] = DType<DT>::from_f32(v[c]);
-        stg_cs_v4(orow, a);
+          for (int c = 0; c < 4; ++c) {
+            o16[2 * c] = static_cast<uint16_t>(w4[c] & 0xFFFFu);
+            o16[2 * c + 1] = static_cast<uint16_t>(w4[c] >> 16);
+          }
+        }
       } else {
+        float v[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) orow[c] = DType<DT>::from_f32(v[c]);
+        for (int c = 0; c < 8; ++c) {
+          const int sh = 4 * nibble_of_col(c, ORDER);
+          const int d = static_cast<int>((q >> sh) & 15u) - static_cast<int>((z >> sh) & 15u);
+          v[c] = __fmul_rn(static_cast<float>(d), s[c]);  // (q - z) exact, one rounding of * s
+        }
+        if constexpr (VEC && W8) {
+          stg_cs_v8(orow, v);
+        } else if constexpr (VEC) {
+          stg_cs_v4(orow, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
+                                     __float_as_uint(v[2]), __float_as_uint(v[3])));
+          stg_cs_v4(orow + 4, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]),
+                                         __float_as_uint(v[6]), __float_as_uint(v[7])));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) orow[c] = v[c];
+        }
       }
     }
   }
