@@ -178,6 +178,10 @@ def run_ours(a, rank, local_rank, world):
     torch.cuda.set_device(dev)
     if world > 1:
         from datetime import timedelta
+        # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE") on
+        # stderr show every rank joined an N-rank communicator; nothing else
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     rows, dt = a.rows, torch.float16
@@ -651,9 +655,12 @@ def _timed_calls(call, n_it, max_over_ranks):
 
 
 def tp_fused_numbers(dev, world, max_over_ranks, reps=20):
-    """configs[4] layers with the collective fused into the GEMM's epilogue
-    (cawq_gemm_colpar_p2p / _rowpar_p2p: pushes over NVLink + flag exchange)
-    against the GEMM followed by NCCL (cawq_gemm_colpar / _rowpar): gate_up
+    """configs[4] layers with the library's own exchange over peer memory
+    (cawq_gemm_colpar_p2p / _rowpar_p2p: the GEMM epilogue pushes over NVLink
+    at decode sizes; above a few MiB per rank the GEMM writes only its own
+    buffer and the peers read it after the flag exchange, with a
+    reduce-scatter + all-gather for the row-parallel sum) against the GEMM
+    followed by NCCL (cawq_gemm_colpar / _rowpar): gate_up
     column-parallel WITH the all-gather (full [M, 57344] on every rank) and
     down row-parallel (all-reduce). us per call, max over ranks."""
     import torch
@@ -674,7 +681,8 @@ def tp_fused_numbers(dev, world, max_over_ranks, reps=20):
     L = _lib.lib()
     f16 = _lib.CAWQ_F16
     stream = torch.cuda.current_stream(dev).cuda_stream
-    res = {"n_gpus": world, "fused_p2p": "GEMM epilogue pushes to peer buffers (CUDA IPC) + flags",
+    res = {"n_gpus": world, "fused_p2p": "CUDA IPC peer buffers + flags: epilogue push at "
+           "M <= 8, peer reads (reduce-scatter + all-gather for the sum) at M = 2048",
            "nccl": "GEMM, then NCCL all-gather + interleave / fp32 all-reduce + epilogue"}
     for m in (1, 8, 2048):
         x1 = synth.make_input(m, k1, dt, dev, seed=4103)

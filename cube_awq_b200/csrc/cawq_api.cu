@@ -272,7 +272,7 @@ static bool plan_supports(const GemmProblem& p, const cawq_plan& plan, const Dev
     case CAWQ_PATH_DECODE: return decode_supports(p, plan, dev);
     case CAWQ_PATH_PREFILL: return prefill_supports(p, plan, dev);
     case CAWQ_PATH_GENERIC:
-      return p.epi == 0 && p.nrep == 0 && !(p.scw && p.out_k) && generic_supports(p);
+      return p.epi == 0 && p.nrep == 0 && generic_supports(p);
     default: return false;
   }
 }
@@ -352,8 +352,7 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
                                cawq_dtype out_dtype, cawq_order order, size_t ld_out,
                                const cawq_plan* plan, void* stream, bool module_rules,
                                int epi = 0, const QkvOut* qkv = nullptr,
-                               void* const* reps = nullptr, int nrep = 0,
-                               void* const* scat = nullptr, size_t scw = 0) {
+                               void* const* reps = nullptr, int nrep = 0) {
   if (!valid_dtype(dtype) || !valid_dtype(out_dtype))
     return fail(CAWQ_ERR_DTYPE, "dtype must be CAWQ_F32, CAWQ_F16 or CAWQ_BF16");
   if (out_dtype != dtype && out_dtype != CAWQ_F32)
@@ -400,10 +399,6 @@ static cawq_status gemm_common(const void* x, const uint32_t* qweight, const uin
   }
   for (int i = 0; i < nrep; ++i) p.rep[i] = reps[i];
   p.nrep = nrep;
-  if (scat && scw) {
-    for (int i = 0; i < 8; ++i) p.scat[i] = scat[i];
-    p.scw = scw;
-  }
   cawq_plan pl = plan ? *plan : choose_plan(p, dev);
   if (plan && !plan_supports(p, pl, dev))
     return fail(CAWQ_ERR_INVALID_ARGUMENT, "the plan cannot run this problem");
@@ -1238,6 +1233,23 @@ CAWQ_API cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t e
   if ((st = p2p_check(peers, epoch, rows * n * es, &off)) != CAWQ_OK) return st;
   if (rows == 0) return CAWQ_OK;
   if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
+  // Above 8 MiB of peer shards per rank the GEMM writes only this rank's
+  // buffer and `out`, and the peers' shards are read after the flag exchange
+  // (pull); below it the epilogue pushes the shard into every peer's buffer
+  // as its tiles finish (the same choice on every rank, from the shapes).
+  const bool pull = peers->world > 1 && rows * nl * es * (size_t)(peers->world - 1) > (8u << 20) &&
+                    reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (pull) {
+    void* rep[CAWQ_TP_MAX_PEERS] = {static_cast<uint8_t*>(out) + n0 * es};
+    void* own = static_cast<uint8_t*>(peers->base[peers->rank]) + off + n0 * es;
+    st = gemm_common(x, qweight, qzeros, scales, bias, own, rows, k, nl, group_size, dtype, dtype,
+                     CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0, nullptr, rep, 1);
+    if (st != CAWQ_OK) return st;
+    cudaError_t e = launch_p2p_colpar_pull(p2p_sync(peers, epoch), off, out, rows, n, dtype,
+                                           static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+    return CAWQ_OK;
+  }
   // this rank's columns of the gathered [rows, n] result, in every buffer
   void* dst[CAWQ_TP_MAX_PEERS];
   int nrep = 0;
@@ -1282,25 +1294,21 @@ CAWQ_API cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t e
                   plane * (size_t)(world - 1) > (4u << 20);
   if (rs) {
     const size_t es = dtype == CAWQ_F32 ? 4 : 2;
-    const size_t gath = (plane + 255) / 256 * 256;  // gather region after the partials
+    const size_t gath = (plane + 255) / 256 * 256;  // gather region after the partial
     if ((st = p2p_check(peers, epoch, gath + rows * n * es, &off)) != CAWQ_OK) return st;
     if (rows == 0) return CAWQ_OK;
     if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
-    // column chunk o of this rank's partial -> rank o's region part[rank]
-    const size_t cw = n / world;
-    void* scat[8] = {};
-    for (int o = 0; o < world; ++o)
-      scat[o] = static_cast<uint8_t*>(peers->base[o]) + off + peers->rank * rows * cw * 4;
-    st = gemm_common(x, qweight, qzeros, scales, nullptr, scat[peers->rank], rows, kl, n,
-                     group_size, dtype, CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0,
-                     nullptr, nullptr, 0, scat, cw);
+    if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
+      return fail(CAWQ_ERR_ALIGNMENT, "out must be 16-byte aligned");
+    // this rank's fp32 partial [rows, n] stays in its own buffer
+    void* own = static_cast<uint8_t*>(peers->base[peers->rank]) + off;
+    st = gemm_common(x, qweight, qzeros, scales, nullptr, own, rows, kl, n, group_size, dtype,
+                     CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
     if (st != CAWQ_OK) return st;
     P2PSync sa = p2p_sync(peers, epoch), sb = p2p_sync(peers, epoch);
     sb.fofs = 8;  // the gather's own flag words
-    const float* part = reinterpret_cast<const float*>(
-        static_cast<uint8_t*>(peers->base[peers->rank]) + off);
-    cudaError_t e = launch_p2p_rowpar_rs(sa, sb, part, off + gath, bias, out, rows, n, dtype,
-                                         static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_p2p_rowpar_pull(sa, sb, off, off + gath, bias, out, rows, n, dtype,
+                                           static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "reduce-scatter launch");
     return CAWQ_OK;
   }

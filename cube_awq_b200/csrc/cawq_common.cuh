@@ -185,19 +185,7 @@ struct OutMap {
   // replicas of a single-range output (peer buffers): rep[i] + (a - p0)
   OT* rep[7];
   uint32_t nrep;
-  // scatter: column chunk o of scw columns lives at sb[o], row stride scw
-  // (scw = 0: off); a store chunk never straddles two owners
-  OT* sb[8];
-  uint32_t scw;
   __device__ __forceinline__ OT* at(uint32_t row, uint32_t col) const {
-    if (scw) {
-      const uint32_t o = col / scw;
-      OT* b = sb[0];
-#pragma unroll
-      for (int i = 1; i < 8; ++i)
-        if (o == static_cast<uint32_t>(i)) b = sb[i];  // selects: no local copy of sb
-      return b + (size_t)row * scw + (col - o * scw);
-    }
     if (col < c1) return p0 + (size_t)row * ld0 + col;
     if (col < c2) return p1 + (size_t)row * ld1 + (col - c1);
     return p2 + (size_t)row * ld2 + (col - c2);
@@ -234,8 +222,6 @@ inline OutMap<OT> out_map(const GemmProblem& p) {
   }
   for (int i = 0; i < 7; ++i) m.rep[i] = static_cast<OT*>(p.rep[i]);
   m.nrep = static_cast<uint32_t>(p.nrep);
-  for (int i = 0; i < 8; ++i) m.sb[i] = static_cast<OT*>(p.scat[i]);
-  m.scw = static_cast<uint32_t>(p.scw);
   return m;
 }
 

@@ -1101,8 +1101,6 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   // range, f16 / bf16 activations, AWQ order
   if (p.nrep > 0 && (p.epi != 0 || p.out_k || p.dtype == kF32 || p.order != kOrderAwq))
     return false;
-  // scattered output (reduce-scatter push): plain epilogue, one output range
-  if (p.scw && (p.epi != 0 || p.out_k || p.nrep > 0)) return false;
   const size_t bands =
       (p.n + (size_t)kDecTileCols * plan.warps - 1) / ((size_t)kDecTileCols * plan.warps);
   if (bands * plan.split >= (1ull << 31)) return false;

@@ -44,11 +44,6 @@ struct GemmProblem {
   // Decode and prefill kernels, f16 / bf16 activations, AWQ order only.
   void* rep[7] = {};
   int nrep = 0;
-  // scatter of a single-range output to the owners of its column chunks (the
-  // reduce-scatter push of a row-parallel layer): columns [o scw, (o+1) scw)
-  // go to scat[o] + row * scw + (col - o scw); scw = 0: off.
-  void* scat[8] = {};
-  size_t scw = 0;
 };
 
 // Thread-local error message (cawq_last_error).
@@ -93,6 +88,8 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
 // f32 activations and scales on the tensor cores (cawq_prefill_f32.cuh);
 // prefill_supports / launch_prefill hand f32 problems to these
 bool prefill_f32_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+// CTA tile width of the f32 kernel for this plan (128 or 256)
+int prefill_f32_tile_n(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
 cudaError_t launch_prefill_f32(const GemmProblem& p, const cawq_plan& plan,
                                const DeviceInfo& dev);
 cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
@@ -127,15 +124,20 @@ struct P2PSync {
 // gathered [rows, n] result (dense in `slot`) to out (row stride ld_out).
 cudaError_t launch_p2p_colpar_finish(const P2PSync& s, const void* slot, void* out, size_t rows,
                                      size_t n, size_t ld_out, int dtype, cudaStream_t stream);
-// Reduce-scatter + all-gather finish of a row-parallel GEMM whose epilogue
-// scattered its fp32 partial to the owners of the column chunks (part =
-// this rank's region [world][rows][n/world]): flag set A, sum the own chunk,
-// push it (cast, + bias) into every gather region (at gath_off of each
-// buffer) and out; flag set B, copy the other chunks from the own gather
-// region to out. dtype f16 / bf16.
-cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, const float* part,
-                                 size_t gath_off, const void* bias, void* out, size_t rows,
-                                 size_t n, int dtype, cudaStream_t stream);
+// Pull variants for large outputs (the GEMM wrote only this rank's own
+// buffer). Column-parallel: flag exchange, then copy every other rank's
+// shard from its slot (dense [rows, n] at byte offset off) into out (row
+// stride n, 16-byte aligned, n * sizeof(F) % (16 * world) == 0).
+cudaError_t launch_p2p_colpar_pull(const P2PSync& s, size_t off, void* out, size_t rows,
+                                   size_t n, int dtype, cudaStream_t stream);
+// Row-parallel: every rank's fp32 partial [rows, n] at byte offset off of its
+// buffer; flag set A, sum the own column chunk over the partials in rank
+// order (+ bias, cast) into out and the own gather region (byte offset
+// gath_off); flag set B, copy the other chunks from the peers' gather
+// regions into out. dtype f16 / bf16, n % (32 world) == 0.
+cudaError_t launch_p2p_rowpar_pull(const P2PSync& sa, const P2PSync& sb, size_t off,
+                                   size_t gath_off, const void* bias, void* out, size_t rows,
+                                   size_t n, int dtype, cudaStream_t stream);
 // After the push of a row-parallel GEMM's fp32 partials into slot[world][rows][n]:
 // signal, wait, then out = sum over ranks (in rank order) + bias, cast to dtype.
 cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const void* bias,

@@ -48,6 +48,11 @@ constexpr int kPfBStages = 2;
 // of the MMA work, so dequantization paces the loop), 8 for 256-row tiles
 // (their registers would not fit 16)
 __host__ __device__ constexpr int pf_dq_warps(int halves) { return halves == 1 ? 16 : 8; }
+// 128-row tiles: the dequantize warps form two groups that take alternate
+// k stages, so two stages are dequantized at once. A stage's wait / load /
+// convert / store / fence / arrive chain is latency bound: with one group the
+// stage cadence stayed the same whether 8 or 16 warps shared each stage.
+__host__ __device__ constexpr int pf_dq_groups(int halves) { return halves == 1 ? 2 : 1; }
 __host__ __device__ constexpr int pf_threads(int halves) {
   return 96 + 32 * pf_dq_warps(halves);  // + X producer, MMA, W producer
 }
@@ -160,6 +165,9 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
   using L = PrefillLayout<HALVES>;
   constexpr int BM = L::kBM;
   constexpr int kPfDqWarps = pf_dq_warps(HALVES);
+  constexpr int kDqGroups = pf_dq_groups(HALVES);
+  constexpr int kGrpWarps = kPfDqWarps / kDqGroups;  // dequantize warps per stage
+  constexpr int kPasses = 16 / kGrpWarps;            // 4-row sets per warp and stage
   constexpr uint32_t kTmemCols = HALVES * kPfBN;
   using H = PfHalf2<DT>;
   extern __shared__ uint8_t smem_raw[];
@@ -209,10 +217,10 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
     }
     for (int s = 0; s < L::kWSt; ++s) {
       mbar_init(&full_w[s], 1);
-      mbar_init(&empty_w[s], 32 * kPfDqWarps);
+      mbar_init(&empty_w[s], 32 * kGrpWarps);
     }
     for (int s = 0; s < L::kBSt; ++s) {
-      mbar_init(&bready[s], 32 * kPfDqWarps);
+      mbar_init(&bready[s], 32 * kGrpWarps);
       mbar_init(&bempty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -316,11 +324,12 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
     __syncwarp();
   } else {
     // ------------------------------------------- dequant, then epilogue
-    const int dw = warp - 3;   // 0..7
-    const int q4 = lane >> 3;  // quarter of the warp -> row offset 2*q4
-    const int l = lane & 7;    // packed word l + 8a, a = 0..3
+    const int dw = warp - 3;
+    const int gw = dw % kGrpWarps;  // warp within its group
+    const int q4 = lane >> 3;       // quarter of the warp -> row offset 2*q4
+    const int l = lane & 7;         // packed word l + 8a, a = 0..3
     bool ok = true;
-    for (int kt = 0; kt < KTL; ++kt) {
+    for (int kt = dw / kGrpWarps; kt < KTL; kt += kDqGroups) {
       const int sw = kt % L::kWSt, uw = kt / L::kWSt;
       const int sb = kt % L::kBSt, ub = kt / L::kBSt;
       if (ok) ok = mbar_wait_bounded(&full_w[sw], (uint32_t)(uw & 1));
@@ -338,11 +347,11 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
           sp[a][0] = sv.x; sp[a][1] = sv.y; sp[a][2] = sv.z; sp[a][3] = sv.w;
           pf_pairs<DT, ORDER>(zrow[w], zp[a]);
         }
-        // 16 row sets of 4 rows (8-row atom x parity); each warp takes 2
-        uint32_t qv[16 / kPfDqWarps][4];
+        // 16 row sets of 4 rows (8-row atom x parity), dealt to the group
+        uint32_t qv[kPasses][4];
 #pragma unroll
-        for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
-          const int sidx = kPfDqWarps * pass + dw;
+        for (int pass = 0; pass < kPasses; ++pass) {
+          const int sidx = kGrpWarps * pass + gw;
           const int row = (sidx >> 1) * 8 + (sidx & 1) + 2 * q4;  // 0..63
           const int r8 = row & 7;
 #pragma unroll
@@ -353,8 +362,8 @@ __global__ void __launch_bounds__(pf_threads(HALVES), 1)
           }
         }
 #pragma unroll
-        for (int pass = 0; pass < 16 / kPfDqWarps; ++pass) {
-          const int sidx = kPfDqWarps * pass + dw;
+        for (int pass = 0; pass < kPasses; ++pass) {
+          const int sidx = kGrpWarps * pass + gw;
           const int row = (sidx >> 1) * 8 + (sidx & 1) + 2 * q4;
           const int r8 = row & 7;
 #pragma unroll
@@ -690,7 +699,7 @@ static size_t pf_smem(int halves) {
 }
 
 bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
-  if (p.dtype == kF32) {  // 128 x 128 tiles of the f32 kernel, no split
+  if (p.dtype == kF32) {  // the f32 kernel (128 x 128 / 256 tiles), no split
     return (plan.warps == 0 || plan.warps == 1) && prefill_f32_supports(p, plan, dev);
   }
   const int halves = pf_halves(plan);
@@ -714,7 +723,6 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
   // replicated output (tensor-parallel push): plain epilogue, one output
   // range, AWQ order
   if (p.nrep > 0 && (p.epi != 0 || p.out_k || p.order != kOrderAwq)) return false;
-  if (p.scw && (p.epi != 0 || p.out_k || p.nrep > 0)) return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
@@ -866,9 +874,11 @@ cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
   pl.tile_n = kPfBN;
   pl.stages = kPfBStages;
   pl.warps = p.rows <= 128 ? 1 : 2;
-  if (p.dtype == kF32) {  // the f32 kernel: 128 x 128 tiles, no split
+  if (p.dtype == kF32) {  // the f32 kernel: 128 x 128 or 128 x 256 tiles, no split
     pl.warps = 1;
     pl.split = 1;
+    pl.tile_n = 0;
+    pl.tile_n = prefill_f32_tile_n(p, pl, dev);
     return pl;
   }
   const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
@@ -944,6 +954,19 @@ cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev) {
 void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
                         int max_count) {
   int c = 0;
+  if (p.dtype == kF32) {
+    for (int tn : {128, 256}) {
+      cawq_plan pl = {};
+      pl.path = CAWQ_PATH_PREFILL;
+      pl.tile_n = tn;
+      pl.stages = kPfBStages;
+      pl.warps = 1;
+      pl.split = 1;
+      if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
+    }
+    *count = c;
+    return;
+  }
   for (int halves : {1, 2}) {
     for (int split : {1, 2, 4, 8}) {
       cawq_plan pl = {};

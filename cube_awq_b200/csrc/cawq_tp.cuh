@@ -208,65 +208,110 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Reduce-scatter half of the row-parallel exchange. Each rank's GEMM pushed
-// the fp32 partial of column chunk o (cw = n / world columns) into rank o's
-// buffer, region part[src][rows][cw]. After the flag exchange (set A) this
-// rank owns chunk `rank`: it sums the world partials in rank order, adds the
-// bias once, casts, and writes the result to its own output and to the same
-// place of every peer's gather region gath[rows][n] (the all-gather push).
+// ------------------------------------------------- fused tensor-parallel pull
+// For large outputs the GEMM writes only into this rank's own buffer (no
+// stores over NVLink inside the epilogue, which would stall it), and after
+// the flag exchange every rank reads what it needs from the peers' buffers:
+// 16-byte loads by every resident thread keep enough bytes in flight to fill
+// the links. A peer's slot is not overwritten before this rank's reads are
+// done: the peer writes that slot again two epochs later, after waiting for
+// this rank's flag of the epoch in between, which this rank publishes only
+// in a later kernel of its stream.
+
+__device__ __forceinline__ const uint8_t* p2p_base(const P2PSync& s, int j) {
+  return reinterpret_cast<const uint8_t*>(p2p_flags(s, j));
+}
+
+// Column-parallel all-gather: this rank's shard is already in `out` (the
+// GEMM's second output); copy every other rank's [rows, n/world] shard from
+// its slot (dense [rows, n] at byte offset `off`) into out (row stride n).
+__global__ void __launch_bounds__(256)
+    p2p_colpar_pull_kernel(const P2PSync s, size_t off, uint4* __restrict__ out, size_t rows,
+                           size_t nv) {
+  if (!p2p_signal_and_wait(s)) return;
+  const size_t cwv = nv / s.world;      // 16-byte vectors per shard row
+  const size_t per_row = nv - cwv;      // outside the own shard
+  const size_t total = rows * per_row;
+  const size_t own0 = (size_t)s.rank * cwv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / per_row;
+    size_t c = i - r * per_row;
+    if (c >= own0) c += cwv;
+    const int o = static_cast<int>(c / cwv);
+    const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, o) + off) + r * nv + c;
+    out[r * nv + c] = __ldcg(src);  // over NVLink
+  }
+}
+
+// Row-parallel reduce-scatter: every rank's fp32 partial [rows, n] is in its
+// own slot (byte offset `off`). After flag set A this rank sums column chunk
+// `rank` (n / world columns) over the world partials in rank order, adds the
+// bias once, casts, and writes it to out and to its own gather region
+// ([rows, n] of F at byte offset gath_off).
 template <int DT>
 __global__ void __launch_bounds__(256)
-    p2p_rowpar_rs_kernel(const P2PSync s, const float* __restrict__ part,
-                         const typename DType<DT>::T* __restrict__ bias,
-                         typename DType<DT>::T* __restrict__ out, size_t gath_off, size_t rows,
-                         size_t n) {
+    p2p_rowpar_pull_rs_kernel(const P2PSync s, size_t off, size_t gath_off,
+                              const typename DType<DT>::T* __restrict__ bias,
+                              typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
   using T = typename DType<DT>::T;
   if (!p2p_signal_and_wait(s)) return;
   const size_t cw = n / s.world, c0 = (size_t)s.rank * cw;
-  const size_t oct = rows * (cw / 8);  // 8 columns per item (cw % 32 == 0)
-  const size_t plane = rows * cw;
+  const size_t per_row = cw / 8;  // 8 columns per item (cw % 32 == 0)
+  const size_t oct = rows * per_row;
+  T* gath = reinterpret_cast<T*>(const_cast<uint8_t*>(p2p_base(s, s.rank)) + gath_off);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < oct;
        i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / (cw / 8), c = (i - r * (cw / 8)) * 8;
+    const size_t r = i / per_row, c = c0 + (i - r * per_row) * 8;
+    const size_t at = r * n + c;
+    float4 a[kP2PMaxWorld], b[kP2PMaxWorld];
+#pragma unroll
+    for (int j = 0; j < kP2PMaxWorld; ++j) {  // all loads in flight first
+      if (j < s.world) {
+        const float4* src = reinterpret_cast<const float4*>(p2p_base(s, j) + off) + at / 4;
+        a[j] = __ldcg(src);
+        b[j] = __ldcg(src + 1);
+      }
+    }
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < s.world; ++j) {  // rank order: the same sum on every rank
-      const float4* src = reinterpret_cast<const float4*>(part + j * plane + r * cw + c);
-      const float4 a = __ldcg(src), b = __ldcg(src + 1);  // L2: peers wrote them
-      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+#pragma unroll
+    for (int j = 0; j < kP2PMaxWorld; ++j) {  // rank order
+      if (j < s.world) {
+        acc[0] += a[j].x; acc[1] += a[j].y; acc[2] += a[j].z; acc[3] += a[j].w;
+        acc[4] += b[j].x; acc[5] += b[j].y; acc[6] += b[j].z; acc[7] += b[j].w;
+      }
     }
     uint4 v;
     T* h = reinterpret_cast<T*>(&v);
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c0 + c + e]) : 0.f));
-    const size_t at = r * n + c0 + c;
+      h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c + e]) : 0.f));
     *reinterpret_cast<uint4*>(out + at) = v;
-    for (int j = 0; j < s.world; ++j) {
-      if (j == s.rank) continue;
-      T* g = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(p2p_flags(s, j)) + gath_off);
-      *reinterpret_cast<uint4*>(g + at) = v;  // over NVLink
-    }
+    *reinterpret_cast<uint4*>(gath + at) = v;
   }
 }
 
-// All-gather half: after the flag exchange (set B) every peer's chunk is in
-// this rank's gather region; copy them (not this rank's own) to the output.
+// Row-parallel all-gather: after flag set B every rank's chunk is in its
+// gather region; copy the other ranks' chunks into out.
 template <int DT>
 __global__ void __launch_bounds__(256)
-    p2p_rowpar_ag_kernel(const P2PSync s, const typename DType<DT>::T* __restrict__ gath,
-                         typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
+    p2p_rowpar_pull_ag_kernel(const P2PSync s, size_t gath_off, typename DType<DT>::T* __restrict__ out,
+                              size_t rows, size_t n) {
   if (!p2p_signal_and_wait(s)) return;
-  const size_t cw = n / s.world;
-  const size_t per_row = (n - cw) / 8;  // 8-element vectors outside the own chunk
+  const size_t nv = n / 8;              // 16-byte vectors per row (8 elements)
+  const size_t cwv = nv / s.world;
+  const size_t per_row = nv - cwv;
   const size_t total = rows * per_row;
+  const size_t own0 = (size_t)s.rank * cwv;
+  uint4* o4 = reinterpret_cast<uint4*>(out);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / per_row;
-    size_t c = (i - r * per_row) * 8;
-    if (c >= (size_t)s.rank * cw) c += cw;  // skip the own chunk
-    const size_t at = r * n + c;
-    *reinterpret_cast<uint4*>(out + at) = __ldcg(reinterpret_cast<const uint4*>(gath + at));
+    size_t c = i - r * per_row;
+    if (c >= own0) c += cwv;
+    const int o = static_cast<int>(c / cwv);
+    const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, o) + gath_off) + r * nv + c;
+    o4[r * nv + c] = __ldcg(src);  // over NVLink
   }
 }
 
@@ -314,24 +359,32 @@ cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const 
   return cudaGetLastError();
 }
 
-cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, const float* part,
-                                 size_t gath_off, const void* bias, void* out, size_t rows,
-                                 size_t n, int dtype, cudaStream_t stream) {
+cudaError_t launch_p2p_colpar_pull(const P2PSync& s, size_t off, void* out, size_t rows,
+                                   size_t n, int dtype, cudaStream_t stream) {
+  const size_t es = dtype == kF32 ? 4 : 2;
+  const size_t nv = n * es / 16;
+  p2p_colpar_pull_kernel<<<p2p_blocks(rows * (nv - nv / s.world)), 256, 0, stream>>>(
+      s, off, static_cast<uint4*>(out), rows, nv);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_p2p_rowpar_pull(const P2PSync& sa, const P2PSync& sb, size_t off,
+                                   size_t gath_off, const void* bias, void* out, size_t rows,
+                                   size_t n, int dtype, cudaStream_t stream) {
   const size_t cw = n / sa.world;
   const unsigned b1 = p2p_blocks(rows * cw / 8);
   const unsigned b2 = p2p_blocks(rows * (n - cw) / 8);
-  const void* gath = reinterpret_cast<const uint8_t*>(sa.flags[sa.rank]) + gath_off;
   if (dtype == kF16) {
-    p2p_rowpar_rs_kernel<kF16><<<b1, 256, 0, stream>>>(
-        sa, part, static_cast<const __half*>(bias), static_cast<__half*>(out), gath_off, rows, n);
-    p2p_rowpar_ag_kernel<kF16><<<b2, 256, 0, stream>>>(
-        sb, static_cast<const __half*>(gath), static_cast<__half*>(out), rows, n);
+    p2p_rowpar_pull_rs_kernel<kF16><<<b1, 256, 0, stream>>>(
+        sa, off, gath_off, static_cast<const __half*>(bias), static_cast<__half*>(out), rows, n);
+    p2p_rowpar_pull_ag_kernel<kF16><<<b2, 256, 0, stream>>>(sb, gath_off,
+                                                            static_cast<__half*>(out), rows, n);
   } else {
-    p2p_rowpar_rs_kernel<kBF16><<<b1, 256, 0, stream>>>(
-        sa, part, static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out),
-        gath_off, rows, n);
-    p2p_rowpar_ag_kernel<kBF16><<<b2, 256, 0, stream>>>(
-        sb, static_cast<const __nv_bfloat16*>(gath), static_cast<__nv_bfloat16*>(out), rows, n);
+    p2p_rowpar_pull_rs_kernel<kBF16><<<b1, 256, 0, stream>>>(
+        sa, off, gath_off, static_cast<const __nv_bfloat16*>(bias),
+        static_cast<__nv_bfloat16*>(out), rows, n);
+    p2p_rowpar_pull_ag_kernel<kBF16><<<b2, 256, 0, stream>>>(
+        sb, gath_off, static_cast<__nv_bfloat16*>(out), rows, n);
   }
   return cudaGetLastError();
 }

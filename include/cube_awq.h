@@ -508,14 +508,20 @@ cawq_status cawq_tp_p2p_create(const cawq_tp_comm* comm, size_t bytes, int timeo
 cawq_status cawq_tp_p2p_destroy(cawq_tp_peers* peers);
 
 /*
- * Column-parallel layer with the all-gather in the epilogue: the same
+ * Column-parallel layer with the all-gather over peer memory: the same
  * shards and result as cawq_gemm_colpar (out [rows, n] in full on every
- * rank), f16 / bf16. The local GEMM writes its [rows, n/world] columns into
- * the slot of every rank's buffer; the finish kernel copies the gathered
- * slot to `out`. Needs rows * n * sizeof(F) bytes per slot. Every rank makes
- * the same fused calls in the same order, each with the next `epoch` of
- * this peer table (1, 2, 3, ...: one counter per table, shared by all
- * layers that use it).
+ * rank), f16 / bf16. Two exchanges, chosen from the shapes alone (the same
+ * on every rank):
+ *   - push (up to 8 MiB of peer shards per rank, or `out` not 16-byte
+ *     aligned): the local GEMM's epilogue writes its [rows, n/world] columns
+ *     into the slot of every rank's buffer as its tiles finish; after the
+ *     flag exchange each rank copies its gathered slot to `out`;
+ *   - pull (larger): the local GEMM writes its columns into its own slot and
+ *     into `out`; after the flag exchange each rank reads the other ranks'
+ *     columns from their slots into `out`.
+ * Needs rows * n * sizeof(F) bytes per slot. Every rank makes the same fused
+ * calls in the same order, each with the next `epoch` of this peer table
+ * (1, 2, 3, ...: one counter per table, shared by all layers that use it).
  */
 cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,
                                  const uint32_t* qweight, const uint32_t* qzeros,
@@ -523,22 +529,25 @@ cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, con
                                  size_t k, size_t n, size_t group_size, cawq_dtype dtype,
                                  void* stream);
 /*
- * Row-parallel layer with the all-reduce in the epilogue: the same shards
+ * Row-parallel layer with the all-reduce over peer memory: the same shards
  * and result as cawq_gemm_rowpar, f16 / bf16. Two exchanges, chosen from the
  * shapes alone (the same on every rank):
- *   - one-shot (when world * rows * n * 4 bytes per rank is at most 4 MiB,
- *     or n is not a multiple of 32 * world): the local GEMM writes its fp32
- *     partial [rows, n] into plane [rank] of the slot of every rank's buffer;
- *     each rank then sums the world planes in rank order, adds the bias once
- *     and casts. Needs world * rows * n * 4 bytes per slot;
- *   - reduce-scatter + all-gather (larger exchanges): the local GEMM writes
- *     column chunk o (n / world columns) of its fp32 partial into rank o's
- *     slot only; rank o sums its chunk over the world partials in rank
- *     order, adds the bias, casts, and writes the chunk into every rank's
- *     gather region; after a second flag exchange (flag words 8..15 of the
- *     header) each rank copies the other chunks to `out`. Each rank sends
- *     (world - 1) / world of a plane in fp32 and of the result in F. Needs
- *     rows * n * 4 (rounded up to 256) + rows * n * sizeof(F) bytes per slot.
+ *   - one-shot (when (world - 1) * rows * n * 4 bytes is at most 4 MiB, or
+ *     n is not a multiple of 32 * world): the local GEMM's epilogue writes
+ *     its fp32 partial [rows, n] into plane [rank] of the slot of every
+ *     rank's buffer; each rank then sums the world planes in rank order,
+ *     adds the bias once and casts. Needs world * rows * n * 4 bytes per
+ *     slot;
+ *   - reduce-scatter + all-gather (larger; `out` must be 16-byte aligned):
+ *     the local GEMM writes its fp32 partial [rows, n] into its own slot;
+ *     after the flag exchange rank o reads column chunk o (n / world
+ *     columns) of every rank's partial, sums them in rank order, adds the
+ *     bias, casts, and writes the chunk to `out` and to its own gather
+ *     region; after a second flag exchange (flag words 8..15 of the header)
+ *     each rank reads the other chunks from the other ranks' gather regions.
+ *     Each rank receives (world - 1) / world of a plane in fp32 and of the
+ *     result in F. Needs rows * n * 4 (rounded up to 256) + rows * n *
+ *     sizeof(F) bytes per slot.
  * Epochs as for cawq_gemm_colpar_p2p.
  */
 cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,

@@ -289,6 +289,9 @@ def test_planner_picks_prefill_for_large_m(cuda_device):
     assert cawq.plan_get(1, 4096, 4096, 128, torch.float16)["path"] == PATH_DECODE
     # f32 activations: the tcgen05 kernel with x split into bf16 hi + lo
     assert cawq.plan_get(2048, 4096, 4096, 128, torch.float32)["path"] == PATH_PREFILL
+    # 128 x 256 tiles once they fill the GPU, else 128 x 128
+    assert cawq.plan_get(2048, 4096, 4096, 128, torch.float32)["tile_n"] == 256
+    assert cawq.plan_get(512, 4096, 4096, 128, torch.float32)["tile_n"] == 128
     # ... which needs whole 64-row groups; the CUDA-core kernel takes the rest
     assert cawq.plan_get(2048, 4096, 4096, 32, torch.float32)["path"] == PATH_GENERIC
 
@@ -297,16 +300,17 @@ PREFILL_F32_SHAPES = [(17, 128, 256, 64), (128, 512, 512, 128), (200, 512, 800, 
                       (37, 1024, 4160, 64), (513, 2048, 1024, 256), (129, 4096, 4096, 128)]
 
 
+@pytest.mark.parametrize("tile_n", [128, 256])
 @pytest.mark.parametrize("rows,k,n,g", PREFILL_F32_SHAPES)
-def test_prefill_f32_tcgen05_parity(cuda_device, rows, k, n, g):
+def test_prefill_f32_tcgen05_parity(cuda_device, rows, k, n, g, tile_n):
     # f32 x and scales on the tensor cores: exact (q - z) weights, x as bf16
     # hi + lo, each group's sum scaled in fp32; N = 800 / 4160 end in a
-    # partial 128-column tile. The north star's bound against the exact sum,
-    # and against the reference's own f32 numerics.
+    # partial column tile (of 128 or 256). The north star's bound against the
+    # exact sum, and against the reference's own f32 numerics.
     x, qw, qz, s, _ = random_awq(k, n, g, "f32", rows, seed=rows + n + 1)
     t = lambda a, d: to_torch(a, d, cuda_device)
     y = cawq.gemm(t(x, "f32"), t(qw, "u32"), t(qz, "u32"), t(s, "f32"), g,
-                  plan={"path": PATH_PREFILL})
+                  plan={"path": PATH_PREFILL, "tile_n": tile_n})
     torch.cuda.synchronize()
     got = y.cpu().numpy().astype(np.float64)
     ref = oracle.gemm_f64(x, qw, qz, s, g, dtype="f32", deq_round=False)
@@ -315,15 +319,16 @@ def test_prefill_f32_tcgen05_parity(cuda_device, rows, k, n, g):
     assert max_rel_err(got, ref_numerics) <= GEMM_TOL["f32"]
 
 
-def test_prefill_f32_bias_natural_order_ld_and_determinism(cuda_device):
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_prefill_f32_bias_natural_order_ld_and_determinism(cuda_device, tile_n):
     rows, k, n, g = 300, 1024, 512, 128
     x, qw, qz, s, b = random_awq(k, n, g, "f32", rows, seed=19)
     t = lambda a, d: to_torch(a, d, cuda_device)
     full = torch.zeros(rows, 2 * n, dtype=torch.float32, device=cuda_device)
     args = (t(x, "f32"), t(qw, "u32"), t(qz, "u32"), t(s, "f32"), g)
-    cawq.gemm(*args, bias=t(b, "f32"), out=full[:, n:], order="natural",
-              plan={"path": PATH_PREFILL})
-    y2 = cawq.gemm(*args, bias=t(b, "f32"), order="natural", plan={"path": PATH_PREFILL})
+    plan = {"path": PATH_PREFILL, "tile_n": tile_n}
+    cawq.gemm(*args, bias=t(b, "f32"), out=full[:, n:], order="natural", plan=plan)
+    y2 = cawq.gemm(*args, bias=t(b, "f32"), order="natural", plan=plan)
     torch.cuda.synchronize()
     ref = oracle.gemm_f64(x, qw, qz, s, g, bias=b, dtype="f32", order="natural",
                           deq_round=False)

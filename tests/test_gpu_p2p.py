@@ -125,44 +125,79 @@ def test_rejects_small_buffers_and_epoch_zero(cuda_device):
         _lib.CAWQ_ERR_INVALID_ARGUMENT
 
 
+def _two_rank_stand_in(dev, nbytes, sets=(1,)):
+    # rank 0 of a two-rank table whose "peer" buffer is a second local buffer;
+    # rank 1's flag word of every set used is preset far ahead, so the waits
+    # pass at once
+    own, other = _buffer(dev, nbytes), _buffer(dev, nbytes)
+    for w in sets:
+        own.view(torch.int32)[w] = 1 << 20
+    return own, other, tp.TPPeers.from_pointers(2, 0, [own.data_ptr(), other.data_ptr()], nbytes)
+
+
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_rowpar_reduce_scatter_push_on_one_gpu(cuda_device, dtype):
-    # Rank 0 of a two-rank table whose "peer" buffer is a second local buffer;
-    # both of its flag sets for rank 1 (words 1 and 8 + 1) are preset far
-    # ahead, so the waits pass at once. rows * n * 4 bytes above 4 MiB take the
-    # reduce-scatter path: the GEMM scatters its fp32 partial by column chunk
-    # (the peer's chunk to the peer's region part[0]), this rank sums its own
-    # chunk over the planes (the peer's plane here is empty), adds the bias,
-    # writes it to the output and pushes it into the peer's gather region;
-    # the other chunk of the output comes from this rank's own gather region,
-    # which no peer wrote (zeros).
+def test_colpar_pull_on_one_gpu(cuda_device, dtype):
+    # Above 8 MiB of peer shards the column-parallel GEMM writes only its own
+    # buffer and the output, and reads the peer's shard from the peer's slot
+    # after the flag exchange. The stand-in peer's slot holds a known shard.
+    rows, k, n, g = 2100, 512, 4096, 128
+    es = 2
+    slot_need = rows * n * es
+    own, other, peers = _two_rank_stand_in(cuda_device, 256 + 2 * (slot_need + 4096))
+    x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed=41)
+    t = lambda a, d: to_torch(a, d, cuda_device)
+    x, qw, qz, s, b = t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), t(b, dtype)
+    off = 256 + peers.slot_bytes                   # epoch 1: slot 1
+    tdt = x.dtype
+    peer_slot = other[off:off + slot_need].view(tdt).view(rows, n)
+    peer_slot.copy_(torch.randn(rows, n, device=cuda_device).to(tdt))
+    col = tp.ColumnParallelAWQLinear(qw, qz, s, b, backend="p2p", peers=peers)
+    y = col(x)
+    torch.cuda.synchronize()
+    assert cawq.device_error() == 0
+    half = n // 2
+    mine = cawq.gemm(x, col.qweight, col.qzeros, col.scales, g, bias=col.bias)
+    assert torch.equal(y[:, :half], mine)
+    assert torch.equal(y[:, half:], peer_slot[:, half:])
+    own_slot = own[off:off + slot_need].view(tdt).view(rows, n)
+    assert torch.equal(own_slot[:, :half], mine)   # what the peer would read
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_rowpar_reduce_scatter_pull_on_one_gpu(cuda_device, dtype):
+    # rows * n * 4 bytes above 4 MiB take the reduce-scatter: this rank's
+    # fp32 partial stays in its own slot; after flag set A it sums its column
+    # chunk over its own and the peer's partial (rank order), adds the bias,
+    # writes the output and its own gather region; after flag set B it reads
+    # the other chunk from the peer's gather region. The stand-in peer holds
+    # a known partial and a known gathered chunk.
     rows, k, n, g = 600, 1024, 2048, 128
     plane = rows * n * 4
     gath = (plane + 255) // 256 * 256
     es = 2
     slot = gath + rows * n * es
-    nbytes = 256 + 2 * (slot + 4096)
-    own, other = _buffer(cuda_device, nbytes), _buffer(cuda_device, nbytes)
-    own.view(torch.int32)[1] = 1 << 20
-    own.view(torch.int32)[9] = 1 << 20
-    peers = tp.TPPeers.from_pointers(2, 0, [own.data_ptr(), other.data_ptr()], nbytes)
+    own, other, peers = _two_rank_stand_in(cuda_device, 256 + 2 * (slot + 4096), sets=(1, 9))
     x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed=31)
     t = lambda a, d: to_torch(a, d, cuda_device)
     x, qw, qz, s, b = t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), t(b, dtype)
+    tdt = x.dtype
+    off = 256 + peers.slot_bytes                   # epoch 1: slot 1
+    peer_part = other[off:off + plane].view(torch.float32).view(rows, n)
+    peer_part.copy_(torch.randn(rows, n, device=cuda_device))
+    peer_gath = other[off + gath:off + gath + rows * n * es].view(tdt).view(rows, n)
+    peer_gath.copy_(torch.randn(rows, n, device=cuda_device).to(tdt))
     row = tp.RowParallelAWQLinear(qw, qz, s, b, backend="p2p", peers=peers,
                                   input_is_parallel=False)
-    y = row(x)                                     # epoch 1: slot 1
+    y = row(x)
     torch.cuda.synchronize()
     assert cawq.device_error() == 0
     part = cawq.gemm(x[:, :k // 2].contiguous(), row.qweight, row.qzeros, row.scales, g,
                      out_dtype=torch.float32)
     cw = n // 2
-    off = 256 + peers.slot_bytes                   # slot 1
-    want0 = (part[:, :cw] + b[:cw].float()).to(x.dtype)
+    want0 = ((part[:, :cw] + peer_part[:, :cw]) + b[:cw].float()).to(tdt)
     assert torch.equal(y[:, :cw], want0)
-    assert float(y[:, cw:].float().abs().max()) == 0.0
-    peer_part = other[off:off + rows * cw * 4].view(torch.float32).view(rows, cw)
-    assert torch.equal(peer_part, part[:, cw:])
-    peer_gath = other[off + gath:off + gath + rows * n * es].view(x.dtype).view(rows, n)
-    assert torch.equal(peer_gath[:, :cw], want0)
-    assert float(peer_gath[:, cw:].float().abs().max()) == 0.0
+    assert torch.equal(y[:, cw:], peer_gath[:, cw:])
+    own_part = own[off:off + plane].view(torch.float32).view(rows, n)
+    assert torch.equal(own_part, part)             # what the peer would read
+    own_gath = own[off + gath:off + gath + rows * n * es].view(tdt).view(rows, n)
+    assert torch.equal(own_gath[:, :cw], want0)

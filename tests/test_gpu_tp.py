@@ -6,9 +6,11 @@ unsharded layer, with torch.distributed's NCCL and with the library's own
 communicator (cawq_gemm_colpar / cawq_gemm_rowpar), and with the collective
 fused into the GEMM's epilogue (cawq_gemm_colpar_p2p / _rowpar_p2p, also
 compared bit for bit with the NCCL path). Rows 1 and 8 run the decode kernel
-(rows = 1 gathers in place), 300 and 600 the tensor-core kernel; at 600 rows
-the fused row-parallel layer reduce-scatters and all-gathers instead of
-pushing whole partials.
+(rows = 1 gathers in place), 300, 600 and 2100 the tensor-core kernel; from
+600 rows the fused row-parallel layer reduce-scatters and all-gathers
+(reading the peers' buffers) instead of pushing whole partials, and at 2100
+rows the fused column-parallel layer reads the peer's shard instead of
+pushing its own.
 """
 
 import multiprocessing as mp
@@ -21,10 +23,11 @@ import tp_worker
 
 pytestmark = pytest.mark.gpu
 
-# the last case exchanges more than 4 MiB per rank, so the fused row-parallel
-# layer takes its reduce-scatter + all-gather path
+# the last two cases exchange more than 4 MiB per rank, so the fused
+# row-parallel layer takes its reduce-scatter + all-gather path; the last one
+# has more than 8 MiB of peer shards, so the column-parallel layer pulls
 CASES = [(1024, 2048, 128, 1), (1024, 2048, 128, 8), (2048, 1024, 64, 300),
-         (2048, 2048, 128, 600)]
+         (2048, 2048, 128, 600), (1024, 4096, 128, 2100)]
 
 
 def _free_port() -> int:
