@@ -178,10 +178,9 @@ def run_ours(a, rank, local_rank, world):
     torch.cuda.set_device(dev)
     if world > 1:
         from datetime import timedelta
-        # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE") on
-        # stderr show every rank joined an N-rank communicator; nothing else
+        # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE")
+        # show that every rank joined an N-rank communicator
         os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     rows, dt = a.rows, torch.float16
@@ -714,6 +713,9 @@ def tp_fused_numbers(dev, world, max_over_ranks, reps=20):
         res[f"M={m}"] = r
         del x1, x2, out1, out2, ws, part
     torch.cuda.synchronize()
+    # bit 1 set on any rank = a flag wait gave up (the fused numbers are void)
+    import cube_awq_b200 as cawq
+    res["device_error_word"] = int(max_over_ranks(float(cawq.device_error())))
     if world > 1:
         import torch.distributed as dist
         dist.barrier()  # every rank's last fused call has completed
