@@ -178,9 +178,6 @@ def run_ours(a, rank, local_rank, world):
     torch.cuda.set_device(dev)
     if world > 1:
         from datetime import timedelta
-        # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE")
-        # show that every rank joined an N-rank communicator
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     rows, dt = a.rows, torch.float16
@@ -949,6 +946,11 @@ def run_reference(a, rank, world):
 def main():
     a = parse()
     rank, local_rank, world = dist_env()
+    if world > 1:
+        # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE")
+        # show that every rank joined an N-rank communicator; NCCL reads this
+        # once, at its first call, so it is set before torch is imported
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
     if a.impl == "reference":
         run_reference(a, rank, world)
     elif a.workload == "prefill":

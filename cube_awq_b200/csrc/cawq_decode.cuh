@@ -134,7 +134,12 @@ __host__ __device__ constexpr int dec_max_consumers(int mt) { return mt == 1 ? 1
 // 2j + 1 of a band are a gate block and its up block); the kernel writes
 // silu(gate) * up (bias, if any, added to both first) to an [rows, n / 2]
 // output, column (band column base) / 2 + pair index.
-template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0>
+//
+// PK (f32 X, rows <= 4): the hi and lo bf16 parts of X row j go to B columns
+// 2j and 2j + 1 of one MMA instead of two MMAs over columns j; the fold works
+// column by column as before, and the two columns of a row are added once,
+// after the last group.
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0, bool PK = false>
 __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
                                      : dec_max_consumers(MT) * 32 + 32,
                                   I8 ? 3 : 1)
@@ -590,7 +595,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     uint32_t xld[MT][2];  // ldmatrix row addresses, step pairs 0 and 1 (16-bit X)
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      const int xr = 8 * m + gq;
+      const int xr = PK ? (gq >> 1) : 8 * m + gq;  // PK: B column gq holds row gq / 2
       xrow[m] = xr * 128;
       x7[m] = static_cast<uint32_t>(xr & 7);
       const int lr = lane & 7, li = lane >> 3;
@@ -710,8 +715,13 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
           const __nv_bfloat162 hi = __floats2bfloat162_rn(xv.x, xv.y);
           const __nv_bfloat162 lo =
               __floats2bfloat162_rn(xv.x - __low2float(hi), xv.y - __high2float(hi));
-          bh[m][h2] = *reinterpret_cast<const uint32_t*>(&hi);
-          bl[m][h2] = *reinterpret_cast<const uint32_t*>(&lo);
+          if constexpr (PK) {  // column gq: the hi part of row gq / 2, or its lo part
+            bh[m][h2] = (gq & 1) ? *reinterpret_cast<const uint32_t*>(&lo)
+                                 : *reinterpret_cast<const uint32_t*>(&hi);
+          } else {
+            bh[m][h2] = *reinterpret_cast<const uint32_t*>(&hi);
+            bl[m][h2] = *reinterpret_cast<const uint32_t*>(&lo);
+          }
         }
       }
     };
@@ -729,7 +739,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
         mma(Dx[m], kOnes, kOnes, kOnes, kOnes, bh[m][0], bh[m][1], zero_tag);
-        if constexpr (DT == kF32)
+        if constexpr (DT == kF32 && !PK)
           mma_16816<true>(Dx[m], kOnes, kOnes, kOnes, kOnes, bl[m][0], bl[m][1]);
       }
       [[maybe_unused]] uint32_t Rh[4];
@@ -753,7 +763,8 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           mma(D[m][n], a[0], a[1], a[2], a[3], bh[m][0], bh[m][1], zero_tag);
-          if constexpr (DT == kF32) mma_16816<true>(D[m][n], a[0], a[1], a[2], a[3], bl[m][0], bl[m][1]);
+          if constexpr (DT == kF32 && !PK)
+            mma_16816<true>(D[m][n], a[0], a[1], a[2], a[3], bl[m][0], bl[m][1]);
         }
       }
     };
@@ -869,6 +880,13 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       }
     }
 
+    if constexpr (PK) {  // columns 2t (hi) + 2t + 1 (lo) = row t
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        tot[0][n][0] += tot[0][n][1];
+        tot[0][n][2] += tot[0][n][3];
+      }
+    }
     // Lanes gq and gq ^ 1 hold the two nibble halves of words wA and wB: swap
     // one slot so that each lane has all 8 columns of one word.
     oword = npar ? wB : wA;
@@ -958,9 +976,9 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
 #pragma unroll
-        for (int e = 0; e < (I8 ? 1 : 2); ++e) {
-          // integer path: lane row t; else rows 8m + 2t + e
-          const uint32_t row = static_cast<uint32_t>(I8 ? t : 8 * m + 2 * t + e);
+        for (int e = 0; e < (I8 || PK ? 1 : 2); ++e) {
+          // integer and packed paths: lane row t; else rows 8m + 2t + e
+          const uint32_t row = static_cast<uint32_t>(I8 || PK ? t : 8 * m + 2 * t + e);
           if (row >= rows_eff) continue;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -983,8 +1001,8 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
 #pragma unroll
-      for (int e = 0; e < (I8 ? 1 : 2); ++e) {
-        const uint32_t row = static_cast<uint32_t>(I8 ? t : 8 * m + 2 * t + e);
+      for (int e = 0; e < (I8 || PK ? 1 : 2); ++e) {
+        const uint32_t row = static_cast<uint32_t>(I8 || PK ? t : 8 * m + 2 * t + e);
         if (row >= rows_eff) continue;
         const float* v = outv[m][e];  // this lane's 8 consecutive columns
         const uint32_t col8 = static_cast<uint32_t>(strip * kDecTileCols + 8 * oword);
@@ -1107,7 +1125,7 @@ bool decode_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceIn
   return decode_smem(p, plan) <= dev.smem_optin && dev.cc_major == 10;
 }
 
-template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0>
+template <int DT, int ODT, int ORDER, int MT, bool GA, bool I8, int EPI = 0, bool PK = false>
 static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) {
   using L = DecodeLayout<DT, MT>;
   using T = typename DType<DT>::T;
@@ -1126,7 +1144,7 @@ static cudaError_t launch_decode_t(const GemmProblem& p, const cawq_plan& plan) 
                  CU_TENSOR_MAP_SWIZZLE_128B)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA, I8, EPI>;
+  auto kern = decode_kernel<DT, ODT, ORDER, MT, GA, I8, EPI, PK>;
   const size_t smem = decode_smem(p, plan);
   // function attributes are per process; set each once (a repeat is harmless)
   static size_t smem_set = 0;
@@ -1205,6 +1223,11 @@ static cudaError_t launch_decode_m(const GemmProblem& p, const cawq_plan& plan) 
   }
   if constexpr (DT != kF32) {
     if (decode_use_i8(p, plan)) return launch_decode_t<DT, ODT, ORDER, 1, true, true>(p, plan);
+  } else {
+    if (p.rows <= 4) {  // hi / lo of X in the columns of one MMA
+      return ga ? launch_decode_t<DT, ODT, ORDER, 1, true, false, 0, true>(p, plan)
+                : launch_decode_t<DT, ODT, ORDER, 1, false, false, 0, true>(p, plan);
+    }
   }
   if (decode_mt(p.rows) == 1) {
     return ga ? launch_decode_t<DT, ODT, ORDER, 1, true, false>(p, plan)

@@ -222,6 +222,43 @@ __device__ __forceinline__ const uint8_t* p2p_base(const P2PSync& s, int j) {
   return reinterpret_cast<const uint8_t*>(p2p_flags(s, j));
 }
 
+// Copies, for every row, the column chunks of the other ranks (chunk o =
+// vectors [o cwv, (o+1) cwv) of a row of nv 16-byte vectors) from rank o's
+// buffer at byte offset `off` (dense [rows, nv]) into out (same layout).
+// Four loads per thread are in flight before their stores: a load from a
+// peer's memory takes microseconds under load, and one at a time left the
+// links mostly idle.
+__device__ __forceinline__ void p2p_pull_other_chunks(const P2PSync& s, size_t off,
+                                                      uint4* __restrict__ out, size_t rows,
+                                                      size_t nv) {
+  constexpr int kU = 4;
+  const size_t cwv = nv / s.world;      // 16-byte vectors per chunk row
+  const size_t per_row = nv - cwv;      // outside the own chunk
+  const size_t total = rows * per_row;
+  const size_t own0 = (size_t)s.rank * cwv;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += kU * stride) {
+    uint4 v[kU];
+    size_t at[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const size_t i = i0 + u * stride;
+      at[u] = ~static_cast<size_t>(0);
+      if (i < total) {
+        const size_t r = i / per_row;
+        size_t c = i - r * per_row;
+        if (c >= own0) c += cwv;
+        const int o = static_cast<int>(c / cwv);
+        at[u] = r * nv + c;
+        v[u] = __ldcg(reinterpret_cast<const uint4*>(p2p_base(s, o) + off) + at[u]);  // NVLink
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (at[u] != ~static_cast<size_t>(0)) out[at[u]] = v[u];
+  }
+}
+
 // Column-parallel all-gather: this rank's shard is already in `out` (the
 // GEMM's second output); copy every other rank's [rows, n/world] shard from
 // its slot (dense [rows, n] at byte offset `off`) into out (row stride n).
@@ -229,19 +266,7 @@ __global__ void __launch_bounds__(256)
     p2p_colpar_pull_kernel(const P2PSync s, size_t off, uint4* __restrict__ out, size_t rows,
                            size_t nv) {
   if (!p2p_signal_and_wait(s)) return;
-  const size_t cwv = nv / s.world;      // 16-byte vectors per shard row
-  const size_t per_row = nv - cwv;      // outside the own shard
-  const size_t total = rows * per_row;
-  const size_t own0 = (size_t)s.rank * cwv;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / per_row;
-    size_t c = i - r * per_row;
-    if (c >= own0) c += cwv;
-    const int o = static_cast<int>(c / cwv);
-    const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, o) + off) + r * nv + c;
-    out[r * nv + c] = __ldcg(src);  // over NVLink
-  }
+  p2p_pull_other_chunks(s, off, out, rows, nv);
 }
 
 // Row-parallel reduce-scatter: every rank's fp32 partial [rows, n] is in its
@@ -260,34 +285,49 @@ __global__ void __launch_bounds__(256)
   const size_t per_row = cw / 8;  // 8 columns per item (cw % 32 == 0)
   const size_t oct = rows * per_row;
   T* gath = reinterpret_cast<T*>(const_cast<uint8_t*>(p2p_base(s, s.rank)) + gath_off);
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < oct;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / per_row, c = c0 + (i - r * per_row) * 8;
-    const size_t at = r * n + c;
-    float4 a[kP2PMaxWorld], b[kP2PMaxWorld];
+  // two items per thread, all their loads in flight before any sum
+  constexpr int kU = 2;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < oct; i0 += kU * stride) {
+    float4 a[kU][kP2PMaxWorld], b[kU][kP2PMaxWorld];
+    size_t at[kU];
 #pragma unroll
-    for (int j = 0; j < kP2PMaxWorld; ++j) {  // all loads in flight first
-      if (j < s.world) {
-        const float4* src = reinterpret_cast<const float4*>(p2p_base(s, j) + off) + at / 4;
-        a[j] = __ldcg(src);
-        b[j] = __ldcg(src + 1);
+    for (int u = 0; u < kU; ++u) {
+      const size_t i = i0 + u * stride;
+      at[u] = ~static_cast<size_t>(0);
+      if (i < oct) {
+        const size_t r = i / per_row, c = c0 + (i - r * per_row) * 8;
+        at[u] = r * n + c;
+#pragma unroll
+        for (int j = 0; j < kP2PMaxWorld; ++j) {
+          if (j < s.world) {
+            const float4* src = reinterpret_cast<const float4*>(p2p_base(s, j) + off) + at[u] / 4;
+            a[u][j] = __ldcg(src);
+            b[u][j] = __ldcg(src + 1);
+          }
+        }
       }
     }
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < kP2PMaxWorld; ++j) {  // rank order
-      if (j < s.world) {
-        acc[0] += a[j].x; acc[1] += a[j].y; acc[2] += a[j].z; acc[3] += a[j].w;
-        acc[4] += b[j].x; acc[5] += b[j].y; acc[6] += b[j].z; acc[7] += b[j].w;
+    for (int u = 0; u < kU; ++u) {
+      if (at[u] == ~static_cast<size_t>(0)) continue;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < kP2PMaxWorld; ++j) {  // rank order
+        if (j < s.world) {
+          acc[0] += a[u][j].x; acc[1] += a[u][j].y; acc[2] += a[u][j].z; acc[3] += a[u][j].w;
+          acc[4] += b[u][j].x; acc[5] += b[u][j].y; acc[6] += b[u][j].z; acc[7] += b[u][j].w;
+        }
       }
-    }
-    uint4 v;
-    T* h = reinterpret_cast<T*>(&v);
+      const size_t c = at[u] % n;
+      uint4 v;
+      T* h = reinterpret_cast<T*>(&v);
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c + e]) : 0.f));
-    *reinterpret_cast<uint4*>(out + at) = v;
-    *reinterpret_cast<uint4*>(gath + at) = v;
+      for (int e = 0; e < 8; ++e)
+        h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c + e]) : 0.f));
+      *reinterpret_cast<uint4*>(out + at[u]) = v;
+      *reinterpret_cast<uint4*>(gath + at[u]) = v;
+    }
   }
 }
 
@@ -298,21 +338,7 @@ __global__ void __launch_bounds__(256)
     p2p_rowpar_pull_ag_kernel(const P2PSync s, size_t gath_off, typename DType<DT>::T* __restrict__ out,
                               size_t rows, size_t n) {
   if (!p2p_signal_and_wait(s)) return;
-  const size_t nv = n / 8;              // 16-byte vectors per row (8 elements)
-  const size_t cwv = nv / s.world;
-  const size_t per_row = nv - cwv;
-  const size_t total = rows * per_row;
-  const size_t own0 = (size_t)s.rank * cwv;
-  uint4* o4 = reinterpret_cast<uint4*>(out);
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / per_row;
-    size_t c = i - r * per_row;
-    if (c >= own0) c += cwv;
-    const int o = static_cast<int>(c / cwv);
-    const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, o) + gath_off) + r * nv + c;
-    o4[r * nv + c] = __ldcg(src);  // over NVLink
-  }
+  p2p_pull_other_chunks(s, gath_off, reinterpret_cast<uint4*>(out), rows, n / 8);
 }
 
 static unsigned p2p_blocks(size_t work) {
