@@ -948,9 +948,12 @@ def main():
     rank, local_rank, world = dist_env()
     if world > 1:
         # NCCL's communicator lines (rank, nranks, device: "Init COMPLETE")
-        # show that every rank joined an N-rank communicator; NCCL reads this
-        # once, at its first call, so it is set before torch is imported
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        # show that every rank joined an N-rank communicator. NCCL reads this
+        # once, at its first call, so it is set before torch is imported; a
+        # quieter level from the environment (VERSION, WARN) is raised.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION", "WARN"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     if a.impl == "reference":
         run_reference(a, rank, world)
     elif a.workload == "prefill":

@@ -51,7 +51,6 @@ namespace cawq {
 
 constexpr int kP32BM = 128;
 constexpr int kP32BK = 64;
-constexpr int kP32EpiWarps = 8;
 // X-split warps: a 128-column tile splits the same X stage for half the
 // MMA work of a 256-column one, so it gets twice the warps; the 256-column
 // tile's fewer threads leave the epilogue registers for 32-column TMEM
@@ -61,7 +60,11 @@ constexpr int kP32EpiWarps = 8;
 // warps and 32-column chunks against 1.54 us with 8 and 16.
 __host__ __device__ constexpr int p32_split_warps(int bn) { return bn == 256 ? 4 : 8; }
 __host__ __device__ constexpr int p32_chunk_cols(int bn) { return bn == 256 ? 32 : 16; }
-__host__ __device__ constexpr int p32_threads(int bn) { return (15 + p32_split_warps(bn)) * 32; }
+// group-epilogue warps (a multiple of 4: whole TMEM lane quarters)
+__host__ __device__ constexpr int p32_epi_warps(int bn) { return 8; }
+__host__ __device__ constexpr int p32_threads(int bn) {
+  return (7 + p32_split_warps(bn) + p32_epi_warps(bn)) * 32;
+}
 
 template <int BN>
 struct P32Layout {
@@ -172,6 +175,9 @@ __global__ void __launch_bounds__(p32_threads(BN), 1)
   using L = P32Layout<BN>;
   constexpr int NB = L::kNB;
   constexpr int kP32SplitWarps = p32_split_warps(BN);
+  constexpr int kP32EpiWarps = p32_epi_warps(BN);
+  constexpr int kParts = kP32EpiWarps / 4;  // epilogue warps per TMEM lane quarter
+  constexpr int kPartCols = 128 / kParts;   // columns of a block per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + L::kOffBars);
@@ -424,11 +430,12 @@ __global__ void __launch_bounds__(p32_threads(BN), 1)
     role_ok = ok;
   } else {
     // ------------------------------------------------ group epilogue
-    // two warps per TMEM lane quarter; warp part p takes columns [64 p,
-    // 64 p + 64) of every 128-column block, blocks in order, so block 0's
-    // slot is free for the next group while block 1 is being read
+    // kParts warps per TMEM lane quarter; warp part p takes columns
+    // [kPartCols p, kPartCols (p + 1)) of every 128-column block, blocks in
+    // order, so block 0's slot is free for the next group while block 1 is
+    // being read
     const int lq = warp & 3;  // TMEM lane quarter this warp may access
-    const int part = (warp - 7 - kP32SplitWarps) >> 2;
+    const int part = (warp - 7 - kP32SplitWarps) >> 2;  // 0 .. kParts - 1
     const uint32_t row_t = (uint32_t)(32 * lq);
     bool ok = true;
     for (int grp = 0; grp < NG; ++grp) {
@@ -444,9 +451,9 @@ __global__ void __launch_bounds__(p32_threads(BN), 1)
           continue;
         }
         tc_fence_after();
-        const int cb = 128 * h + 64 * part;  // first tile column of this warp
+        const int cb = 128 * h + kPartCols * part;  // first tile column of this warp
         const float* sc = s_slot(b) + cb;
-        const uint32_t dbuf = tmem + (uint32_t)(slot * 128 + 64 * part) + (row_t << 16);
+        const uint32_t dbuf = tmem + (uint32_t)(slot * 128 + kPartCols * part) + (row_t << 16);
         const uint32_t run = tmem + 256 + (uint32_t)cb + (row_t << 16);
         // Chunks of kCW columns (two kCW-register arrays live at a time).
         // Per chunk one wait for both loads; the running-sum stores are
@@ -454,12 +461,12 @@ __global__ void __launch_bounds__(p32_threads(BN), 1)
         // the MMA as soon as its last chunk has been read.
         constexpr int kCW = p32_chunk_cols(BN);
 #pragma unroll 1
-        for (int c = 0; c < 64 / kCW; ++c) {
+        for (int c = 0; c < kPartCols / kCW; ++c) {
           float d[kCW], acc[kCW];
           tmem_ld_cols_nowait<kCW>(dbuf + kCW * c, d);
           if (grp > 0) tmem_ld_cols_nowait<kCW>(run + kCW * c, acc);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (c == 64 / kCW - 1) {
+          if (c == kPartCols / kCW - 1) {
             tc_fence_before();
             mbar_arrive(&dempty[slot]);
           }
