@@ -894,6 +894,11 @@ struct cawq_tp_comm {
   ncclComm_t comm = nullptr;
   int world = 0, rank = 0, device = -1;
   int timeout_ms = 60000;
+  // side stream of the row-parallel layer: the all-reduce of one row half
+  // runs there while the other half's GEMM runs on the caller's stream
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork[2] = {nullptr, nullptr};
+  cudaEvent_t join = nullptr;
 };
 
 // A non-blocking communicator returns ncclInProgress while it sets up; wait
@@ -963,6 +968,14 @@ CAWQ_API cawq_status cawq_tp_init(int world, int rank, const uint8_t* id, int ti
     delete c;
     return st;
   }
+  // the row-parallel layer's side stream and events (without them it runs
+  // unsplit)
+  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->fork[0], cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->fork[1], cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming) != cudaSuccess) {
+    (void)cudaGetLastError();
+  }
   *comm = c;
   return CAWQ_OK;
 }
@@ -976,6 +989,10 @@ CAWQ_API cawq_status cawq_tp_destroy(cawq_tp_comm* comm) {
     if (r == ncclInProgress) st = nccl_settle(comm, r, "ncclCommDestroy");
     else if (r != ncclSuccess) st = nccl_fail(r, "ncclCommDestroy");
   }
+  if (comm->side) (void)cudaStreamSynchronize(comm->side);
+  for (cudaEvent_t e : {comm->fork[0], comm->fork[1], comm->join})
+    if (e) (void)cudaEventDestroy(e);
+  if (comm->side) (void)cudaStreamDestroy(comm->side);
   delete comm;
   return st;
 }
@@ -1048,22 +1065,49 @@ CAWQ_API cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x,
     return st;
   if (rows == 0) return CAWQ_OK;
   if (!out || !partial) return fail(CAWQ_ERR_NULL_POINTER, "out and partial must be non-null");
-  st = gemm_common(x, qweight, qzeros, scales, nullptr, partial, rows, kl, n, group_size, dtype,
-                   CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
-  if (st != CAWQ_OK) return st;
   const NcclApi& a = nccl();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ncclResult_t r = a.all_reduce(partial, partial, rows * n, ncclFloat32, ncclSum, comm->comm, s);
-  if (r == ncclInProgress) {
-    st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
-    if (st != CAWQ_OK) return st;
-  } else if (r != ncclSuccess) {
-    return nccl_fail(r, "ncclAllReduce");
+  const size_t es = dtype_size(dtype);
+  // local GEMM of rows [r0, r0 + rc) -> fp32 partial, its all-reduce and the
+  // epilogue (bias once, cast), the last two on stream `cs`
+  auto part = [&](size_t r0, size_t rc, cudaStream_t gs, cudaStream_t cs,
+                  cudaEvent_t fork) -> cawq_status {
+    float* pp = partial + r0 * n;
+    cawq_status s2 = gemm_common(static_cast<const uint8_t*>(x) + r0 * kl * es, qweight, qzeros,
+                                 scales, nullptr, pp, rc, kl, n, group_size, dtype, CAWQ_F32,
+                                 CAWQ_ORDER_AWQ, n, nullptr, gs, true);
+    if (s2 != CAWQ_OK) return s2;
+    if (cs != gs) {
+      cudaError_t e = cudaEventRecord(fork, gs);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, fork, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "row-parallel fork");
+    }
+    ncclResult_t r = a.all_reduce(pp, pp, rc * n, ncclFloat32, ncclSum, comm->comm, cs);
+    if (r == ncclInProgress) {
+      s2 = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
+      if (s2 != CAWQ_OK) return s2;
+    } else if (r != ncclSuccess) {
+      return nccl_fail(r, "ncclAllReduce");
+    }
+    if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
+    cudaError_t e = launch_rowpar_finish(pp, bias, static_cast<uint8_t*>(out) + r0 * n * es,
+                                         rc, n, dtype, cs);
+    return e == cudaSuccess ? CAWQ_OK : cuda_fail(e, "row-parallel epilogue launch");
+  };
+  // From 1024 rows on two or more ranks: two row halves, each all-reduced on
+  // the communicator's side stream as soon as its GEMM is done, so the first
+  // half's all-reduce overlaps the second half's GEMM (each half still fills
+  // the GPU). The same split on every rank (from the shapes alone).
+  if (comm->world > 1 && rows >= 1024 && comm->side && comm->fork[0] && comm->fork[1] &&
+      comm->join) {
+    const size_t h = (rows / 2 + 127) / 128 * 128;
+    if ((st = part(0, h, s, comm->side, comm->fork[0])) != CAWQ_OK) return st;
+    if ((st = part(h, rows - h, s, comm->side, comm->fork[1])) != CAWQ_OK) return st;
+    cudaError_t e = cudaEventRecord(comm->join, comm->side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, comm->join, 0);
+    return e == cudaSuccess ? CAWQ_OK : cuda_fail(e, "row-parallel join");
   }
-  if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
-  cudaError_t e = launch_rowpar_finish(partial, bias, out, rows, n, dtype, s);
-  if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
-  return CAWQ_OK;
+  return part(0, rows, s, s, nullptr);
 }
 
 // ------------------------------------------ fused tensor-parallel push

@@ -407,7 +407,11 @@ cawq_status cawq_gemm_colpar(const cawq_tp_comm* comm, const void* x, const uint
  * input. Computes the fp32 partial [rows, N] into `partial` (caller
  * workspace, rows * N floats), all-reduces it (sum, fp32) over NCCL, then
  * writes out [rows, N] = partial + bias (bias [N] or NULL, added once).
- * With dtype CAWQ_F32, out may be `partial` itself.
+ * With dtype CAWQ_F32, out may be `partial` itself. From 1024 rows on two or
+ * more ranks the rows are done in two halves: each half's all-reduce and
+ * epilogue run on the communicator's own stream (made by cawq_tp_init)
+ * while the next half's GEMM runs on `stream`, which waits for both before
+ * the call's later work (also under stream capture).
  */
 cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint32_t* qweight,
                              const uint32_t* qzeros, const void* scales, const void* bias,
