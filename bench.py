@@ -758,7 +758,11 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
     graph so that the host stays out of the timed region, max over ranks.
     `one_gpu_us` is the same MLP unsharded on one GPU (each rank times it on
     its own GPU alone, max over ranks), and `efficiency` = one_gpu_us / (n_gpus
-    * us), the strong-scaling efficiency of the sharded layer."""
+    * us), the strong-scaling efficiency of the sharded layer. `fused_us` /
+    `fused_efficiency`: the same MLP with down through cawq_gemm_rowpar_p2p
+    (the library's exchange over peer memory), timed from back-to-back direct
+    calls (its host-side epoch keeps it out of graphs; the host stays ahead of
+    the GPU), device time, max over ranks."""
     import torch
 
     from cube_awq_b200 import _lib, synth, tp
@@ -773,6 +777,11 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
     L = _lib.lib()
     f16 = _lib.CAWQ_F16
     nl = n1 // world
+    peers = None
+    if world > 1:
+        plane = 2048 * n2 * 4
+        slot = 2 * ((plane + 255) // 256 * 256) + 2048 * n2 * 2
+        peers = tp.TPPeers(comm, 256 + 2 * slot + 4096, timeout_ms=10000)
     res = {"n_gpus": world, "backend": "native NCCL (cawq_gemm_colpar shard / cawq_gemm_rowpar)",
            "timing": "CUDA graph per part (NCCL calls captured), device time, max over ranks",
            "limit": "the down all-reduce (fp32 [M, 8192]) and per-call latency at small M"}
@@ -812,9 +821,28 @@ def tp_mlp_numbers(dev, world, max_over_ranks, reps=20):
         res[f"M={m}"] = {"us": round(t, 2), "gate_up_colpar_us": t_col,
                          "down_rowpar_allreduce_us": t_row, "one_gpu_us": t_one,
                          "efficiency": round(t_one / (world * t), 3)}
+        if peers is not None:
+            stream = torch.cuda.current_stream(dev).cuda_stream
+
+            def fused_call(i):
+                col_call(stream)
+                hh_c.copy_(hh)
+                check(L.cawq_gemm_rowpar_p2p(peers.table, peers.next_epoch(), hh_c.data_ptr(),
+                                             row.qweight.data_ptr(), row.qzeros.data_ptr(),
+                                             row.scales.data_ptr(), None, out.data_ptr(), m,
+                                             k2, n2, g, f16, stream))
+            for i in range(3):
+                fused_call(i)
+            t_f = _timed_calls(fused_call, n_rep, max_over_ranks)
+            res[f"M={m}"]["fused_us"] = t_f
+            res[f"M={m}"]["fused_efficiency"] = round(t_one / (world * t_f), 3)
         del x, h, hh_c, out, part, h1, x2f
     del col, row, w1, w2
     torch.cuda.synchronize()
+    if peers is not None:
+        import torch.distributed as dist
+        dist.barrier()  # every rank's last fused call has completed
+        peers.close()
     comm.close()
     torch.cuda.empty_cache()
     return res

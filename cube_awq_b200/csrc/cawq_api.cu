@@ -894,11 +894,6 @@ struct cawq_tp_comm {
   ncclComm_t comm = nullptr;
   int world = 0, rank = 0, device = -1;
   int timeout_ms = 60000;
-  // side stream of the row-parallel layer: the all-reduce of one row half
-  // runs there while the other half's GEMM runs on the caller's stream
-  cudaStream_t side = nullptr;
-  cudaEvent_t fork[2] = {nullptr, nullptr};
-  cudaEvent_t join = nullptr;
 };
 
 // A non-blocking communicator returns ncclInProgress while it sets up; wait
@@ -968,14 +963,6 @@ CAWQ_API cawq_status cawq_tp_init(int world, int rank, const uint8_t* id, int ti
     delete c;
     return st;
   }
-  // the row-parallel layer's side stream and events (without them it runs
-  // unsplit)
-  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaEventCreateWithFlags(&c->fork[0], cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&c->fork[1], cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming) != cudaSuccess) {
-    (void)cudaGetLastError();
-  }
   *comm = c;
   return CAWQ_OK;
 }
@@ -989,10 +976,6 @@ CAWQ_API cawq_status cawq_tp_destroy(cawq_tp_comm* comm) {
     if (r == ncclInProgress) st = nccl_settle(comm, r, "ncclCommDestroy");
     else if (r != ncclSuccess) st = nccl_fail(r, "ncclCommDestroy");
   }
-  if (comm->side) (void)cudaStreamSynchronize(comm->side);
-  for (cudaEvent_t e : {comm->fork[0], comm->fork[1], comm->join})
-    if (e) (void)cudaEventDestroy(e);
-  if (comm->side) (void)cudaStreamDestroy(comm->side);
   delete comm;
   return st;
 }
@@ -1065,49 +1048,26 @@ CAWQ_API cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x,
     return st;
   if (rows == 0) return CAWQ_OK;
   if (!out || !partial) return fail(CAWQ_ERR_NULL_POINTER, "out and partial must be non-null");
+  // (Splitting the rows in two halves, with the first half's all-reduce on a
+  // side stream while the second half's GEMM runs, was measured slower on 4
+  // GPUs: 499 against 470 us at M = 2048. The GEMM half is sized to fill
+  // every SM, and NCCL's kernel takes some of them.)
+  st = gemm_common(x, qweight, qzeros, scales, nullptr, partial, rows, kl, n, group_size, dtype,
+                   CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
+  if (st != CAWQ_OK) return st;
   const NcclApi& a = nccl();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t es = dtype_size(dtype);
-  // local GEMM of rows [r0, r0 + rc) -> fp32 partial, its all-reduce and the
-  // epilogue (bias once, cast), the last two on stream `cs`
-  auto part = [&](size_t r0, size_t rc, cudaStream_t gs, cudaStream_t cs,
-                  cudaEvent_t fork) -> cawq_status {
-    float* pp = partial + r0 * n;
-    cawq_status s2 = gemm_common(static_cast<const uint8_t*>(x) + r0 * kl * es, qweight, qzeros,
-                                 scales, nullptr, pp, rc, kl, n, group_size, dtype, CAWQ_F32,
-                                 CAWQ_ORDER_AWQ, n, nullptr, gs, true);
-    if (s2 != CAWQ_OK) return s2;
-    if (cs != gs) {
-      cudaError_t e = cudaEventRecord(fork, gs);
-      if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, fork, 0);
-      if (e != cudaSuccess) return cuda_fail(e, "row-parallel fork");
-    }
-    ncclResult_t r = a.all_reduce(pp, pp, rc * n, ncclFloat32, ncclSum, comm->comm, cs);
-    if (r == ncclInProgress) {
-      s2 = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
-      if (s2 != CAWQ_OK) return s2;
-    } else if (r != ncclSuccess) {
-      return nccl_fail(r, "ncclAllReduce");
-    }
-    if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
-    cudaError_t e = launch_rowpar_finish(pp, bias, static_cast<uint8_t*>(out) + r0 * n * es,
-                                         rc, n, dtype, cs);
-    return e == cudaSuccess ? CAWQ_OK : cuda_fail(e, "row-parallel epilogue launch");
-  };
-  // From 1024 rows on two or more ranks: two row halves, each all-reduced on
-  // the communicator's side stream as soon as its GEMM is done, so the first
-  // half's all-reduce overlaps the second half's GEMM (each half still fills
-  // the GPU). The same split on every rank (from the shapes alone).
-  if (comm->world > 1 && rows >= 1024 && comm->side && comm->fork[0] && comm->fork[1] &&
-      comm->join) {
-    const size_t h = (rows / 2 + 127) / 128 * 128;
-    if ((st = part(0, h, s, comm->side, comm->fork[0])) != CAWQ_OK) return st;
-    if ((st = part(h, rows - h, s, comm->side, comm->fork[1])) != CAWQ_OK) return st;
-    cudaError_t e = cudaEventRecord(comm->join, comm->side);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, comm->join, 0);
-    return e == cudaSuccess ? CAWQ_OK : cuda_fail(e, "row-parallel join");
+  ncclResult_t r = a.all_reduce(partial, partial, rows * n, ncclFloat32, ncclSum, comm->comm, s);
+  if (r == ncclInProgress) {
+    st = nccl_settle(const_cast<cawq_tp_comm*>(comm), r, "ncclAllReduce");
+    if (st != CAWQ_OK) return st;
+  } else if (r != ncclSuccess) {
+    return nccl_fail(r, "ncclAllReduce");
   }
-  return part(0, rows, s, s, nullptr);
+  if (out == partial && !bias && dtype == CAWQ_F32) return CAWQ_OK;
+  cudaError_t e = launch_rowpar_finish(partial, bias, out, rows, n, dtype, s);
+  if (e != cudaSuccess) return cuda_fail(e, "row-parallel epilogue launch");
+  return CAWQ_OK;
 }
 
 // ------------------------------------------ fused tensor-parallel push
@@ -1278,18 +1238,18 @@ CAWQ_API cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t e
   if (rows == 0) return CAWQ_OK;
   if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
   // Above 8 MiB of peer shards per rank the GEMM writes only this rank's
-  // buffer and `out`, and the peers' shards are read after the flag exchange
-  // (pull); below it the epilogue pushes the shard into every peer's buffer
-  // as its tiles finish (the same choice on every rank, from the shapes).
-  const bool pull = peers->world > 1 && rows * nl * es * (size_t)(peers->world - 1) > (8u << 20) &&
-                    reinterpret_cast<uintptr_t>(out) % 16 == 0;
-  if (pull) {
+  // buffer and `out`, and a kernel after it pushes the shard into every
+  // peer's buffer; below it the epilogue pushes the shard as its tiles
+  // finish (the same choice on every rank, from the shapes).
+  const bool large = peers->world > 1 && rows * nl * es * (size_t)(peers->world - 1) > (8u << 20) &&
+                     reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (large) {
     void* rep[CAWQ_TP_MAX_PEERS] = {static_cast<uint8_t*>(out) + n0 * es};
     void* own = static_cast<uint8_t*>(peers->base[peers->rank]) + off + n0 * es;
     st = gemm_common(x, qweight, qzeros, scales, bias, own, rows, k, nl, group_size, dtype, dtype,
                      CAWQ_ORDER_AWQ, n, nullptr, stream, true, 0, nullptr, rep, 1);
     if (st != CAWQ_OK) return st;
-    cudaError_t e = launch_p2p_colpar_pull(p2p_sync(peers, epoch), off, out, rows, n, dtype,
+    cudaError_t e = launch_p2p_colpar_push(p2p_sync(peers, epoch), off, out, rows, n, dtype,
                                            static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "gather launch");
     return CAWQ_OK;
@@ -1338,21 +1298,21 @@ CAWQ_API cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t e
                   plane * (size_t)(world - 1) > (4u << 20);
   if (rs) {
     const size_t es = dtype == CAWQ_F32 ? 4 : 2;
-    const size_t gath = (plane + 255) / 256 * 256;  // gather region after the partial
-    if ((st = p2p_check(peers, epoch, gath + rows * n * es, &off)) != CAWQ_OK) return st;
+    const size_t pl = (plane + 255) / 256 * 256;  // partial, receive region, gather region
+    if ((st = p2p_check(peers, epoch, 2 * pl + rows * n * es, &off)) != CAWQ_OK) return st;
     if (rows == 0) return CAWQ_OK;
     if (!out) return fail(CAWQ_ERR_NULL_POINTER, "out must be non-null");
     if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
       return fail(CAWQ_ERR_ALIGNMENT, "out must be 16-byte aligned");
-    // this rank's fp32 partial [rows, n] stays in its own buffer
+    // this rank's fp32 partial [rows, n] into its own buffer
     void* own = static_cast<uint8_t*>(peers->base[peers->rank]) + off;
     st = gemm_common(x, qweight, qzeros, scales, nullptr, own, rows, kl, n, group_size, dtype,
                      CAWQ_F32, CAWQ_ORDER_AWQ, n, nullptr, stream, true);
     if (st != CAWQ_OK) return st;
     P2PSync sa = p2p_sync(peers, epoch), sb = p2p_sync(peers, epoch);
     sb.fofs = 8;  // the gather's own flag words
-    cudaError_t e = launch_p2p_rowpar_pull(sa, sb, off, off + gath, bias, out, rows, n, dtype,
-                                           static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_p2p_rowpar_rs(sa, sb, off, off + pl, off + 2 * pl, bias, out, rows, n,
+                                         dtype, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "reduce-scatter launch");
     return CAWQ_OK;
   }

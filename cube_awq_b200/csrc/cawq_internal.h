@@ -124,20 +124,23 @@ struct P2PSync {
 // gathered [rows, n] result (dense in `slot`) to out (row stride ld_out).
 cudaError_t launch_p2p_colpar_finish(const P2PSync& s, const void* slot, void* out, size_t rows,
                                      size_t n, size_t ld_out, int dtype, cudaStream_t stream);
-// Pull variants for large outputs (the GEMM wrote only this rank's own
-// buffer). Column-parallel: flag exchange, then copy every other rank's
-// shard from its slot (dense [rows, n] at byte offset off) into out (row
-// stride n, 16-byte aligned, n * sizeof(F) % (16 * world) == 0).
-cudaError_t launch_p2p_colpar_pull(const P2PSync& s, size_t off, void* out, size_t rows,
+// Exchanges for large outputs (the GEMM wrote only this rank's own buffer).
+// Column-parallel: push this rank's columns of its slot (dense [rows, n] at
+// byte offset off) into every other rank's slot; flag exchange; copy the
+// other ranks' columns from the own slot into out (row stride n, 16-byte
+// aligned, n * sizeof(F) % (16 * world) == 0).
+cudaError_t launch_p2p_colpar_push(const P2PSync& s, size_t off, void* out, size_t rows,
                                    size_t n, int dtype, cudaStream_t stream);
-// Row-parallel: every rank's fp32 partial [rows, n] at byte offset off of its
-// buffer; flag set A, sum the own column chunk over the partials in rank
-// order (+ bias, cast) into out and the own gather region (byte offset
-// gath_off); flag set B, copy the other chunks from the peers' gather
-// regions into out. dtype f16 / bf16, n % (32 world) == 0.
-cudaError_t launch_p2p_rowpar_pull(const P2PSync& sa, const P2PSync& sb, size_t off,
-                                   size_t gath_off, const void* bias, void* out, size_t rows,
-                                   size_t n, int dtype, cudaStream_t stream);
+// Row-parallel reduce-scatter + all-gather after the local GEMM wrote its
+// fp32 partial [rows, n] at byte offset off of this rank's buffer: push the
+// other ranks' column chunks into their receive regions (recv_off:
+// [world][rows][n / world] fp32); flag set A, sum the own chunk in rank
+// order (+ bias, cast) into out and push it into the other ranks' gather
+// regions (gath_off: [rows, n] of F); flag set B, copy the other chunks from
+// the own gather region into out. dtype f16 / bf16, n % (32 world) == 0.
+cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, size_t off,
+                                 size_t recv_off, size_t gath_off, const void* bias, void* out,
+                                 size_t rows, size_t n, int dtype, cudaStream_t stream);
 // After the push of a row-parallel GEMM's fp32 partials into slot[world][rows][n]:
 // signal, wait, then out = sum over ranks (in rank order) + bias, cast to dtype.
 cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const void* bias,

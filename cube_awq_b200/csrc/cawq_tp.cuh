@@ -208,27 +208,25 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// ------------------------------------------------- fused tensor-parallel pull
-// For large outputs the GEMM writes only into this rank's own buffer (no
-// stores over NVLink inside the epilogue, which would stall it), and after
-// the flag exchange every rank reads what it needs from the peers' buffers:
-// 16-byte loads by every resident thread keep enough bytes in flight to fill
-// the links. A peer's slot is not overwritten before this rank's reads are
-// done: the peer writes that slot again two epochs later, after waiting for
-// this rank's flag of the epoch in between, which this rank publishes only
-// in a later kernel of its stream.
+// ------------------------------------- fused tensor-parallel, large outputs
+// For large outputs the GEMM writes only into this rank's own buffer (stores
+// over NVLink inside the epilogue stall it), and separate kernels after it
+// push the data to the peers: plain 16-byte stores, which are posted, so the
+// links stay busy (reading the peers' buffers instead reached about half the
+// rate). A peer's slot is not overwritten while the peer still reads it: this
+// rank writes slot (epoch & 1) again only two epochs later, after waiting for
+// the peer's flag of the epoch in between, which the peer publishes only in a
+// later kernel of its stream than its reads.
 
 __device__ __forceinline__ const uint8_t* p2p_base(const P2PSync& s, int j) {
   return reinterpret_cast<const uint8_t*>(p2p_flags(s, j));
 }
 
 // Copies, for every row, the column chunks of the other ranks (chunk o =
-// vectors [o cwv, (o+1) cwv) of a row of nv 16-byte vectors) from rank o's
-// buffer at byte offset `off` (dense [rows, nv]) into out (same layout).
-// Four loads per thread are in flight before their stores: a load from a
-// peer's memory takes microseconds under load, and one at a time left the
-// links mostly idle.
-__device__ __forceinline__ void p2p_pull_other_chunks(const P2PSync& s, size_t off,
+// vectors [o cwv, (o+1) cwv) of a row of nv 16-byte vectors) from this
+// rank's buffer at byte offset `off` (dense [rows, nv], where the other
+// ranks pushed them) into out (same layout). Four loads in flight per thread.
+__device__ __forceinline__ void p2p_copy_other_chunks(const P2PSync& s, size_t off,
                                                       uint4* __restrict__ out, size_t rows,
                                                       size_t nv) {
   constexpr int kU = 4;
@@ -236,6 +234,7 @@ __device__ __forceinline__ void p2p_pull_other_chunks(const P2PSync& s, size_t o
   const size_t per_row = nv - cwv;      // outside the own chunk
   const size_t total = rows * per_row;
   const size_t own0 = (size_t)s.rank * cwv;
+  const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, s.rank) + off);
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += kU * stride) {
     uint4 v[kU];
@@ -248,9 +247,8 @@ __device__ __forceinline__ void p2p_pull_other_chunks(const P2PSync& s, size_t o
         const size_t r = i / per_row;
         size_t c = i - r * per_row;
         if (c >= own0) c += cwv;
-        const int o = static_cast<int>(c / cwv);
         at[u] = r * nv + c;
-        v[u] = __ldcg(reinterpret_cast<const uint4*>(p2p_base(s, o) + off) + at[u]);  // NVLink
+        v[u] = __ldcg(src + at[u]);  // L2: peers wrote it
       }
     }
 #pragma unroll
@@ -259,86 +257,152 @@ __device__ __forceinline__ void p2p_pull_other_chunks(const P2PSync& s, size_t o
   }
 }
 
-// Column-parallel all-gather: this rank's shard is already in `out` (the
-// GEMM's second output); copy every other rank's [rows, n/world] shard from
-// its slot (dense [rows, n] at byte offset `off`) into out (row stride n).
+// Column-parallel all-gather of large outputs, step 1 (no flags; the GEMM
+// before it has completed and wrote this rank's columns into its own slot,
+// dense [rows, nv] at byte offset `off`, and into out): copy this rank's
+// chunk of every row into the same place of every other rank's slot. Stores
+// over NVLink are posted, so the links stay busy without the round trip a
+// peer load waits for; four vectors in flight per thread.
 __global__ void __launch_bounds__(256)
-    p2p_colpar_pull_kernel(const P2PSync s, size_t off, uint4* __restrict__ out, size_t rows,
-                           size_t nv) {
-  if (!p2p_signal_and_wait(s)) return;
-  p2p_pull_other_chunks(s, off, out, rows, nv);
-}
-
-// Row-parallel reduce-scatter: every rank's fp32 partial [rows, n] is in its
-// own slot (byte offset `off`). After flag set A this rank sums column chunk
-// `rank` (n / world columns) over the world partials in rank order, adds the
-// bias once, casts, and writes it to out and to its own gather region
-// ([rows, n] of F at byte offset gath_off).
-template <int DT>
-__global__ void __launch_bounds__(256)
-    p2p_rowpar_pull_rs_kernel(const P2PSync s, size_t off, size_t gath_off,
-                              const typename DType<DT>::T* __restrict__ bias,
-                              typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
-  using T = typename DType<DT>::T;
-  if (!p2p_signal_and_wait(s)) return;
-  const size_t cw = n / s.world, c0 = (size_t)s.rank * cw;
-  const size_t per_row = cw / 8;  // 8 columns per item (cw % 32 == 0)
-  const size_t oct = rows * per_row;
-  T* gath = reinterpret_cast<T*>(const_cast<uint8_t*>(p2p_base(s, s.rank)) + gath_off);
-  // two items per thread, all their loads in flight before any sum
-  constexpr int kU = 2;
+    p2p_colpar_push_kernel(const P2PSync s, size_t off, size_t rows, size_t nv) {
+  constexpr int kU = 4;
+  const size_t cwv = nv / s.world;
+  const size_t total = rows * cwv;
+  const size_t own0 = (size_t)s.rank * cwv;
+  const uint4* src = reinterpret_cast<const uint4*>(p2p_base(s, s.rank) + off);
   const size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < oct; i0 += kU * stride) {
-    float4 a[kU][kP2PMaxWorld], b[kU][kP2PMaxWorld];
+  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += kU * stride) {
+    uint4 v[kU];
     size_t at[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const size_t i = i0 + u * stride;
       at[u] = ~static_cast<size_t>(0);
-      if (i < oct) {
-        const size_t r = i / per_row, c = c0 + (i - r * per_row) * 8;
-        at[u] = r * n + c;
-#pragma unroll
-        for (int j = 0; j < kP2PMaxWorld; ++j) {
-          if (j < s.world) {
-            const float4* src = reinterpret_cast<const float4*>(p2p_base(s, j) + off) + at[u] / 4;
-            a[u][j] = __ldcg(src);
-            b[u][j] = __ldcg(src + 1);
-          }
-        }
+      if (i < total) {
+        const size_t r = i / cwv;
+        at[u] = r * nv + own0 + (i - r * cwv);
+        v[u] = __ldcg(src + at[u]);
       }
     }
+    for (int j = 0; j < s.world; ++j) {
+      if (j == s.rank) continue;
+      uint4* dst = reinterpret_cast<uint4*>(const_cast<uint8_t*>(p2p_base(s, j)) + off);
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (at[u] == ~static_cast<size_t>(0)) continue;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int j = 0; j < kP2PMaxWorld; ++j) {  // rank order
-        if (j < s.world) {
-          acc[0] += a[u][j].x; acc[1] += a[u][j].y; acc[2] += a[u][j].z; acc[3] += a[u][j].w;
-          acc[4] += b[u][j].x; acc[5] += b[u][j].y; acc[6] += b[u][j].z; acc[7] += b[u][j].w;
-        }
-      }
-      const size_t c = at[u] % n;
-      uint4 v;
-      T* h = reinterpret_cast<T*>(&v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c + e]) : 0.f));
-      *reinterpret_cast<uint4*>(out + at[u]) = v;
-      *reinterpret_cast<uint4*>(gath + at[u]) = v;
+      for (int u = 0; u < kU; ++u)
+        if (at[u] != ~static_cast<size_t>(0)) dst[at[u]] = v[u];  // over NVLink
     }
   }
 }
 
-// Row-parallel all-gather: after flag set B every rank's chunk is in its
-// gather region; copy the other ranks' chunks into out.
+// Step 2 (flags): every rank's chunk is in this rank's slot; copy the other
+// ranks' chunks into out (this rank's own is there already).
+__global__ void __launch_bounds__(256)
+    p2p_colpar_gather_kernel(const P2PSync s, size_t off, uint4* __restrict__ out, size_t rows,
+                             size_t nv) {
+  if (!p2p_signal_and_wait(s)) return;
+  p2p_copy_other_chunks(s, off, out, rows, nv);
+}
+
+// Row-parallel reduce-scatter, written by the ranks that own the data: every
+// rank's fp32 partial [rows, n] is in its own slot (byte offset `off`),
+// followed by a receive region recv[world][rows][n / world] (byte offset
+// recv_off) and a gather region [rows, n] of F (byte offset gath_off).
+//
+// Step 1 (no flags; the GEMM before it has completed): copy column chunk o
+// (n / world columns) of this rank's partial into recv[rank] of rank o, for
+// every o != rank: stores over NVLink, four 16-byte vectors in flight per
+// thread. Stores are posted, so the links stay busy without the round trip
+// a peer load waits for.
+__global__ void __launch_bounds__(256)
+    p2p_rowpar_scatter_kernel(const P2PSync s, size_t off, size_t recv_off, size_t rows,
+                              size_t n) {
+  constexpr int kU = 4;
+  const size_t cw = n / s.world;
+  const size_t cwv = cw / 4;               // float4 vectors per chunk row
+  const size_t per_row = (n - cw) / 4;     // vectors outside the own chunk
+  const size_t total = rows * per_row;
+  const size_t own0 = (size_t)s.rank * cwv;
+  const float4* part = reinterpret_cast<const float4*>(p2p_base(s, s.rank) + off);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < total; i0 += kU * stride) {
+    float4 v[kU];
+    size_t src[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const size_t i = i0 + u * stride;
+      src[u] = ~static_cast<size_t>(0);
+      if (i < total) {
+        const size_t r = i / per_row;
+        size_t c = i - r * per_row;
+        if (c >= own0) c += cwv;
+        src[u] = r * (n / 4) + c;
+        v[u] = __ldcg(part + src[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (src[u] == ~static_cast<size_t>(0)) continue;
+      const size_t r = src[u] / (n / 4), c = src[u] - r * (n / 4);
+      const int o = static_cast<int>(c / cwv);
+      float4* dst = reinterpret_cast<float4*>(const_cast<uint8_t*>(p2p_base(s, o)) + recv_off) +
+                    ((size_t)s.rank * rows + r) * cwv + (c - (size_t)o * cwv);
+      *dst = v[u];  // over NVLink
+    }
+  }
+}
+
+// Step 2 (flag set A: every rank's step 1 is done): sum column chunk `rank`
+// over the world partials in rank order (this rank's from its partial, the
+// others' from its receive region), add the bias once, cast, and write the
+// chunk to out and into every other rank's gather region.
 template <int DT>
 __global__ void __launch_bounds__(256)
-    p2p_rowpar_pull_ag_kernel(const P2PSync s, size_t gath_off, typename DType<DT>::T* __restrict__ out,
-                              size_t rows, size_t n) {
+    p2p_rowpar_reduce_kernel(const P2PSync s, size_t off, size_t recv_off, size_t gath_off,
+                             const typename DType<DT>::T* __restrict__ bias,
+                             typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
+  using T = typename DType<DT>::T;
   if (!p2p_signal_and_wait(s)) return;
-  p2p_pull_other_chunks(s, gath_off, reinterpret_cast<uint4*>(out), rows, n / 8);
+  const size_t cw = n / s.world, c0 = (size_t)s.rank * cw;
+  const size_t per_row = cw / 8;  // 8 columns per item (cw % 32 == 0)
+  const size_t oct = rows * per_row;
+  const uint8_t* own = p2p_base(s, s.rank);
+  const float* part = reinterpret_cast<const float*>(own + off);
+  const float* recv = reinterpret_cast<const float*>(own + recv_off);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < oct;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / per_row, cl = (i - r * per_row) * 8;  // column inside the chunk
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < s.world; ++j) {  // rank order: the same sum on every rank
+      const float* src = j == s.rank ? part + r * n + c0 + cl
+                                     : recv + ((size_t)j * rows + r) * cw + cl;
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(src));  // L2: peers wrote it
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    uint4 v;
+    T* h = reinterpret_cast<T*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      h[e] = DType<DT>::from_f32(acc[e] + (bias ? DType<DT>::to_f32(bias[c0 + cl + e]) : 0.f));
+    const size_t at = r * n + c0 + cl;
+    *reinterpret_cast<uint4*>(out + at) = v;
+    for (int j = 0; j < s.world; ++j) {
+      if (j == s.rank) continue;
+      T* g = reinterpret_cast<T*>(const_cast<uint8_t*>(p2p_base(s, j)) + gath_off);
+      *reinterpret_cast<uint4*>(g + at) = v;  // over NVLink
+    }
+  }
+}
+
+// Step 3 (flag set B: every rank's step 2 is done): the other chunks are in
+// this rank's gather region; copy them to out.
+template <int DT>
+__global__ void __launch_bounds__(256)
+    p2p_rowpar_gather_kernel(const P2PSync s, size_t gath_off,
+                             typename DType<DT>::T* __restrict__ out, size_t rows, size_t n) {
+  if (!p2p_signal_and_wait(s)) return;
+  p2p_copy_other_chunks(s, gath_off, reinterpret_cast<uint4*>(out), rows, n / 8);
 }
 
 static unsigned p2p_blocks(size_t work) {
@@ -385,31 +449,36 @@ cudaError_t launch_p2p_rowpar_finish(const P2PSync& s, const float* slot, const 
   return cudaGetLastError();
 }
 
-cudaError_t launch_p2p_colpar_pull(const P2PSync& s, size_t off, void* out, size_t rows,
+cudaError_t launch_p2p_colpar_push(const P2PSync& s, size_t off, void* out, size_t rows,
                                    size_t n, int dtype, cudaStream_t stream) {
   const size_t es = dtype == kF32 ? 4 : 2;
   const size_t nv = n * es / 16;
-  p2p_colpar_pull_kernel<<<p2p_blocks(rows * (nv - nv / s.world)), 256, 0, stream>>>(
+  p2p_colpar_push_kernel<<<p2p_blocks(rows * (nv / s.world) / 4), 256, 0, stream>>>(s, off, rows,
+                                                                                  nv);
+  p2p_colpar_gather_kernel<<<p2p_blocks(rows * (nv - nv / s.world)), 256, 0, stream>>>(
       s, off, static_cast<uint4*>(out), rows, nv);
   return cudaGetLastError();
 }
 
-cudaError_t launch_p2p_rowpar_pull(const P2PSync& sa, const P2PSync& sb, size_t off,
-                                   size_t gath_off, const void* bias, void* out, size_t rows,
-                                   size_t n, int dtype, cudaStream_t stream) {
+cudaError_t launch_p2p_rowpar_rs(const P2PSync& sa, const P2PSync& sb, size_t off,
+                                 size_t recv_off, size_t gath_off, const void* bias, void* out,
+                                 size_t rows, size_t n, int dtype, cudaStream_t stream) {
   const size_t cw = n / sa.world;
+  const unsigned b0 = p2p_blocks(rows * (n - cw) / 16);
   const unsigned b1 = p2p_blocks(rows * cw / 8);
   const unsigned b2 = p2p_blocks(rows * (n - cw) / 8);
+  p2p_rowpar_scatter_kernel<<<b0, 256, 0, stream>>>(sa, off, recv_off, rows, n);
   if (dtype == kF16) {
-    p2p_rowpar_pull_rs_kernel<kF16><<<b1, 256, 0, stream>>>(
-        sa, off, gath_off, static_cast<const __half*>(bias), static_cast<__half*>(out), rows, n);
-    p2p_rowpar_pull_ag_kernel<kF16><<<b2, 256, 0, stream>>>(sb, gath_off,
-                                                            static_cast<__half*>(out), rows, n);
+    p2p_rowpar_reduce_kernel<kF16><<<b1, 256, 0, stream>>>(
+        sa, off, recv_off, gath_off, static_cast<const __half*>(bias), static_cast<__half*>(out),
+        rows, n);
+    p2p_rowpar_gather_kernel<kF16><<<b2, 256, 0, stream>>>(sb, gath_off,
+                                                           static_cast<__half*>(out), rows, n);
   } else {
-    p2p_rowpar_pull_rs_kernel<kBF16><<<b1, 256, 0, stream>>>(
-        sa, off, gath_off, static_cast<const __nv_bfloat16*>(bias),
+    p2p_rowpar_reduce_kernel<kBF16><<<b1, 256, 0, stream>>>(
+        sa, off, recv_off, gath_off, static_cast<const __nv_bfloat16*>(bias),
         static_cast<__nv_bfloat16*>(out), rows, n);
-    p2p_rowpar_pull_ag_kernel<kBF16><<<b2, 256, 0, stream>>>(
+    p2p_rowpar_gather_kernel<kBF16><<<b2, 256, 0, stream>>>(
         sb, gath_off, static_cast<__nv_bfloat16*>(out), rows, n);
   }
   return cudaGetLastError();

@@ -407,11 +407,7 @@ cawq_status cawq_gemm_colpar(const cawq_tp_comm* comm, const void* x, const uint
  * input. Computes the fp32 partial [rows, N] into `partial` (caller
  * workspace, rows * N floats), all-reduces it (sum, fp32) over NCCL, then
  * writes out [rows, N] = partial + bias (bias [N] or NULL, added once).
- * With dtype CAWQ_F32, out may be `partial` itself. From 1024 rows on two or
- * more ranks the rows are done in two halves: each half's all-reduce and
- * epilogue run on the communicator's own stream (made by cawq_tp_init)
- * while the next half's GEMM runs on `stream`, which waits for both before
- * the call's later work (also under stream capture).
+ * With dtype CAWQ_F32, out may be `partial` itself.
  */
 cawq_status cawq_gemm_rowpar(const cawq_tp_comm* comm, const void* x, const uint32_t* qweight,
                              const uint32_t* qzeros, const void* scales, const void* bias,
@@ -520,9 +516,10 @@ cawq_status cawq_tp_p2p_destroy(cawq_tp_peers* peers);
  *     aligned): the local GEMM's epilogue writes its [rows, n/world] columns
  *     into the slot of every rank's buffer as its tiles finish; after the
  *     flag exchange each rank copies its gathered slot to `out`;
- *   - pull (larger): the local GEMM writes its columns into its own slot and
- *     into `out`; after the flag exchange each rank reads the other ranks'
- *     columns from their slots into `out`.
+ *   - after the GEMM (larger): the local GEMM writes its columns into its
+ *     own slot and into `out`; a kernel then copies them into every other
+ *     rank's slot; after the flag exchange each rank copies the other ranks'
+ *     columns from its own slot into `out`.
  * Needs rows * n * sizeof(F) bytes per slot. Every rank makes the same fused
  * calls in the same order, each with the next `epoch` of this peer table
  * (1, 2, 3, ...: one counter per table, shared by all layers that use it).
@@ -543,15 +540,16 @@ cawq_status cawq_gemm_colpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, con
  *     adds the bias once and casts. Needs world * rows * n * 4 bytes per
  *     slot;
  *   - reduce-scatter + all-gather (larger; `out` must be 16-byte aligned):
- *     the local GEMM writes its fp32 partial [rows, n] into its own slot;
- *     after the flag exchange rank o reads column chunk o (n / world
- *     columns) of every rank's partial, sums them in rank order, adds the
- *     bias, casts, and writes the chunk to `out` and to its own gather
- *     region; after a second flag exchange (flag words 8..15 of the header)
- *     each rank reads the other chunks from the other ranks' gather regions.
- *     Each rank receives (world - 1) / world of a plane in fp32 and of the
- *     result in F. Needs rows * n * 4 (rounded up to 256) + rows * n *
- *     sizeof(F) bytes per slot.
+ *     the local GEMM writes its fp32 partial [rows, n] into its own slot; a
+ *     kernel copies column chunk o (n / world columns) of it into rank o's
+ *     receive region, for every o != rank; after the flag exchange rank o
+ *     sums its chunk over the world partials in rank order, adds the bias,
+ *     casts, and writes the chunk to `out` and into every other rank's
+ *     gather region; after a second flag exchange (flag words 8..15 of the
+ *     header) each rank copies the other chunks from its gather region. Each
+ *     rank sends (world - 1) / world of a plane in fp32 and of the result in
+ *     F. Needs 2 * (rows * n * 4 rounded up to 256) + rows * n * sizeof(F)
+ *     bytes per slot.
  * Epochs as for cawq_gemm_colpar_p2p.
  */
 cawq_status cawq_gemm_rowpar_p2p(const cawq_tp_peers* peers, uint32_t epoch, const void* x,

@@ -136,10 +136,11 @@ def _two_rank_stand_in(dev, nbytes, sets=(1,)):
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_colpar_pull_on_one_gpu(cuda_device, dtype):
+def test_colpar_large_output_push_on_one_gpu(cuda_device, dtype):
     # Above 8 MiB of peer shards the column-parallel GEMM writes only its own
-    # buffer and the output, and reads the peer's shard from the peer's slot
-    # after the flag exchange. The stand-in peer's slot holds a known shard.
+    # slot and the output; a kernel after it pushes the shard into the peer's
+    # slot, and after the flag exchange the peer's shard is copied from this
+    # rank's own slot, where the peer pushed it (preset here with known data).
     rows, k, n, g = 2100, 512, 4096, 128
     es = 2
     slot_need = rows * n * es
@@ -149,43 +150,48 @@ def test_colpar_pull_on_one_gpu(cuda_device, dtype):
     x, qw, qz, s, b = t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), t(b, dtype)
     off = 256 + peers.slot_bytes                   # epoch 1: slot 1
     tdt = x.dtype
-    peer_slot = other[off:off + slot_need].view(tdt).view(rows, n)
-    peer_slot.copy_(torch.randn(rows, n, device=cuda_device).to(tdt))
+    half = n // 2
+    own_slot = own[off:off + slot_need].view(tdt).view(rows, n)
+    own_slot[:, half:].copy_(torch.randn(rows, half, device=cuda_device).to(tdt))  # the peer's
+    pushed = own_slot[:, half:].clone()
     col = tp.ColumnParallelAWQLinear(qw, qz, s, b, backend="p2p", peers=peers)
     y = col(x)
     torch.cuda.synchronize()
     assert cawq.device_error() == 0
-    half = n // 2
     mine = cawq.gemm(x, col.qweight, col.qzeros, col.scales, g, bias=col.bias)
     assert torch.equal(y[:, :half], mine)
-    assert torch.equal(y[:, half:], peer_slot[:, half:])
-    own_slot = own[off:off + slot_need].view(tdt).view(rows, n)
-    assert torch.equal(own_slot[:, :half], mine)   # what the peer would read
+    assert torch.equal(y[:, half:], pushed)
+    assert torch.equal(own_slot[:, :half], mine)
+    peer_slot = other[off:off + slot_need].view(tdt).view(rows, n)
+    assert torch.equal(peer_slot[:, :half], mine)  # pushed to the peer
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_rowpar_reduce_scatter_pull_on_one_gpu(cuda_device, dtype):
-    # rows * n * 4 bytes above 4 MiB take the reduce-scatter: this rank's
-    # fp32 partial stays in its own slot; after flag set A it sums its column
-    # chunk over its own and the peer's partial (rank order), adds the bias,
-    # writes the output and its own gather region; after flag set B it reads
-    # the other chunk from the peer's gather region. The stand-in peer holds
-    # a known partial and a known gathered chunk.
+def test_rowpar_reduce_scatter_on_one_gpu(cuda_device, dtype):
+    # rows * n * 4 bytes above 4 MiB take the reduce-scatter: the GEMM writes
+    # this rank's fp32 partial into its own slot; a kernel copies the peer's
+    # column chunk of it into the peer's receive region; after flag set A this
+    # rank sums its own chunk over its partial and its receive region (rank
+    # order), adds the bias, writes the output and the peer's gather region;
+    # after flag set B it copies the other chunk from its own gather region.
+    # The stand-in peer's data in this rank's buffer (receive region, gather
+    # region) is preset with known values.
     rows, k, n, g = 600, 1024, 2048, 128
     plane = rows * n * 4
-    gath = (plane + 255) // 256 * 256
+    pl = (plane + 255) // 256 * 256
     es = 2
-    slot = gath + rows * n * es
+    slot = 2 * pl + rows * n * es
     own, other, peers = _two_rank_stand_in(cuda_device, 256 + 2 * (slot + 4096), sets=(1, 9))
     x, qw, qz, s, b = random_awq(k, n, g, dtype, rows, seed=31)
     t = lambda a, d: to_torch(a, d, cuda_device)
     x, qw, qz, s, b = t(x, dtype), t(qw, "u32"), t(qz, "u32"), t(s, dtype), t(b, dtype)
     tdt = x.dtype
+    cw = n // 2
     off = 256 + peers.slot_bytes                   # epoch 1: slot 1
-    peer_part = other[off:off + plane].view(torch.float32).view(rows, n)
-    peer_part.copy_(torch.randn(rows, n, device=cuda_device))
-    peer_gath = other[off + gath:off + gath + rows * n * es].view(tdt).view(rows, n)
-    peer_gath.copy_(torch.randn(rows, n, device=cuda_device).to(tdt))
+    recv_in = own[off + pl:off + pl + 2 * rows * cw * 4].view(torch.float32).view(2, rows, cw)
+    recv_in[1].copy_(torch.randn(rows, cw, device=cuda_device))      # from rank 1
+    gath_in = own[off + 2 * pl:off + 2 * pl + rows * n * es].view(tdt).view(rows, n)
+    gath_in.copy_(torch.randn(rows, n, device=cuda_device).to(tdt))  # rank 1's chunk
     row = tp.RowParallelAWQLinear(qw, qz, s, b, backend="p2p", peers=peers,
                                   input_is_parallel=False)
     y = row(x)
@@ -193,11 +199,11 @@ def test_rowpar_reduce_scatter_pull_on_one_gpu(cuda_device, dtype):
     assert cawq.device_error() == 0
     part = cawq.gemm(x[:, :k // 2].contiguous(), row.qweight, row.qzeros, row.scales, g,
                      out_dtype=torch.float32)
-    cw = n // 2
-    want0 = ((part[:, :cw] + peer_part[:, :cw]) + b[:cw].float()).to(tdt)
+    want0 = ((part[:, :cw] + recv_in[1]) + b[:cw].float()).to(tdt)
     assert torch.equal(y[:, :cw], want0)
-    assert torch.equal(y[:, cw:], peer_gath[:, cw:])
-    own_part = own[off:off + plane].view(torch.float32).view(rows, n)
-    assert torch.equal(own_part, part)             # what the peer would read
-    own_gath = own[off + gath:off + gath + rows * n * es].view(tdt).view(rows, n)
-    assert torch.equal(own_gath[:, :cw], want0)
+    assert torch.equal(y[:, cw:], gath_in[:, cw:])
+    assert torch.equal(own[off:off + plane].view(torch.float32).view(rows, n), part)
+    peer_recv = other[off + pl:off + pl + rows * cw * 4].view(torch.float32).view(rows, cw)
+    assert torch.equal(peer_recv, part[:, cw:])    # recv[0] of the peer
+    peer_gath = other[off + 2 * pl:off + 2 * pl + rows * n * es].view(tdt).view(rows, n)
+    assert torch.equal(peer_gath[:, :cw], want0)

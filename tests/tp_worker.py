@@ -98,7 +98,7 @@ def gpu_rank(rank, world, port, cases, backend, q):
         if backend in ("native", "p2p"):
             comm = tp.TPComm(timeout_ms=60000)
         if backend == "p2p":
-            peers = tp.TPPeers(comm, 128 << 20, timeout_ms=5000)
+            peers = tp.TPPeers(comm, 256 << 20, timeout_ms=5000)
         msgs = []
         for (k, n, g, rows) in cases:
             x, qw, qz, s, b = problem(k, n, g, rows, seed=k + n + rows)
