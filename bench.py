@@ -354,9 +354,12 @@ def run_ours(a, rank, local_rank, world):
         tp_keys["tp_llama3_70b_mlp"] = tp_mlp_numbers(dev, world, max_over_ranks)
 
     if world > 1:
+        # Every rank's work is done. The process group is left to process exit
+        # (main() ends every rank with os._exit): NCCL logs its teardown on
+        # stdout, and other ranks' lines would land after rank 0's JSON line.
         del graph
+        torch.cuda.synchronize()
         dist.barrier()
-        dist.destroy_process_group()
     if rank != 0:
         return
 
@@ -988,6 +991,13 @@ def main():
         run_prefill_only(a, rank, local_rank, world)
     else:
         run_ours(a, rank, local_rank, world)
+        if world > 1:
+            # All device work is done; leave without the libraries' exit-time
+            # teardown, whose NCCL log lines would otherwise follow the JSON
+            # line on stdout.
+            sys.stdout.flush()
+            sys.stderr.flush()
+            os._exit(0)
 
 
 if __name__ == "__main__":
