@@ -93,6 +93,10 @@ int prefill_f32_tile_n(const GemmProblem& p, const cawq_plan& plan, const Device
 cudaError_t launch_prefill_f32(const GemmProblem& p, const cawq_plan& plan,
                                const DeviceInfo& dev);
 cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+// prefill_supports / launch_prefill hand plans with warps == 4 (weights as the
+// MMA's A operand in tensor memory, rows <= 128) to these
+bool prefill_tw_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
+cudaError_t launch_prefill_tw(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev);
 void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* out, int* count,
                         int max_count);
 cawq_plan prefill_default_plan(const GemmProblem& p, const DeviceInfo& dev);

@@ -23,4 +23,5 @@ cudaError_t read_device_error(uint32_t* word, int reset) {
 #include "cawq_generic.cuh"
 #include "cawq_prefill.cuh"
 #include "cawq_prefill_f32.cuh"
+#include "cawq_prefill_tw.cuh"
 #include "cawq_tp.cuh"

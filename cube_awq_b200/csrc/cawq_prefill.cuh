@@ -702,6 +702,7 @@ bool prefill_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceI
   if (p.dtype == kF32) {  // the f32 kernel (128 x 128 / 256 tiles), no split
     return (plan.warps == 0 || plan.warps == 1) && prefill_f32_supports(p, plan, dev);
   }
+  if (plan.warps == 4) return prefill_tw_supports(p, plan, dev);
   const int halves = pf_halves(plan);
   if (plan.warps != 0 && plan.warps != 1 && plan.warps != 2) return false;
   const int split = plan.split < 1 ? 1 : plan.split;
@@ -806,6 +807,7 @@ static cudaError_t launch_prefill_o(const GemmProblem& p, int halves, int split,
 
 cudaError_t launch_prefill(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
   if (p.dtype == kF32) return launch_prefill_f32(p, plan, dev);
+  if (plan.warps == 4) return launch_prefill_tw(p, plan, dev);
   const int halves = pf_halves(plan);
   const int split = plan.split < 1 ? 1 : plan.split;
   // Programmatic dependent launch for grids of one wave, whose ~14-26 us of
