@@ -980,6 +980,17 @@ void prefill_candidates(const GemmProblem& p, const DeviceInfo& dev, cawq_plan* 
       if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
     }
   }
+  // the weights-in-tensor-memory tile (rows <= 128): 256 / 512 columns
+  for (int tn : {256, 512}) {
+    for (int split : {1, 2, 4, 8}) {
+      cawq_plan pl = {};
+      pl.path = CAWQ_PATH_PREFILL;
+      pl.warps = 4;
+      pl.tile_n = tn;
+      pl.split = split;
+      if (prefill_supports(p, pl, dev) && c < max_count) out[c++] = pl;
+    }
+  }
   *count = c;
 }
 

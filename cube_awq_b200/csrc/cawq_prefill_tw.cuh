@@ -17,21 +17,28 @@
 // bytes of shared-memory traffic per weight on top of the packed load, which
 // at M <= 128 kept its stages well below the weight-streaming rate.
 //
-// CTA: 256 weight columns (two 128-column blocks, one MMA each per 16-k
-// step), every row of X, and a K slice (split K over a cluster of up to 8
-// CTAs along z). Rings:
-//   X (4 x M' x 128 B, TMA, 128-byte swizzle, K-major): the B operand, freed
-//     by the MMA;
-//   W (plan.stages x 9 KB, TMA): packed weight box 64 k x 32 words (128-byte swizzle)
-//     and the stage's scale and zero rows, freed by the dequantize warps;
-//   A (4 x 64 TMEM columns): the dequantized weights of a stage, two blocks
-//     of 32 columns (64 k as 16-bit pairs) x 128 lanes, freed by the MMA.
-// TMEM: the accumulators D (2 x M' fp32 columns) from column 0, the A ring
+// CTA: NB 128-column blocks of weight columns (NB = 2: 256 columns, NB = 4:
+// 512 columns for M <= 64), every row of X, and a K slice (split K over a
+// cluster of up to 8 CTAs along z). A CTA streams its packed weights at about
+// one 64-row TMA box per 0.45 us whatever the box's width (measured on B200:
+// 16 GB/s with one 128-byte row per k, 33 / 58 GB/s with two / four boxes side
+// by side), so with one CTA per SM the weight stream per SM grows with the
+// columns a CTA covers: NB = 4 loads two 128-byte boxes side by side per
+// k row. Rings:
+//   X (4 x M' x 128 B, 64 k per stage, TMA, 128-byte swizzle, K-major): the B
+//     operand, freed by the MMA;
+//   W (plan.stages x 9-10 KB, TMA): 128 / NB k rows x NB / 2 packed weight
+//     boxes of 32 words (128-byte swizzle), the stage's scale and zero rows;
+//     freed by the dequantize warps;
+//   A (4 x 64 TMEM columns): the dequantized weights of a W stage, NB blocks
+//     of 64 / NB columns (128 / NB k as 16-bit pairs) x 128 lanes, freed by
+//     the MMA.
+// TMEM: the accumulators D (NB x M' fp32 columns) from column 0, the A ring
 // from column 256 (512 columns, one CTA per SM).
 // Warps: 0 X producer, 1 TMEM allocation + MMA issue, 2 W producer, 3..18
 // dequantize, then run the epilogue. Warp w may only touch TMEM lanes
 // 32 (w % 4) .. + 31, so the 16 dequantize warps are four per lane quarter:
-// block b = j & 1 and stage parity j >> 1 (j = (w - 3) / 4).
+// block b = j % NB of stages kt = j / NB (mod 4 / NB) (j = (w - 3) / 4).
 //
 // Dequantize. ldmatrix.x4.trans gives a lane, per register, one 16-bit
 // element (4 nibbles = 4 weight columns) of two consecutive k rows. The
@@ -63,22 +70,24 @@
 
 namespace cawq {
 
-constexpr int kTwBN = 256;      // weight columns per CTA
-constexpr int kTwBK = 64;       // k rows per stage
+constexpr int kTwXK = 64;       // k rows per X stage
 constexpr int kTwXSt = 4;       // X stages
 constexpr int kTwWStMax = 16;   // packed W stages (plan.stages; 6 by default)
 constexpr int kTwWStDefault = 6;
 constexpr int kTwASt = 4;       // dequantized A stages in TMEM
 constexpr int kTwDqWarps = 16;  // dequantize / epilogue warps
 constexpr int kTwThreads = 96 + 32 * kTwDqWarps;
-constexpr int kTwMaxRows = 128;
 constexpr int kTwMaxSplit = 8;
 constexpr int kTwACol = 256;  // first TMEM column of the A ring
 
+template <int NB>
 struct TwLayout {
-  static constexpr int kW = kTwBK * kTwBN / 8 * 4;  // 8192
-  static constexpr int kS = kTwBN * 2;              // 512
-  static constexpr int kZ = kTwBN / 8 * 4;          // 128
+  static constexpr int kBN = 128 * NB;              // weight columns per CTA
+  static constexpr int kKA = 128 / NB;              // k rows per W / A stage
+  static constexpr int kMaxRows = 256 / NB;         // D: NB x M' <= 256 columns
+  static constexpr int kW = kKA * kBN / 8 * 4;      // 8192
+  static constexpr int kS = kBN * 2;
+  static constexpr int kZ = kBN / 8 * 4;
   static constexpr int kWSlot = ((kW + kS + kZ) + 1023) / 1024 * 1024;
   // X rows of the MMA (M rounded up to 16)
   static __host__ __device__ uint32_t nx(uint32_t rows) { return (rows + 15) / 16 * 16; }
@@ -86,13 +95,13 @@ struct TwLayout {
   static __host__ __device__ uint32_t rpo(uint32_t rows, uint32_t split) {
     return ((rows + split - 1) / split + 3) / 4 * 4;
   }
-  static __host__ __device__ size_t x_bytes(uint32_t nx) { return (size_t)nx * kTwBK * 2; }
+  static __host__ __device__ size_t x_bytes(uint32_t nx) { return (size_t)nx * kTwXK * 2; }
   static __host__ __device__ size_t off_w(uint32_t nx) { return x_bytes(nx) * kTwXSt; }
   static __host__ __device__ size_t ring_bytes(uint32_t nx, uint32_t nw) {
     return off_w(nx) + (size_t)kWSlot * nw;
   }
   static __host__ __device__ size_t recv_bytes(uint32_t rows, uint32_t split) {
-    return split > 1 ? (size_t)split * 2 * 128 * rpo(rows, split) * 4 : 0;
+    return split > 1 ? (size_t)split * NB * 128 * rpo(rows, split) * 4 : 0;
   }
   static __host__ __device__ size_t off_bars(uint32_t rows, uint32_t split, uint32_t nw) {
     const size_t a = ring_bytes(nx(rows), nw), b = recv_bytes(rows, split);
@@ -135,6 +144,12 @@ __device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st_16x256b_x2(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -163,7 +178,7 @@ __device__ __forceinline__ uint32_t tw_col_of_lane(int b, int q, int lane) {
                                col_of_nibble(4 * (e & 1) + c, ORDER));
 }
 
-template <int DT, int ODT, int ORDER>
+template <int DT, int ODT, int ORDER, int NB>
 __global__ void __launch_bounds__(kTwThreads, 1)
     prefill_tw_kernel(const __grid_constant__ CUtensorMap tm_x,
                       const __grid_constant__ CUtensorMap tm_w,
@@ -172,8 +187,12 @@ __global__ void __launch_bounds__(kTwThreads, 1)
                       const typename DType<DT>::T* __restrict__ bias,
                       const OutMap<typename DType<ODT>::T> om, uint32_t rows, uint32_t k,
                       uint32_t n, uint32_t g, uint32_t split, uint32_t nw) {
-  using L = TwLayout;
+  using L = TwLayout<NB>;
   using H = PfHalf2<DT>;
+  constexpr int KA = L::kKA;        // k rows per W / A stage
+  constexpr int NJB = KA / 16;      // 16-k MMA steps per stage
+  constexpr int XPS = kTwXK / KA;   // W / A stages per X stage
+  constexpr int G = 4 / NB;         // dequantize groups (stages in flight)
   constexpr uint32_t kTmemCols = 512;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -194,11 +213,13 @@ __global__ void __launch_bounds__(kTwThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t n0 = blockIdx.x * kTwBN;
+  const uint32_t n0 = blockIdx.x * L::kBN;
   const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
-  const int KT = static_cast<int>(k / kTwBK);
-  const int kt0 = static_cast<int>((uint64_t)KT * rank / split);
-  const int KTL = static_cast<int>((uint64_t)KT * (rank + 1) / split) - kt0;
+  // K is dealt out to the CTAs of a cluster in whole X stages (64 k)
+  const int XT = static_cast<int>(k / kTwXK);
+  const int xt0 = static_cast<int>((uint64_t)XT * rank / split);
+  const int XTL = static_cast<int>((uint64_t)XT * (rank + 1) / split) - xt0;
+  const int kt0 = xt0 * XPS, KTL = XTL * XPS;  // W / A stages
   // split K: rows [q rpo, q rpo + rpo) belong to CTA q; groups of 4 rows
   // below round_up(rows, 4) travel
   const uint32_t rpo = L::rpo(rows, split);
@@ -216,16 +237,16 @@ __global__ void __launch_bounds__(kTwThreads, 1)
     }
     for (int s = 0; s < NW; ++s) {
       mbar_init(&full_w[s], 1);
-      mbar_init(&empty_w[s], 8 * 32);  // the 8 warps of the stage's group
+      mbar_init(&empty_w[s], 4 * NB * 32);  // the warps of the stage's group
     }
     for (int s = 0; s < kTwASt; ++s) {
-      mbar_init(&afull[s], 8 * 32);
+      mbar_init(&afull[s], 4 * NB * 32);
       mbar_init(&aempty[s], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(drain_bar, 1);
     mbar_init(recv_bar, 1);
-    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * 2u * 128u * own4 * 4u);
+    if (split > 1) mbar_arrive_expect_tx(recv_bar, (split - 1) * (uint32_t)NB * 128u * own4 * 4u);
     fence_mbarrier_init();
     fence_proxy_async_smem();
     tma_prefetch_desc(&tm_x);
@@ -249,12 +270,12 @@ __global__ void __launch_bounds__(kTwThreads, 1)
       // every X stage, so they also wait for the previous grid.
       pdl_wait();
       const uint32_t xb = static_cast<uint32_t>(L::x_bytes(NX));
-      for (int i = 0; i < KTL && ok; ++i) {
+      for (int i = 0; i < XTL && ok; ++i) {
         const int s = i % kTwXSt, u = i / kTwXSt;
         if (u > 0) ok = mbar_wait_bounded(&empty_x[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         mbar_arrive_expect_tx(&full_x[s], xb);
-        tma_load_2d(x_slot(s), &tm_x, (kt0 + i) * kTwBK, 0, &full_x[s]);
+        tma_load_2d(x_slot(s), &tm_x, (xt0 + i) * kTwXK, 0, &full_x[s]);
         issued = i + 1;
       }
       s_x_issued = issued;
@@ -272,10 +293,16 @@ __global__ void __launch_bounds__(kTwThreads, 1)
         if (u > 0) ok = mbar_wait_bounded(&empty_w[s], (uint32_t)((u - 1) & 1));
         if (!ok) break;
         uint8_t* b = w_slot(s);
-        const int grp = static_cast<int>((uint32_t)kt * kTwBK / g);
+        const int grp = static_cast<int>((uint32_t)kt * KA / g);
         mbar_arrive_expect_tx(&full_w[s], L::kW + L::kS + L::kZ);
-        tma_load_2d(b, &tm_w, static_cast<int>(n0 / 8), kt * kTwBK, &full_w[s]);
-        tma_load_2d(b + L::kW, &tm_s, static_cast<int>(n0), grp, &full_w[s]);
+        // NB / 2 boxes of 32 words side by side: one 64-row box costs the
+        // same time whatever its width, so wider k rows stream faster
+#pragma unroll
+        for (int h = 0; h < NB / 2; ++h) {
+          tma_load_2d(b + h * (KA * 128), &tm_w, static_cast<int>(n0 / 8 + 32 * h), kt * KA,
+                      &full_w[s]);
+          tma_load_2d(b + L::kW + h * 512, &tm_s, static_cast<int>(n0 + 256 * h), grp, &full_w[s]);
+        }
         tma_load_2d(b + L::kW + L::kS, &tm_z, static_cast<int>(n0 / 8), grp, &full_w[s]);
         issued = i + 1;
       }
@@ -288,25 +315,30 @@ __global__ void __launch_bounds__(kTwThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = tw_idesc(DT == kBF16, NX);
       bool ok = true;
+      int sx = 0, sa = 0, sub = 0;
+      uint32_t px = 0, pa = 0;  // phase parities of the X and A slots
       for (int kt = 0; kt < KTL && ok; ++kt) {
-        const int sx = kt % kTwXSt, ux = kt / kTwXSt;
-        const int sa = kt % kTwASt, ua = kt / kTwASt;
-        ok = mbar_wait_bounded(&full_x[sx], (uint32_t)(ux & 1)) &&
-             mbar_wait_bounded(&afull[sa], (uint32_t)(ua & 1));
+        if (sub == 0) ok = mbar_wait_bounded(&full_x[sx], px);
+        ok = ok && mbar_wait_bounded(&afull[sa], pa);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t xa = smem_u32(x_slot(sx));
+        const uint32_t xa = smem_u32(x_slot(sx)) + 2 * KA * sub;  // this stage's k in the X row
 #pragma unroll
-        for (int j = 0; j < kTwBK / 16; ++j) {
+        for (int j = 0; j < NJB; ++j) {
           const uint64_t bd = umma_desc_sw128(xa + 32 * j, 16, 1024);
 #pragma unroll
-          for (int b = 0; b < 2; ++b) {
-            umma_f16_tmem_a(tmem + b * NX, tmem + kTwACol + 64 * sa + 32 * b + 8 * j, bd, idesc,
-                            (kt > 0 || j > 0) ? 1u : 0u);
+          for (int b = 0; b < NB; ++b) {
+            umma_f16_tmem_a(tmem + b * NX, tmem + kTwACol + 64 * sa + (KA / 2) * b + 8 * j, bd,
+                            idesc, (kt > 0 || j > 0) ? 1u : 0u);
           }
         }
-        umma_commit(&empty_x[sx]);
         umma_commit(&aempty[sa]);
+        if (++sa == kTwASt) { sa = 0; pa ^= 1u; }
+        if (++sub == XPS) {
+          umma_commit(&empty_x[sx]);
+          sub = 0;
+          if (++sx == kTwXSt) { sx = 0; px ^= 1u; }
+        }
       }
       if (ok) {
         umma_commit(acc_full);
@@ -320,33 +352,37 @@ __global__ void __launch_bounds__(kTwThreads, 1)
   } else {
     // ----------------------------------------------------- dequantize
     const int dw = warp - 3;
-    const int q = warp & 3;   // TMEM lane quarter of this warp
-    const int jq = dw >> 2;   // 0..3 among the quarter's warps
-    const int blk = jq & 1;   // 128-column block
-    const int grp_par = jq >> 1;  // stage parity
-    const int ch = 4 * blk + q;   // 16-byte chunk of the W row: 32 weight columns
-    const int e = lane >> 2, p = lane & 3;
+    const int q = warp & 3;        // TMEM lane quarter of this warp
+    const int jq = dw >> 2;        // 0..3 among the quarter's warps
+    const int blk = jq % NB;       // 128-column block
+    const int gi = jq / NB;        // group: stages kt = gi (mod G)
+    const int ch = 4 * blk + q;    // 16-byte chunk of the k row: 32 weight columns
+    const int e = lane >> 2;
     const int wi = 4 * ch + (e >> 1);  // packed word of this lane's 4 columns
     int ncol[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) ncol[c] = 8 * wi + col_of_nibble(4 * (e & 1) + c, ORDER);
-    // ldmatrix row address offsets: lane L supplies row r of matrix mi
-    uint32_t ldoff[2];
+    // ldmatrix row address offsets: lane L supplies row r of matrix mi; the
+    // chunk lies in box ch / 8 at position ch % 8 of its 128-byte rows
+    uint32_t ldoff[NJB / 2];
     {
       const int mi = lane >> 3, r = lane & 7;
+      const int bx = ch >> 3, cx = ch & 7;
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
+      for (int x = 0; x < NJB / 2; ++x) {
         const int kk = 16 * (2 * x + (mi >> 1)) + 4 * (r >> 1) + 2 * (mi & 1) + (r & 1);
-        ldoff[x] = static_cast<uint32_t>(kk * 128 + ((ch ^ (kk & 7)) << 4));
+        ldoff[x] = static_cast<uint32_t>(bx * (KA * 128) + kk * 128 + ((cx ^ (kk & 7)) << 4));
       }
     }
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     bool ok = true;
-    for (int kt = grp_par; kt < KTL; kt += 2) {
-      const int sw = kt % NW, uw = kt / NW;
-      const int sa = kt % kTwASt, ua = kt / kTwASt;
-      if (ok) ok = mbar_wait_bounded(&full_w[sw], (uint32_t)(uw & 1));
-      if (ok && ua > 0) ok = mbar_wait_bounded(&aempty[sa], (uint32_t)((ua - 1) & 1));
+    // this group's W and A slots and phase parities, advanced by G per stage
+    int sw = gi % NW, sa = gi % kTwASt;
+    uint32_t pw = 0, pa = 0;
+    bool first_use = true;  // an A slot's first use needs no wait for the MMA
+    for (int kt = gi; kt < KTL; kt += G) {
+      if (ok) ok = mbar_wait_bounded(&full_w[sw], pw);
+      if (ok && !first_use) ok = mbar_wait_bounded(&aempty[sa], pa ^ 1u);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.st is warp-collective
       if (ok) {
         tc_fence_after();
@@ -361,13 +397,13 @@ __global__ void __launch_bounds__(kTwThreads, 1)
           const uint32_t sb = srow[ncol[c]];
           sp[c] = sb | (sb << 16);
         }
-        uint32_t R[2][4];
+        uint32_t R[NJB / 2][4];
 #pragma unroll
-        for (int x = 0; x < 2; ++x)
+        for (int x = 0; x < NJB / 2; ++x)
           ldmatrix_x4_trans(smem_u32(wsm) + ldoff[x], R[x][0], R[x][1], R[x][2], R[x][3]);
-        uint32_t st0[16], st1[16];
+        uint32_t st0[4 * NJB], st1[4 * NJB];
 #pragma unroll
-        for (int jb = 0; jb < 4; ++jb) {
+        for (int jb = 0; jb < NJB; ++jb) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t reg = R[jb >> 1][2 * (jb & 1) + h];
@@ -381,15 +417,24 @@ __global__ void __launch_bounds__(kTwThreads, 1)
             }
           }
         }
-        const uint32_t acol = tmem + kTwACol + 64 * sa + 32 * blk;
-        tmem_st_16x256b_x4(acol + lane_base, st0);
-        tmem_st_16x256b_x4(acol + lane_base + (16u << 16), st1);
+        const uint32_t acol = tmem + kTwACol + 64 * sa + (KA / 2) * blk;
+        if constexpr (NJB == 4) {
+          tmem_st_16x256b_x4(acol + lane_base, st0);
+          tmem_st_16x256b_x4(acol + lane_base + (16u << 16), st1);
+        } else {
+          tmem_st_16x256b_x2(acol + lane_base, st0);
+          tmem_st_16x256b_x2(acol + lane_base + (16u << 16), st1);
+        }
         tmem_wait_st();
       }
       // the W slot's values are consumed (the stores above used them)
       mbar_arrive(&empty_w[sw]);
       tc_fence_before();
       mbar_arrive(&afull[sa]);
+      sw += G;
+      if (sw >= NW) { sw -= NW; pw ^= 1u; }
+      sa += G;
+      if (sa >= kTwASt) { sa -= kTwASt; pa ^= 1u; first_use = false; }
     }
     // ---- accumulators complete
     if (ok) ok = mbar_wait_bounded(acc_full, 0u);
@@ -420,8 +465,8 @@ __global__ void __launch_bounds__(kTwThreads, 1)
     if (split == 1) {
       if (ok) {
 #pragma unroll 1
-        for (int u = jq; u < 2 * nchunk; u += 4) {
-          const int b = u & 1, cc = u >> 1;
+        for (int u = jq; u < NB * nchunk; u += 4) {
+          const int b = u % NB, cc = u / NB;
           float v[16];
           tmem_ld_32x32b_x16(tmem + lane_base + b * NX + 16 * cc, v);
           const uint32_t col = n0 + tw_col_of_lane<ORDER>(b, q, lane);
@@ -440,8 +485,8 @@ __global__ void __launch_bounds__(kTwThreads, 1)
       const uint32_t bar_local = smem_u32(recv_bar);
       if (ok) {
 #pragma unroll 1
-        for (int u = jq; u < 2 * nchunk; u += 4) {
-          const int b = u & 1, cc = u >> 1;
+        for (int u = jq; u < NB * nchunk; u += 4) {
+          const int b = u % NB, cc = u / NB;
           if (static_cast<uint32_t>(16 * cc) >= rows4) continue;
           float v[16];
           tmem_ld_32x32b_x16(tmem + lane_base + b * NX + 16 * cc, v);
@@ -450,7 +495,8 @@ __global__ void __launch_bounds__(kTwThreads, 1)
             const uint32_t r0 = 16 * cc + 4 * i4;  // first row of the group
             if (r0 >= rows4) continue;
             const uint32_t o = r0 / rpo;
-            float* dst = recv + (((size_t)rank * 2 + b) * 128 + 32 * q + lane) * rpo + (r0 - o * rpo);
+            float* dst =
+                recv + (((size_t)rank * NB + b) * 128 + 32 * q + lane) * rpo + (r0 - o * rpo);
             if (o == rank) {
               *reinterpret_cast<float4*>(dst) =
                   make_float4(v[4 * i4], v[4 * i4 + 1], v[4 * i4 + 2], v[4 * i4 + 3]);
@@ -464,14 +510,14 @@ __global__ void __launch_bounds__(kTwThreads, 1)
       const bool got = mbar_wait_bounded(recv_bar, 0u);
       named_bar_sync(1, 32 * kTwDqWarps);  // this CTA's own groups are in place
       if (ok && got) {
-        // the warps of a quarter: block jq & 1, every other group of 4 rows
-        const int b = jq & 1;
+        // the warps of a quarter: block jq % NB, every G-th group of 4 rows
+        const int b = jq % NB;
         const uint32_t col = n0 + tw_col_of_lane<ORDER>(b, q, lane);
-        for (uint32_t i4 = (uint32_t)(jq >> 1) * 4; i4 < own4; i4 += 8) {
+        for (uint32_t i4 = (uint32_t)(jq / NB) * 4; i4 < own4; i4 += 4 * G) {
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           for (uint32_t src = 0; src < split; ++src) {
             const float4 f = *reinterpret_cast<const float4*>(
-                recv + (((size_t)src * 2 + b) * 128 + 32 * q + lane) * rpo + i4);
+                recv + (((size_t)src * NB + b) * 128 + 32 * q + lane) * rpo + i4);
             acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
           }
           if (col < n) {
@@ -505,46 +551,56 @@ __global__ void __launch_bounds__(kTwThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
+// plan.tile_n = 512 selects NB = 4 (rows <= 64), else NB = 2 (rows <= 128).
+static int tw_nb(const cawq_plan& plan) { return plan.tile_n == 512 ? 4 : 2; }
+
+template <int NB>
+static size_t tw_smem(const GemmProblem& p, int split, int nw) {
+  return TwLayout<NB>::smem(static_cast<uint32_t>(p.rows), static_cast<uint32_t>(split),
+                            static_cast<uint32_t>(nw));
+}
+
 bool prefill_tw_supports(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
   const int split = plan.split < 1 ? 1 : plan.split;
+  const int nb = tw_nb(plan);
+  if (plan.tile_n != 0 && plan.tile_n != 256 && plan.tile_n != 512) return false;
   if (split > kTwMaxSplit || (split & (split - 1))) return false;
   if (dev.cc_major != 10) return false;
   if (p.dtype != kF16 && p.dtype != kBF16) return false;
-  if (p.rows == 0 || p.rows > (size_t)kTwMaxRows) return false;
-  if (p.k % kTwBK != 0 || p.g % kTwBK != 0 || p.k % p.g != 0 || p.n % 32 != 0) return false;
-  if ((size_t)split > p.k / kTwBK) return false;
+  if (p.rows == 0 || p.rows > (size_t)(256 / nb)) return false;
+  if (p.k % kTwXK != 0 || p.g % kTwXK != 0 || p.k % p.g != 0 || p.n % 32 != 0) return false;
+  if ((size_t)split > p.k / kTwXK) return false;
   if (p.k >= (1ull << 31) || p.n >= (1ull << 31) || p.ld_out >= (1ull << 31)) return false;
   if (p.epi != 0 || p.nrep > 0) return false;  // plain epilogue (one or three outputs)
   const int nw = plan.stages == 0 ? kTwWStDefault : plan.stages;
-  if (nw < 2 || nw > kTwWStMax) return false;
-  if (dev.smem_optin < TwLayout::smem(static_cast<uint32_t>(p.rows), static_cast<uint32_t>(split),
-                                      static_cast<uint32_t>(nw)))
+  if (nw < 4 / nb || nw > kTwWStMax) return false;
+  if (dev.smem_optin < (nb == 4 ? tw_smem<4>(p, split, nw) : tw_smem<2>(p, split, nw)))
     return false;
   const uintptr_t ax = reinterpret_cast<uintptr_t>(p.x), aw = reinterpret_cast<uintptr_t>(p.qw);
   const uintptr_t az = reinterpret_cast<uintptr_t>(p.qz), as = reinterpret_cast<uintptr_t>(p.sc);
   return ax % 16 == 0 && aw % 16 == 0 && az % 16 == 0 && as % 16 == 0;
 }
 
-template <int DT, int ODT, int ORDER>
+template <int DT, int ODT, int ORDER, int NB>
 static cudaError_t launch_prefill_tw_t(const GemmProblem& p, int split, int nw, bool pdl) {
   using T = typename DType<DT>::T;
   using OT = typename DType<ODT>::T;
-  using L = TwLayout;
+  using L = TwLayout<NB>;
   const CUtensorMapDataType xdt =
       DT == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint32_t rows = static_cast<uint32_t>(p.rows);
   const uint32_t nx = L::nx(rows);
   CUtensorMap tx, tw, ts, tz;
   const uint64_t npk = p.n / 8, groups = p.k / p.g;
-  if (!pf_encode(&tx, xdt, p.x, p.k, p.rows, p.k * 2, kTwBK, nx, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !pf_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, kTwBN / 8, kTwBK,
+  if (!pf_encode(&tx, xdt, p.x, p.k, p.rows, p.k * 2, kTwXK, nx, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !pf_encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qw, npk, p.k, npk * 4, 32, L::kKA,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !pf_encode(&ts, xdt, p.sc, p.n, groups, p.n * 2, kTwBN, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !pf_encode(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qz, npk, groups, npk * 4, kTwBN / 8, 1,
+      !pf_encode(&ts, xdt, p.sc, p.n, groups, p.n * 2, 256, 1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !pf_encode(&tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, p.qz, npk, groups, npk * 4, L::kBN / 8, 1,
                  CU_TENSOR_MAP_SWIZZLE_NONE)) {
     return cudaErrorInvalidValue;
   }
-  auto kern = prefill_tw_kernel<DT, ODT, ORDER>;
+  auto kern = prefill_tw_kernel<DT, ODT, ORDER, NB>;
   const size_t smem = L::smem(rows, static_cast<uint32_t>(split), static_cast<uint32_t>(nw));
   static size_t attr_smem = 0;  // per instantiation: the largest size set so far
   if (smem > attr_smem) {
@@ -554,7 +610,7 @@ static cudaError_t launch_prefill_tw_t(const GemmProblem& p, int split, int nw, 
     attr_smem = smem;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<uint32_t>((p.n + kTwBN - 1) / kTwBN), 1,
+  cfg.gridDim = dim3(static_cast<uint32_t>((p.n + L::kBN - 1) / L::kBN), 1,
                      static_cast<uint32_t>(split));
   cfg.blockDim = dim3(kTwThreads);
   cfg.dynamicSmemBytes = smem;
@@ -581,25 +637,33 @@ static cudaError_t launch_prefill_tw_t(const GemmProblem& p, int split, int nw, 
                             static_cast<uint32_t>(split), static_cast<uint32_t>(nw));
 }
 
-template <int DT, int ODT>
+template <int DT, int ODT, int NB>
 static cudaError_t launch_prefill_tw_o(const GemmProblem& p, int split, int nw, bool pdl) {
-  return p.order == kOrderNatural ? launch_prefill_tw_t<DT, ODT, kOrderNatural>(p, split, nw, pdl)
-                                  : launch_prefill_tw_t<DT, ODT, kOrderAwq>(p, split, nw, pdl);
+  return p.order == kOrderNatural
+             ? launch_prefill_tw_t<DT, ODT, kOrderNatural, NB>(p, split, nw, pdl)
+             : launch_prefill_tw_t<DT, ODT, kOrderAwq, NB>(p, split, nw, pdl);
+}
+
+template <int DT, int ODT>
+static cudaError_t launch_prefill_tw_nb(const GemmProblem& p, int nb, int split, int nw, bool pdl) {
+  return nb == 4 ? launch_prefill_tw_o<DT, ODT, 4>(p, split, nw, pdl)
+                 : launch_prefill_tw_o<DT, ODT, 2>(p, split, nw, pdl);
 }
 
 cudaError_t launch_prefill_tw(const GemmProblem& p, const cawq_plan& plan, const DeviceInfo& dev) {
   const int split = plan.split < 1 ? 1 : plan.split;
-  const size_t ctas = ((p.n + kTwBN - 1) / kTwBN) * (size_t)split;
+  const int nb = tw_nb(plan);
+  const size_t ctas = ((p.n + 128 * nb - 1) / (128 * nb)) * (size_t)split;
   const size_t sms = static_cast<size_t>(dev.sm_count > 0 ? dev.sm_count : 148);
   const bool pdl = plan.reserved[0] == 0 && ctas <= sms;
   const int nw = plan.stages == 0 ? kTwWStDefault : plan.stages;
   if (p.dtype == kF16) {
-    return p.out_dtype == kF32 ? launch_prefill_tw_o<kF16, kF32>(p, split, nw, pdl)
-                               : launch_prefill_tw_o<kF16, kF16>(p, split, nw, pdl);
+    return p.out_dtype == kF32 ? launch_prefill_tw_nb<kF16, kF32>(p, nb, split, nw, pdl)
+                               : launch_prefill_tw_nb<kF16, kF16>(p, nb, split, nw, pdl);
   }
   if (p.dtype == kBF16) {
-    return p.out_dtype == kF32 ? launch_prefill_tw_o<kBF16, kF32>(p, split, nw, pdl)
-                               : launch_prefill_tw_o<kBF16, kBF16>(p, split, nw, pdl);
+    return p.out_dtype == kF32 ? launch_prefill_tw_nb<kBF16, kF32>(p, nb, split, nw, pdl)
+                               : launch_prefill_tw_nb<kBF16, kBF16>(p, nb, split, nw, pdl);
   }
   return cudaErrorNotSupported;
 }

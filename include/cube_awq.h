@@ -102,10 +102,17 @@ typedef struct cawq_gemm_args {
 /* A kernel choice for one (M, K, N, g, dtype) problem. */
 typedef struct cawq_plan {
   int path;      /* cawq_path                                            */
-  int split;     /* decode: CTAs per cluster splitting K (1..16)         */
-  int warps;     /* decode: 128-column strips per CTA (even, 2..8)      */
-  int tile_n;    /* prefill: CTA tile N; decode: 0                       */
-  int stages;    /* pipeline stages                                      */
+  int split;     /* decode: CTAs per cluster splitting K (1..16);
+                    prefill: 1, 2, 4, 8                                  */
+  int warps;     /* decode: 128-column strips per CTA (even, 2..8);
+                    prefill: 1 / 2 = 128 / 256-row X tiles; 4 = the
+                    weights as the MMA's A operand in tensor memory,
+                    X rows as its N (rows <= 128, f16 / bf16,
+                    group_size % 64 == 0; autotune candidate only)      */
+  int tile_n;    /* prefill: CTA tile N (warps 4: 256, or 512 for rows
+                    <= 64); decode: 0                                    */
+  int stages;    /* pipeline stages (prefill warps 4: packed weight
+                    stages in flight, 0 = 6)                            */
   int reserved[3]; /* reserved[0] = 1: launch without programmatic
                       dependent launch (no overlap with the previous
                       kernel of the stream).
