@@ -336,6 +336,7 @@ def run_ours(a, rank, local_rank, world):
         torch.cuda.empty_cache()
         extras["fused_neighbours"] = fused_neighbour_numbers(dev)
         extras["qwen2_m_sweep"] = qwen2_sweep(dev)
+        extras["crossover_sweep"] = crossover_sweep(dev)
         extras["decode_sweep_m"] = sweep
         extras["us_per_linear_isolated"] = {k: round(statistics.median(v) * 1e3, 2)
                                             for k, v in per_name.items()}
@@ -388,7 +389,8 @@ def run_ours(a, rank, local_rank, world):
     }
     # bulky diagnostics first, the compact key numbers last (the end of the
     # line is what a truncated log keeps)
-    for key in ("fused_neighbours", "qwen2_m_sweep", "decode_sweep_m", "us_per_linear_isolated"):
+    for key in ("fused_neighbours", "qwen2_m_sweep", "crossover_sweep", "decode_sweep_m",
+                "us_per_linear_isolated"):
         if key in extras:
             line[key] = extras.pop(key)
     if "tp_fused_collectives" in tp_keys:
@@ -567,6 +569,59 @@ def qwen2_sweep(dev, reps=10):
         del xs, ys
     del ws
     return res
+
+
+def crossover_sweep(dev, reps=10):
+    """Where the decode / prefill crossover belongs: us per decoder layer
+    (4 linears, f16, graph-timed, 3 weight copies rotated) of Llama-2-7B (g
+    128) and Qwen2-7B (g 64) at M = 8 ... 64. Up to M = 16 both kernels run:
+    the decode kernel with its default plan, and the 128-row prefill tile
+    with the fastest split (1-8) per linear; above 16 only the prefill kernel
+    applies (default plans). `planner` is the path the default planner takes."""
+    import torch
+
+    import cube_awq_b200 as cawq
+    from cube_awq_b200 import synth
+    models = {"llama2_7b": (128, (("qkv", 4096, 12288), ("o_proj", 4096, 4096),
+                                  ("gate_up", 4096, 22016), ("down", 11008, 4096))),
+              "qwen2_7b": (64, (("qkv", 3584, 4608), ("o_proj", 3584, 3584),
+                                ("gate_up", 3584, 37888), ("down", 18944, 3584)))}
+    dt, copies = torch.float16, 3
+    stream = torch.cuda.Stream(dev)
+    out = {}
+    for model, (g, shapes) in models.items():
+        ws = {name: [synth.make_weights(k, n, g, dt, dev, seed=1100 + 10 * j + c)
+                     for c in range(copies)] for j, (name, k, n) in enumerate(shapes)}
+        res = {}
+        for m in (8, 12, 16, 24, 32, 48, 64):
+            xs = {name: synth.make_input(m, k, dt, dev, seed=1150) for name, k, n in shapes}
+            ys = {name: torch.empty(m, n, dtype=dt, device=dev) for name, k, n in shapes}
+
+            def linear_us(name, plan):
+                def run():
+                    for c in range(copies):
+                        w = ws[name][c]
+                        cawq.gemm(xs[name], w.qweight, w.qzeros, w.scales, g, out=ys[name],
+                                  plan=plan)
+                return _graph_us(run, reps, stream) / copies
+
+            row = {"planner": sorted({cawq.plan_get(m, k, n, g, dt)["path"]
+                                      for name, k, n in shapes})}
+            pre = 0.0
+            for name, k, n in shapes:
+                if m <= 16:
+                    pre += min(linear_us(name, {"path": 2, "warps": 1, "split": sp})
+                               for sp in (1, 2, 4, 8) if sp * 8 <= k // 64)
+                else:
+                    pre += linear_us(name, None)
+            row["prefill_us"] = round(pre, 2)
+            if m <= 16:
+                row["decode_us"] = round(sum(linear_us(name, None) for name, _, _ in shapes), 2)
+            res[f"M={m}"] = row
+            del xs, ys
+        out[model] = res
+        del ws
+    return out
 
 
 def fused_neighbour_numbers(dev, reps=10):
