@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
     // more slots each lane has waited for its own previous stage's release
     // first (consumers release in order), so it is; a one-slot ring keeps a
     // single issuing lane.
-    const int np = NS >= 2 ? 2 : 1;  // issuing lanes
+    const int np = NS >= 4 ? 4 : NS >= 2 ? 2 : 1;  // issuing lanes (<= ring slots)
     if (lane < np) {
       // valid columns of the band (the bulk copies must stay inside a row)
       const uint32_t bcol0 = pband * 8;
@@ -305,7 +305,8 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
       pdl_wait();                                       // X may be the previous kernel's output
       for (int j = lane; j < pro; j += np) issue_x(j);
       int issued = pro;
-      for (int j = pro + (pro + lane) % np; j < nst && ok; j += np) {  // this lane's stages
+      // this lane's stages: the first j >= pro with j = lane (mod np)
+      for (int j = pro + ((lane - pro) % np + np) % np; j < nst && ok; j += np) {
         const int sl = j % NS;
         ok = mbar_wait_bounded(&empty[sl], static_cast<uint32_t>(((j / NS) - 1) & 1));
         if (!ok) break;
