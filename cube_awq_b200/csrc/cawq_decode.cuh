@@ -231,14 +231,14 @@ __global__ void __launch_bounds__(I8 ? (2 * kDecI8MaxStrips + 2) * 32
   bool ok = true;
   if (warp == consumers) {
     // ------------------------------------------------------ TMA producer
-    // Lanes 0 and 1 issue alternate stages: a thread that issues every stage
-    // lands about one 64-row weight box per 0.45-0.5 us, two threads about
-    // one per 0.31-0.35 us (measured on B200; four were no faster). A lane
-    // waits for its stage's slot by phase parity, which is only unambiguous
-    // while it is at most one phase ahead of the slot: with a ring of two or
-    // more slots each lane has waited for its own previous stage's release
-    // first (consumers release in order), so it is; a one-slot ring keeps a
-    // single issuing lane.
+    // Up to four lanes issue the stages round robin (stage j by lane j mod
+    // np): a thread that issues every stage lands about one 64-row weight box
+    // per 0.45-0.5 us, two threads about one per 0.31-0.35 us (measured on
+    // B200), and with a stage's four or five copies four lanes gained again in
+    // the decode chain. A lane waits for its stage's slot by phase parity,
+    // which is only unambiguous while it is at most one phase ahead of the
+    // slot: with at least np slots each lane has waited for its own previous
+    // stage's release first (consumers release in order), so it is.
     const int np = NS >= 4 ? 4 : NS >= 2 ? 2 : 1;  // issuing lanes (<= ring slots)
     if (lane < np) {
       // valid columns of the band (the bulk copies must stay inside a row)
